@@ -1,0 +1,293 @@
+/*
+ * spx.h — C ABI of libspx, the B200 (sm_100a) operator backend for
+ * SPIRV_INFERENCE-style graphs.
+ *
+ * Two layers are exported:
+ *
+ *  1. The drop-in dispatch boundary, `spx_run_kernel`.  It replaces
+ *     `tflite_loader::vulkan::run_kernel(device_selector, &KernelRun) ->
+ *     KernelOutput` (source/tflite_loader/src/vulkan.rs:18-44).  Kernels are
+ *     named exactly as in the reference registry (source/tflite_loader/src/
+ *     kernels.rs:12-238, plus the HLO kernels of source/xla_hlo/src/
+ *     compiler.rs:1155-1228: hlo_conv_nhwc_hwio, hlo_dot_rank2,
+ *     hlo_dot_batched, hlo_reduce_rank4, hlo_reduce_window_rank4, pad), take
+ *     the same two f32 inputs, the same i32 push constants in the same order,
+ *     and produce the same output layout.  A ".spv" suffix on the name is
+ *     accepted and ignored, so the reference's `dispatch(…, "conv2d.spv", …)`
+ *     call sites (source/tflite_loader/src/scheduler.rs:1096-1144) map 1:1.
+ *     Host buffers in, host buffer out, synchronous, like the reference.
+ *
+ *  2. The device-resident graph API (`spx_graph_*`, `spx_buf_*`, `spx_op_*`).
+ *     It generalises the create-once / record / submit pattern of
+ *     runtime/chained_graph_runtime/src/main.rs:298-547: one CUDA stream per
+ *     graph, device allocations made once, ops recorded back to back on the
+ *     stream (optionally captured into a CUDA graph and replayed).  Activations
+ *     are NHWC; conv weights are OHWI (TFLite's own order, so no repack) or
+ *     HWIO (the HLO path's order).
+ *
+ * Every call returns SPX_OK (0) or an error code; `spx_last_error()` returns a
+ * thread-local message for the last failure on the calling thread.  There is
+ * no CPU fallback: without a CUDA device every compute call fails with
+ * SPX_ERR_NO_DEVICE.
+ */
+#ifndef SPX_H_
+#define SPX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define SPX_OK 0
+#define SPX_ERR_INVALID_ARGUMENT 1 /* bad sizes / push constants / null ptr  */
+#define SPX_ERR_UNSUPPORTED 2      /* unknown kernel or unsupported feature;
+                                      the reference maps this case to
+                                      "blocked_unsupported_feature"
+                                      (source/tflite_loader/src/main.rs:66-76) */
+#define SPX_ERR_CUDA 3             /* a CUDA runtime call failed             */
+#define SPX_ERR_OUT_OF_MEMORY 4
+#define SPX_ERR_NO_DEVICE 5        /* no CUDA device / bad ordinal           */
+
+/* ---- activations fused into epilogues ---------------------------------- */
+/* Numbering follows TFLite's ActivationFunctionType as decoded by
+ * source/tflite_loader/src/op_decoder.rs:21-44 (None=0, Relu=1, Relu6=3);
+ * values above 15 are spx extensions for the HLO / transformer graphs. */
+#define SPX_ACT_NONE 0
+#define SPX_ACT_RELU 1
+#define SPX_ACT_RELU_N1_TO_1 2
+#define SPX_ACT_RELU6 3
+#define SPX_ACT_TANH 4
+#define SPX_ACT_GELU_ERF 16  /* x * 0.5 * (1 + erf(x / sqrt 2))           */
+#define SPX_ACT_GELU_TANH 17 /* tanh approximation of GELU                 */
+#define SPX_ACT_SILU 18      /* x * sigmoid(x)                             */
+
+/* ---- library / device info --------------------------------------------- */
+const char* spx_last_error(void);
+const char* spx_version(void);
+/* Number of CUDA devices (0 when none; never fails). */
+int spx_device_count(void);
+/* Maps the reference's device selector ("any" | "nvidia" | "intel",
+ * source/tflite_loader/src/vulkan.rs:204-231) or a decimal ordinal to a CUDA
+ * ordinal.  "intel" has no CUDA device and fails with SPX_ERR_NO_DEVICE. */
+int spx_select_device(const char* selector, int* ordinal);
+
+/* ---- kernel registry (mirror of kernels.rs:12-238 + HLO kernels) ------- */
+int spx_kernel_count(void);
+/* Name of registry entry i (0 <= i < spx_kernel_count()), NULL if out of range. */
+const char* spx_kernel_name(int i);
+/* Number of i32 push constants kernel `name` expects, or -1 if unknown. */
+int spx_kernel_push_count(const char* name);
+/* Work-group size the reference dispatches this kernel with (64 or 128). */
+int spx_kernel_local_size(const char* name);
+
+/* ---- 1. drop-in dispatch boundary -------------------------------------- */
+/* Mirrors `KernelOutput { values, device_name, vendor_id, device_id,
+ * elapsed_ms }` (vulkan.rs:18-25) minus `values`, which go to `output`. */
+typedef struct spx_kernel_output_info {
+  double elapsed_ms;     /* device time of the kernel(s), CUDA events     */
+  char device_name[256];
+  uint32_t vendor_id;    /* 0x10de                                        */
+  uint32_t device_id;    /* PCI device id                                 */
+} spx_kernel_output_info;
+
+/* Replaces vulkan::run_kernel (vulkan.rs:42-185).  `kernel` is a registry
+ * name or spv file name.  input0/input1 are the reference's bindings 0 and 1,
+ * output is binding 2 with `output_elements` floats.  `push` holds the i32
+ * push constants in the registry order (floats as bit patterns, e.g.
+ * leaky_relu alpha_bits, kernels.rs:92-97).  `info` may be NULL.
+ * Device buffers are cached per device and reused between calls (the
+ * reference creates and destroys every Vulkan object per call). */
+int spx_run_kernel(const char* kernel, const float* input0, size_t input0_len,
+                   const float* input1, size_t input1_len, float* output,
+                   size_t output_elements, const int32_t* push, size_t push_len,
+                   int device, spx_kernel_output_info* info);
+
+/* ---- 2. device-resident graph API -------------------------------------- */
+typedef struct spx_graph spx_graph;
+
+/* Creates a graph on `device` with its own non-blocking stream. */
+int spx_graph_create(int device, spx_graph** out);
+/* Same, but records onto a caller-owned cudaStream_t (passed as void*). */
+int spx_graph_create_on_stream(int device, void* cuda_stream, spx_graph** out);
+int spx_graph_destroy(spx_graph* g);
+void* spx_graph_stream(spx_graph* g);
+int spx_graph_device(spx_graph* g);
+/* Blocks until all work recorded so far has finished; reports async errors. */
+int spx_graph_sync(spx_graph* g);
+/* Number of spx kernel launches recorded on this graph since creation or the
+ * last reset (replays of a captured CUDA graph count their kernels too). */
+int64_t spx_graph_launch_count(spx_graph* g);
+void spx_graph_reset_launch_count(spx_graph* g);
+
+/* CUDA-graph capture of everything recorded between begin and end. */
+int spx_graph_capture_begin(spx_graph* g);
+int spx_graph_capture_end(spx_graph* g);
+int spx_graph_replay(spx_graph* g);
+
+/* Device buffers owned by the graph (freed by spx_graph_destroy). */
+int spx_buf_alloc(spx_graph* g, size_t bytes, void** dptr);
+int spx_buf_free(spx_graph* g, void* dptr);
+/* Stream-ordered copies; host buffers should be pinned for overlap. */
+int spx_buf_upload(spx_graph* g, void* dst_device, const void* src_host, size_t bytes);
+int spx_buf_download(spx_graph* g, void* dst_host, const void* src_device, size_t bytes);
+int spx_buf_zero(spx_graph* g, void* dst_device, size_t bytes);
+/* Stream-ordered device-to-device copy. */
+int spx_buf_copy(spx_graph* g, void* dst_device, const void* src_device, size_t bytes);
+int spx_host_alloc_pinned(size_t bytes, void** ptr);
+int spx_host_free_pinned(void* ptr);
+
+/* -- ops (all pointers are device pointers, NHWC activations) ------------ */
+
+/* Dense convolution, NHWC in and out, as implicit GEMM
+ * (M = n*oh*ow, N = oc, K = kh*kw*ic).  Covers the TFLite Conv2D lowering
+ * (scheduler.rs:321-427 + conv2d.comp) and the HLO convolution lowering
+ * (compiler.rs:768-855 + hlo_conv_nhwc_hwio.comp).  y = act(conv(x, w) +
+ * bias + residual); bias and residual may be NULL. */
+#define SPX_WEIGHT_OHWI 0 /* [oc][kh][kw][ic]  (TFLite Conv2D)          */
+#define SPX_WEIGHT_HWIO 1 /* [kh][kw][ic][oc]  (HLO b01f_01io->b01f)    */
+typedef struct spx_conv_params {
+  int32_t n, ih, iw, ic, oc, oh, ow, kh, kw;
+  int32_t stride_h, stride_w, pad_top, pad_left, dilation_h, dilation_w;
+  int32_t weight_layout; /* SPX_WEIGHT_*                                  */
+  int32_t activation;    /* SPX_ACT_*                                     */
+} spx_conv_params;
+int spx_op_conv2d_nhwc(spx_graph* g, const float* x, const float* w,
+                       const float* bias, const float* residual, float* y,
+                       const spx_conv_params* p);
+
+/* Depthwise convolution (depth_multiplier 1), NHWC, weights [kh][kw][c]
+ * (TFLite's [1,kh,kw,c]).  Follows depthwise_conv2d.comp:27-49 and the
+ * lowering at scheduler.rs:428-548, with the activation fused. */
+typedef struct spx_dw_params {
+  int32_t n, ih, iw, c, oh, ow, kh, kw;
+  int32_t stride_h, stride_w, pad_top, pad_left, dilation_h, dilation_w;
+  int32_t activation;
+} spx_dw_params;
+int spx_op_depthwise_conv2d_nhwc(spx_graph* g, const float* x, const float* w,
+                                 const float* bias, float* y, const spx_dw_params* p);
+
+/* Batched strided GEMM: C[b][m][n] = act(alpha * sum_k A[b,m,k] B[b,k,n]
+ * + bias[n] + R[b][m][n]).  Element strides let one entry cover
+ * fully_connected (B = W^T), hlo_dot_rank2, hlo_dot_batched with any
+ * contracting/batch dims (compiler.rs:1009-1084, without the host
+ * transposes) and attention QK^T / PV.  C is row-major with row stride c_ms;
+ * R (optional) shares C's strides. */
+typedef struct spx_gemm_params {
+  int32_t batch, m, n, k; /* batch = number of outer batches (>= 1)      */
+  int32_t batch_inner;    /* inner batches per outer batch (>= 1)        */
+  int32_t b_inner_div;    /* B uses inner index / b_inner_div (>= 1):
+                             grouped-query attention shares one K/V head
+                             among b_inner_div query heads               */
+  int64_t a_bs, a_ms, a_ks;  /* A strides: outer batch, row, k           */
+  int64_t b_bs, b_ks, b_ns;  /* B strides: outer batch, k, column        */
+  int64_t c_bs, c_ms;        /* C strides: outer batch, row (column = 1) */
+  int64_t a_bis, b_bis, c_bis; /* inner-batch strides                    */
+  float alpha;
+  int32_t activation;
+} spx_gemm_params;
+int spx_op_gemm(spx_graph* g, const float* a, const float* b, const float* bias,
+                const float* residual, float* c, const spx_gemm_params* p);
+
+/* Window pooling NHWC (max / sum / average), reduce_window semantics of
+ * hlo_reduce_window_rank4.comp:25-49 and max_pool2d.comp:25-44.
+ * Average divides by the number of in-bounds taps. */
+#define SPX_POOL_MAX 1
+#define SPX_POOL_SUM 0
+#define SPX_POOL_AVG 2
+typedef struct spx_pool_params {
+  int32_t n, ih, iw, c, oh, ow, kh, kw, stride_h, stride_w, pad_top, pad_left;
+  int32_t kind;
+} spx_pool_params;
+int spx_op_pool2d_nhwc(spx_graph* g, const float* x, float* y, const spx_pool_params* p);
+
+/* Global average pool NHWC [n][hw][c] -> [n][c] (global_avg_pool_sum.comp +
+ * _finalize.comp in one pass). */
+int spx_op_global_avg_pool_nhwc(spx_graph* g, const float* x, float* y,
+                                int32_t n, int32_t hw, int32_t c);
+
+/* Row softmax over `cols`, for `rows` rows (softmax10/softmax1000.comp,
+ * generalised to batches).  Optional additive mask row-broadcast is not
+ * applied here; see spx_op_attention_softmax. */
+int spx_op_softmax_rows(spx_graph* g, const float* x, float* y, int32_t rows, int32_t cols);
+
+/* Scaled, masked softmax for attention scores [rows][cols]:
+ * y = softmax(scale * x + mask), causal when `causal` != 0 (column j is
+ * masked for j > q_offset + row % q_len).  mask may be NULL. */
+int spx_op_attention_softmax(spx_graph* g, const float* x, float* y, int32_t rows,
+                             int32_t cols, float scale, int32_t causal, int32_t q_len,
+                             int32_t q_offset);
+
+/* Elementwise ops.  Unary codes mirror the reference shader set. */
+#define SPX_UN_ABS 0
+#define SPX_UN_EXP 1
+#define SPX_UN_LOG 2
+#define SPX_UN_NEG 3
+#define SPX_UN_SQRT 4
+#define SPX_UN_RSQRT 5
+#define SPX_UN_SIGMOID 6
+#define SPX_UN_TANH 7
+#define SPX_UN_RELU 8
+#define SPX_UN_RELU6 9
+#define SPX_UN_LEAKY_RELU 10
+#define SPX_UN_SIN 11
+#define SPX_UN_COPY 12
+#define SPX_UN_GELU_ERF 13
+#define SPX_UN_SILU 14
+int spx_op_unary(spx_graph* g, int32_t op, const float* x, float* y, int64_t n, float alpha);
+
+#define SPX_BIN_ADD 0
+#define SPX_BIN_SUB 1
+#define SPX_BIN_MUL 2
+#define SPX_BIN_DIV 3
+#define SPX_BIN_POW 4
+#define SPX_BIN_MIN 5
+#define SPX_BIN_MAX 6
+/* y[i0,i1,i2,i3] = a[.] op b[.] over a rank-4 output with element strides
+ * for a and b (0 = broadcast along that axis), replacing the reference's CPU
+ * broadcast before every HLO elementwise dispatch (compiler.rs:705-729). */
+typedef struct spx_bcast_params {
+  int32_t d[4];
+  int64_t a_stride[4];
+  int64_t b_stride[4];
+} spx_bcast_params;
+int spx_op_binary(spx_graph* g, int32_t op, const float* a, const float* b, float* y,
+                  const spx_bcast_params* p);
+
+/* hlo_reduce_rank4 with the reference's 15 push constants
+ * (compiler.rs:975-991): rank,d0..d3,od0..od3,r0..r3,kind,total. */
+int spx_op_reduce_rank4(spx_graph* g, const float* x, float* y, const int32_t push[15]);
+
+/* Row LayerNorm: y = (x - mean) / sqrt(var + eps) * gamma + beta (+ the
+ * optional residual added to x first, written to x_out when non-NULL). */
+int spx_op_layernorm(spx_graph* g, const float* x, const float* residual, float* x_out,
+                     const float* gamma, const float* beta, float* y, int32_t rows,
+                     int32_t cols, float eps);
+/* Row RMSNorm: y = x / sqrt(mean(x^2) + eps) * gamma. */
+int spx_op_rmsnorm(spx_graph* g, const float* x, const float* gamma, float* y, int32_t rows,
+                   int32_t cols, float eps);
+/* Rotary embedding (rotate-half form) in place on [tokens][heads][head_dim];
+ * positions[t] gives each token's position. */
+int spx_op_rope(spx_graph* g, float* x, const int32_t* positions, int32_t tokens,
+                int32_t heads, int32_t head_dim, float theta);
+/* Embedding gather: y[t][:] = table[ids[t]][:]. */
+int spx_op_embedding(spx_graph* g, const float* table, const int32_t* ids, float* y,
+                     int32_t tokens, int32_t dim);
+/* Row argmax (first maximum wins): idx[r] = argmax_c x[r][c]. */
+int spx_op_argmax_rows(spx_graph* g, const float* x, int32_t* idx, float* val, int32_t rows,
+                       int32_t cols);
+/* y = silu(gate) * up, elementwise over n values. */
+int spx_op_swiglu(spx_graph* g, const float* gate, const float* up, float* y, int64_t n);
+
+/* Rank-4 constant pad (pad.comp with the reference's 13 push constants
+ * od0..3, id0..3, pl0..3, total) and rank-4 permutation (transpose.comp's
+ * 13 push constants in0..3, out0..3, p0..3, total). */
+int spx_op_pad4(spx_graph* g, const float* x, float* y, float pad_value, const int32_t push[13]);
+int spx_op_transpose4(spx_graph* g, const float* x, float* y, const int32_t push[13]);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPX_H_ */

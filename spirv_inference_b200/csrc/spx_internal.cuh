@@ -1,0 +1,123 @@
+// Internal declarations shared by the libspx translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <vector>
+
+#include "spx.h"
+
+// Graph object behind the opaque `spx_graph*` handle.
+struct spx_graph {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  std::vector<void*> buffers;
+  cudaGraph_t cuda_graph = nullptr;
+  cudaGraphExec_t cuda_exec = nullptr;
+  bool capturing = false;
+  int64_t launches = 0;          // kernels launched (or replayed)
+  int64_t captured_launches = 0; // kernels inside the captured CUDA graph
+  int64_t capture_start = 0;
+};
+
+namespace spx {
+
+constexpr int kNumSms = 148;  // B200: 2 dies x 74 SMs
+
+// Thread-local error reporting.  `fail` records a message and returns code.
+int fail(int code, const char* fmt, ...);
+int check_cuda(cudaError_t e, const char* what);
+// Checks the launch that was just issued and bumps the launch counter.
+int after_launch(int64_t* counter, const char* what);
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline int grid_for(int64_t work, int threads, int per_sm = 8) {
+  int64_t g = ceil_div(work, threads);
+  int64_t cap = (int64_t)kNumSms * per_sm;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (int)g;
+}
+
+// Epilogue activation (SPX_ACT_* codes), shared by every fused epilogue.
+__device__ __forceinline__ float apply_act(int act, float v) {
+  switch (act) {
+    case SPX_ACT_RELU: return v > 0.0f ? v : 0.0f;
+    case SPX_ACT_RELU6: return fminf(v > 0.0f ? v : 0.0f, 6.0f);
+    case SPX_ACT_RELU_N1_TO_1: return fminf(fmaxf(v, -1.0f), 1.0f);
+    case SPX_ACT_TANH: return tanhf(v);
+    case SPX_ACT_GELU_ERF: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+    case SPX_ACT_GELU_TANH: {
+      float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+      return 0.5f * v * (1.0f + tanhf(u));
+    }
+    case SPX_ACT_SILU: return v / (1.0f + expf(-v));
+    default: return v;
+  }
+}
+
+// ---- launchers (each returns SPX_OK or an error code) -------------------
+// All take the stream to record on and a launch counter (may be null).
+int launch_unary(cudaStream_t s, int64_t* cnt, int op, const float* x, float* y, int64_t n,
+                 float alpha);
+int launch_binary(cudaStream_t s, int64_t* cnt, int op, const float* a, const float* b,
+                  float* y, const spx_bcast_params* p);
+int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
+                     const float* bias, const float* res, float* y, const spx_conv_params* p);
+int launch_gemm(cudaStream_t s, int64_t* cnt, const float* a, const float* b,
+                const float* bias, const float* res, float* c, const spx_gemm_params* p);
+int launch_dw_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
+                   const float* bias, float* y, const spx_dw_params* p);
+int launch_pool_nhwc(cudaStream_t s, int64_t* cnt, const float* x, float* y,
+                     const spx_pool_params* p);
+int launch_gap_nhwc(cudaStream_t s, int64_t* cnt, const float* x, float* y, int n, int hw,
+                    int c);
+int launch_softmax_rows(cudaStream_t s, int64_t* cnt, const float* x, float* y, int rows,
+                        int cols, float scale, int causal, int q_len, int q_offset);
+int launch_reduce_rank4(cudaStream_t s, int64_t* cnt, const float* x, float* y,
+                        const int32_t* push);
+int launch_layernorm(cudaStream_t s, int64_t* cnt, const float* x, const float* res,
+                     float* x_out, const float* gamma, const float* beta, float* y, int rows,
+                     int cols, float eps);
+int launch_rmsnorm(cudaStream_t s, int64_t* cnt, const float* x, const float* gamma, float* y,
+                   int rows, int cols, float eps);
+int launch_rope(cudaStream_t s, int64_t* cnt, float* x, const int32_t* pos, int tokens,
+                int heads, int head_dim, float theta);
+int launch_embedding(cudaStream_t s, int64_t* cnt, const float* table, const int32_t* ids,
+                     float* y, int tokens, int dim);
+int launch_argmax_rows(cudaStream_t s, int64_t* cnt, const float* x, int32_t* idx, float* val,
+                       int rows, int cols);
+int launch_swiglu(cudaStream_t s, int64_t* cnt, const float* gate, const float* up, float* y,
+                  int64_t n);
+int launch_pad4(cudaStream_t s, int64_t* cnt, const float* x, float* y, float pad_value,
+                const int32_t* push);
+int launch_transpose4(cudaStream_t s, int64_t* cnt, const float* x, float* y,
+                      const int32_t* push);
+
+// Exact-fp32 SIMT implementations (k_gemm_simt.cu).
+int launch_gemm_simt(cudaStream_t s, int64_t* cnt, const float* a, const float* b,
+                     const float* bias, const float* res, float* c, const spx_gemm_params* p);
+int launch_conv_simt(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
+                     const float* bias, const float* res, float* y, const spx_conv_params* p);
+
+// ---- reference-layout kernels used only by the drop-in boundary ---------
+// (NCHW layouts of the TFLite shader set, one output element per thread.)
+int launch_compat_dw_nchw(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
+                          float* y, const int32_t* push);
+int launch_compat_maxpool_nchw(cudaStream_t s, int64_t* cnt, const float* x, float* y,
+                               const int32_t* push);
+int launch_compat_gap_sum_nchw(cudaStream_t s, int64_t* cnt, const float* x, float* y, int n,
+                               int c, int h, int w);
+int launch_compat_gap_finalize(cudaStream_t s, int64_t* cnt, const float* x, float* y, int n,
+                               int c, int h, int w);
+int launch_compat_resize_bilinear(cudaStream_t s, int64_t* cnt, const float* x, float* y,
+                                  const int32_t* push);
+int launch_compat_l2norm(cudaStream_t s, int64_t* cnt, const float* x, float* y, int total,
+                         float norm);
+int launch_compat_concat(cudaStream_t s, int64_t* cnt, const float* a, const float* b, float* y,
+                         int a_total, int total);
+
+}  // namespace spx

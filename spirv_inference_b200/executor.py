@@ -1,0 +1,216 @@
+"""Device-resident executor for TFLite-style CNN graphs (NHWC, fused).
+
+Where the reference scheduler round-trips every op through the host and
+issues activations and residual adds as extra dispatches
+(source/tflite_loader/src/scheduler.rs:75-1039, 1146-1197), this executor:
+
+* uploads weights once in their native TFLite layouts (Conv2D OHWI is the
+  implicit-GEMM B operand as is; depthwise [1,kh,kw,c] is read as
+  [kh][kw][c]; FullyConnected [out][in] is read transposed by strides),
+* keeps every activation in HBM in NHWC,
+* fuses bias + activation into every conv / depthwise / FC epilogue and the
+  residual ADD of an inverted-residual block into the projecting 1x1 conv,
+* treats RESHAPE as an alias, and
+* records the whole graph on one stream, optionally captured once into a
+  CUDA graph and replayed.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import _lib
+from .graph import DeviceTensor, Graph
+from .lowering import same_padding_offsets
+from .nets import Model
+
+
+class CnnExecutor:
+    def __init__(self, model: Model, batch: int, device: int = 0, graph: Graph | None = None,
+                 fuse_residual: bool = True):
+        self.model = model
+        self.batch = batch
+        self.g = graph or Graph(device)
+        self.fuse_residual = fuse_residual
+        self.w: dict[str, DeviceTensor] = {}
+        for name, arr in model.weights.items():
+            self.w[name] = self.g.tensor(arr)
+        self.t: dict[str, DeviceTensor] = {}
+        self._plan = []
+        self._build()
+        self._captured = False
+
+    # -- planning ------------------------------------------------------------
+    def _buf(self, name: str) -> DeviceTensor:
+        if name not in self.t:
+            self.t[name] = self.g.alloc((self.batch,) + tuple(self.model.shapes[name]))
+        return self.t[name]
+
+    def _build(self) -> None:
+        m = self.model
+        uses: dict[str, int] = {}
+        for op in m.ops:
+            for i in op.inputs:
+                uses[i] = uses.get(i, 0) + 1
+        # Residual fusion: ADD(conv_out, skip) where conv_out feeds only the ADD
+        # and the conv has no activation -> conv epilogue adds `skip`.
+        fused_into: dict[str, tuple[str, str]] = {}  # conv output -> (add output, skip)
+        if self.fuse_residual:
+            producers = {op.output: op for op in m.ops}
+            for op in m.ops:
+                if op.type != "ADD" or op.attrs.get("activation", 0):
+                    continue
+                for ci, si in ((0, 1), (1, 0)):
+                    p = producers.get(op.inputs[ci])
+                    if (p is not None and p.type == "CONV_2D" and uses[p.output] == 1
+                            and p.attrs.get("activation", 0) == 0):
+                        fused_into[p.output] = (op.output, op.inputs[si])
+                        break
+        skip_adds = {v[0] for v in fused_into.values()}
+        self._buf(m.input)
+        for op in m.ops:
+            a = op.attrs
+            if op.type == "CONV_2D":
+                x = self._buf(op.inputs[0])
+                res = None
+                out_name = op.output
+                if op.output in fused_into:
+                    out_name, skip = fused_into[op.output]
+                    res = self._buf(skip)
+                y = self._buf(out_name)
+                self.t[op.output] = y
+                w = self.w[op.inputs[1]]
+                kh, kw = w.shape[1], w.shape[2]
+                ih, iw = x.shape[1], x.shape[2]
+                oh, ow = y.shape[1], y.shape[2]
+                pt, pl = same_padding_offsets(a["padding"], ih, iw, oh, ow, kh, kw, *a["stride"])
+                self._plan.append(("conv", dict(x=x, w=w, bias=self.w[op.inputs[2]], y=y,
+                                                stride=a["stride"], pad=(pt, pl),
+                                                activation=a.get("activation", 0),
+                                                residual=res)))
+            elif op.type == "DEPTHWISE_CONV_2D":
+                x, y = self._buf(op.inputs[0]), self._buf(op.output)
+                w = self.w[op.inputs[1]]
+                kh, kw = w.shape[1], w.shape[2]
+                dil = a.get("dilation", (1, 1))
+                pt, pl = same_padding_offsets(a["padding"], x.shape[1], x.shape[2], y.shape[1],
+                                              y.shape[2], (kh - 1) * dil[0] + 1,
+                                              (kw - 1) * dil[1] + 1, *a["stride"])
+                self._plan.append(("dw", dict(x=x, w=w.view((kh, kw, w.shape[3])),
+                                              bias=self.w[op.inputs[2]], y=y, stride=a["stride"],
+                                              pad=(pt, pl), dilation=dil,
+                                              activation=a.get("activation", 0))))
+            elif op.type == "ADD":
+                if op.output in skip_adds:
+                    continue
+                a_, b_ = self._buf(op.inputs[0]), self._buf(op.inputs[1])
+                self._plan.append(("add", dict(a=a_, b=b_, y=self._buf(op.output))))
+            elif op.type == "AVERAGE_POOL_2D":
+                x, y = self._buf(op.inputs[0]), self._buf(op.output)
+                self._plan.append(("gap", dict(x=x, y=y)))
+            elif op.type == "RESHAPE":
+                x = self._buf(op.inputs[0])
+                self.t[op.output] = x.view((self.batch,) + tuple(m.shapes[op.output]))
+            elif op.type == "FULLY_CONNECTED":
+                x, y = self._buf(op.inputs[0]), self._buf(op.output)
+                w = self.w[op.inputs[1]]
+                out, inp = w.shape
+                self._plan.append(("fc", dict(x=x, w=w, bias=self.w[op.inputs[2]], y=y, m=self.batch,
+                                              n=out, k=inp, activation=a.get("activation", 0))))
+            elif op.type == "SOFTMAX":
+                x, y = self._buf(op.inputs[0]), self._buf(op.output)
+                self._plan.append(("softmax", dict(x=x, y=y, rows=self.batch,
+                                                   cols=x.size // self.batch)))
+            else:
+                raise NotImplementedError(f"op {op.type}")
+        self.input = self.t[m.input]
+        self.output = self.t[m.output]
+
+    # -- execution -------------------------------------------------------------
+    def record(self) -> None:
+        """Records the whole graph onto the graph's stream (asynchronous)."""
+        g = self.g
+        for kind, p in self._plan:
+            if kind == "conv":
+                g.conv2d_nhwc(p["x"], p["w"], p["bias"], p["y"], stride=p["stride"], pad=p["pad"],
+                              activation=p["activation"], residual=p["residual"])
+            elif kind == "dw":
+                g.depthwise_nhwc(p["x"], p["w"], p["bias"], p["y"], stride=p["stride"],
+                                 pad=p["pad"], dilation=p["dilation"], activation=p["activation"])
+            elif kind == "add":
+                g.add(p["a"], p["b"], p["y"])
+            elif kind == "gap":
+                g.global_avg_pool_nhwc(p["x"], p["y"])
+            elif kind == "fc":
+                g.gemm(p["x"], p["w"], p["y"], m=p["m"], n=p["n"], k=p["k"],
+                       a_strides=(0, p["k"], 1), b_strides=(0, 1, p["k"]), c_strides=(0, p["n"]),
+                       bias=p["bias"], activation=p["activation"])
+            elif kind == "softmax":
+                g.softmax_rows(p["x"], p["y"], p["rows"], p["cols"])
+
+    @property
+    def kernels_per_run(self) -> int:
+        return len(self._plan)
+
+    def op_costs(self) -> list[dict]:
+        """Algorithmic cost of each recorded kernel: flops (2 x MACs) and HBM
+        bytes (every input / weight / bias / residual read once, the output
+        written once, fp32)."""
+        out = []
+        for kind, p in self._plan:
+            if kind == "conv":
+                x, w, y = p["x"], p["w"], p["y"]
+                k = w.shape[1] * w.shape[2] * w.shape[3]
+                f = 2 * y.size * k
+                b = x.size + w.size + y.shape[-1] + y.size + (y.size if p["residual"] else 0)
+                label = f"conv{w.shape[1]}x{w.shape[2]}"
+            elif kind == "dw":
+                x, w, y = p["x"], p["w"], p["y"]
+                f = 2 * y.size * w.shape[0] * w.shape[1]
+                b = x.size + w.size + y.shape[-1] + y.size
+                label = f"dw{w.shape[0]}x{w.shape[1]}"
+            elif kind == "add":
+                f, b, label = p["y"].size, 3 * p["y"].size, "add"
+            elif kind == "gap":
+                f, b, label = p["x"].size, p["x"].size + p["y"].size, "gap"
+            elif kind == "fc":
+                f = 2 * p["m"] * p["n"] * p["k"]
+                b = p["m"] * p["k"] + p["n"] * p["k"] + p["n"] + p["m"] * p["n"]
+                label = "fc"
+            else:
+                f, b, label = 3 * p["x"].size, 2 * p["x"].size, "softmax"
+            out.append({"kind": kind, "label": label, "flops": int(f), "bytes": int(4 * b)})
+        return out
+
+    def record_op(self, i: int) -> None:
+        """Records only plan entry i (for per-kernel timing)."""
+        plan, self._plan = self._plan, [self._plan[i]]
+        try:
+            self.record()
+        finally:
+            self._plan = plan
+
+    def capture(self) -> None:
+        """Captures one recording into a CUDA graph for replay()."""
+        self.g.sync()
+        self.g.capture_begin()
+        self.record()
+        self.g.capture_end()
+        self._captured = True
+
+    def run(self) -> None:
+        if self._captured:
+            self.g.replay()
+        else:
+            self.record()
+
+    def forward(self, x_nhwc: np.ndarray) -> np.ndarray:
+        """Host in, host out: upload, run, download (synchronous)."""
+        self.g.upload(self.input, x_nhwc)
+        self.run()
+        return self.g.download(self.output)
+
+    def tensor(self, name: str) -> np.ndarray:
+        return self.g.download(self.t[name])
+
+    def close(self) -> None:
+        self.g.close()

@@ -1,0 +1,112 @@
+"""Independent float64 numpy formulations of the kernel math.
+
+Used to cross-check the C++ oracle (a second, structurally different
+implementation: vectorised tensor algebra instead of per-output loops) and
+the graph-API ops whose layout has no reference kernel (NHWC depthwise etc.).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def conv_nhwc(x, w_hwio, stride, pad_tl, out_hw, dilation=(1, 1)):
+    """x [n,ih,iw,ic], w [kh,kw,ic,oc]; low-side pad pad_tl, out size out_hw."""
+    x = x.astype(np.float64)
+    w = w_hwio.astype(np.float64)
+    n, ih, iw, ic = x.shape
+    kh, kw, _, oc = w.shape
+    oh, ow = out_hw
+    y = np.zeros((n, oh, ow, oc))
+    for ky in range(kh):
+        for kx in range(kw):
+            iy = np.arange(oh) * stride[0] + ky * dilation[0] - pad_tl[0]
+            ix = np.arange(ow) * stride[1] + kx * dilation[1] - pad_tl[1]
+            vy = (iy >= 0) & (iy < ih)
+            vx = (ix >= 0) & (ix < iw)
+            patch = np.zeros((n, oh, ow, ic))
+            sub = x[:, np.clip(iy, 0, ih - 1)][:, :, np.clip(ix, 0, iw - 1)]
+            mask = (vy[:, None] & vx[None, :])[None, :, :, None]
+            patch = np.where(mask, sub, 0.0)
+            y += patch @ w[ky, kx]
+    return y
+
+
+def conv_nchw(x, w_oihw, bias, stride, pad_tl, out_hw):
+    y = conv_nhwc(np.transpose(x, (0, 2, 3, 1)), np.transpose(w_oihw, (2, 3, 1, 0)), stride,
+                  pad_tl, out_hw)
+    return np.transpose(y + bias.astype(np.float64), (0, 3, 1, 2))
+
+
+def depthwise_nhwc(x, w_hwc, bias, stride, pad_tl, out_hw, dilation=(1, 1)):
+    x = x.astype(np.float64)
+    n, ih, iw, c = x.shape
+    kh, kw, _ = w_hwc.shape
+    oh, ow = out_hw
+    y = np.zeros((n, oh, ow, c)) + (bias.astype(np.float64) if bias is not None else 0.0)
+    for ky in range(kh):
+        for kx in range(kw):
+            iy = np.arange(oh) * stride[0] + ky * dilation[0] - pad_tl[0]
+            ix = np.arange(ow) * stride[1] + kx * dilation[1] - pad_tl[1]
+            vy = (iy >= 0) & (iy < ih)
+            vx = (ix >= 0) & (ix < iw)
+            sub = x[:, np.clip(iy, 0, ih - 1)][:, :, np.clip(ix, 0, iw - 1)]
+            mask = (vy[:, None] & vx[None, :])[None, :, :, None]
+            y += np.where(mask, sub, 0.0) * w_hwc[ky, kx].astype(np.float64)
+    return y
+
+
+def pool_nhwc(x, k, stride, pad_tl, out_hw, kind):
+    """kind 1 max, 0 sum, 2 average over in-range taps."""
+    x = x.astype(np.float64)
+    n, ih, iw, c = x.shape
+    oh, ow = out_hw
+    acc = np.full((n, oh, ow, c), -3.4028234663852886e38 if kind == 1 else 0.0)
+    cnt = np.zeros((1, oh, ow, 1))
+    for ky in range(k[0]):
+        for kx in range(k[1]):
+            iy = np.arange(oh) * stride[0] + ky - pad_tl[0]
+            ix = np.arange(ow) * stride[1] + kx - pad_tl[1]
+            vy = (iy >= 0) & (iy < ih)
+            vx = (ix >= 0) & (ix < iw)
+            mask = (vy[:, None] & vx[None, :])[None, :, :, None]
+            sub = x[:, np.clip(iy, 0, ih - 1)][:, :, np.clip(ix, 0, iw - 1)]
+            cnt += mask
+            if kind == 1:
+                acc = np.where(mask, np.maximum(acc, sub), acc)
+            else:
+                acc = acc + np.where(mask, sub, 0.0)
+    if kind == 2:
+        acc = acc / np.maximum(cnt, 1)
+    return acc
+
+
+def softmax_rows(x):
+    x = x.astype(np.float64)
+    e = np.exp(x - x.max(axis=-1, keepdims=True))
+    return e / e.sum(axis=-1, keepdims=True)
+
+
+def resize_bilinear_nchw(x, oh, ow, align_corners, half_pixel):
+    n, c, ih, iw = x.shape
+
+    def coords(o, i_size, o_size):
+        o = np.arange(o_size, dtype=np.float64)
+        if align_corners and o_size > 1:
+            s = o * (i_size - 1) / (o_size - 1)
+        elif half_pixel:
+            s = (o + 0.5) * i_size / o_size - 0.5
+        else:
+            s = o * i_size / o_size
+        return np.clip(s, 0, i_size - 1)
+
+    ys, xs = coords(None, ih, oh), coords(None, iw, ow)
+    y0 = np.floor(ys).astype(int)
+    x0 = np.floor(xs).astype(int)
+    y1 = np.minimum(y0 + 1, ih - 1)
+    x1 = np.minimum(x0 + 1, iw - 1)
+    yl = (ys - y0)[:, None]
+    xl = (xs - x0)[None, :]
+    xd = x.astype(np.float64)
+    top = xd[:, :, y0][:, :, :, x0] * (1 - xl) + xd[:, :, y0][:, :, :, x1] * xl
+    bot = xd[:, :, y1][:, :, :, x0] * (1 - xl) + xd[:, :, y1][:, :, :, x1] * xl
+    return top * (1 - yl) + bot * yl

@@ -1,0 +1,140 @@
+"""CPU tests of the host side: the C-ABI library loads and exports every
+declared symbol, the registry mirrors the reference's, argument errors are
+reported without touching a device, and the TFLite-style graphs have the
+reference's structure."""
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from spirv_inference_b200 import _lib, dispatch, lowering, nets
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _declared_functions() -> list[str]:
+    text = (ROOT / "include" / "spx.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(spx_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol(spx_built):
+    out = subprocess.run(["nm", "-D", "--defined-only", str(spx_built)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r" T (spx_\w+)", out))
+    declared = _declared_functions()
+    assert declared, "no declarations parsed"
+    missing = [d for d in declared if d not in exported]
+    assert not missing, missing
+    l = _lib.lib()
+    for d in declared:
+        assert hasattr(l, d)
+    assert set(_lib.exported_symbols()) <= set(declared)
+
+
+def test_library_is_sm100a_only(spx_built):
+    # cuobjdump --list-elf only lists the embedded ELF names (arch tags); it
+    # does not disassemble anything.
+    r = subprocess.run(["/usr/local/cuda/bin/cuobjdump", "--list-elf", str(spx_built)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    arches = set(re.findall(r"sm_\w+", r.stdout))
+    assert arches == {"sm_100a"}, arches
+
+
+def test_registry_matches_library(spx_built):
+    l = _lib.lib()
+    names = [l.spx_kernel_name(i).decode() for i in range(l.spx_kernel_count())]
+    reg = dispatch.registry()
+    assert sorted(names) == sorted(reg)
+    for name, spec in reg.items():
+        assert l.spx_kernel_push_count(name.encode()) == len(spec.push_constants), name
+        assert l.spx_kernel_push_count(spec.spv.encode()) == len(spec.push_constants), name
+    assert l.spx_kernel_push_count(b"nope") == -1
+    # kernels.rs:12-238 order and push names for the TFLite set
+    assert [k.name for k in dispatch.TFLITE_KERNELS][:5] == ["add", "sub", "mul", "div", "pow"]
+    conv = reg["conv2d"]
+    assert conv.push_constants[-1] == "total" and conv.push_constants[11] == "same"
+
+
+def test_groups():
+    assert dispatch.groups(65, 64) == 2 and dispatch.groups(64, 64) == 1
+
+
+def test_unknown_kernel_is_unsupported(spx_built):
+    with pytest.raises(_lib.SpxError) as e:
+        dispatch.run_kernel(0, dispatch.KernelRun("x", "warp_drive.spv", np.ones(1), np.ones(1), 1,
+                                                  1, [1]))
+    assert e.value.code == _lib.SPX_ERR_UNSUPPORTED
+    assert "warp_drive" in str(e.value)
+
+
+def test_bad_push_count_is_invalid(spx_built):
+    with pytest.raises(_lib.SpxError) as e:
+        dispatch.run_kernel(0, dispatch.KernelRun("x", "conv2d.spv", np.ones(1), np.ones(1), 1, 1,
+                                                  [1, 2, 3]))
+    assert e.value.code == _lib.SPX_ERR_INVALID_ARGUMENT
+
+
+def test_no_device_behaviour(spx_built):
+    l = _lib.lib()
+    if l.spx_device_count() > 0:
+        pytest.skip("a CUDA device is present")
+    with pytest.raises(_lib.SpxError) as e:
+        dispatch.run_kernel("any", dispatch.KernelRun("x", "relu", np.ones(4), np.ones(1), 4, 1, [4]))
+    assert e.value.code == _lib.SPX_ERR_NO_DEVICE
+    h = ctypes.c_void_p()
+    assert l.spx_graph_create(0, ctypes.byref(h)) == _lib.SPX_ERR_NO_DEVICE
+    assert l.spx_op_unary(None, 0, None, None, 0, 0.0) == _lib.SPX_ERR_INVALID_ARGUMENT
+    o = ctypes.c_int()
+    assert l.spx_select_device(b"intel", ctypes.byref(o)) == _lib.SPX_ERR_NO_DEVICE
+
+
+def test_models_structure():
+    m = nets.mobilenet_v2(seed=0)
+    # source/tflite_loader/TFLITE_REPORT.md:16 histogram
+    assert m.op_counts() == {"CONV_2D": 36, "DEPTHWISE_CONV_2D": 17, "ADD": 10,
+                             "AVERAGE_POOL_2D": 1, "RESHAPE": 1, "SOFTMAX": 1}
+    assert abs(m.flops_per_image() / 1e9 - 0.6015) < 1e-3
+    assert m.shapes[m.output] == (1001,)
+    e = nets.efficientnet_lite0(seed=0)
+    assert e.op_counts()["DEPTHWISE_CONV_2D"] == 16
+    assert e.shapes[e.output] == (1000,)
+    # seeded: identical weights on rebuild
+    m2 = nets.mobilenet_v2(seed=0)
+    for k in m.weights:
+        assert np.array_equal(m.weights[k], m2.weights[k])
+
+
+def test_packing_and_padding():
+    w = np.arange(2 * 3 * 3 * 4, dtype=np.float32).reshape(2, 3, 3, 4)
+    b = np.array([100, 200], np.float32)
+    p = lowering.pack_conv_weight(w, b)
+    assert p.size == w.size + 2 and p[-1] == 200
+    oihw = p[:-2].reshape(2, 4, 3, 3)
+    assert oihw[1, 2, 0, 1] == w[1, 0, 1, 2]
+    d = lowering.pack_depthwise_weight(np.arange(9 * 5, dtype=np.float32).reshape(1, 3, 3, 5),
+                                       np.zeros(5, np.float32))
+    assert d[:-5].reshape(5, 3, 3)[4, 1, 2] == (1 * 3 + 2) * 5 + 4
+    # SAME with stride 2 on an even size pads 0 on top, 1 on the bottom
+    assert lowering.same_padding_offsets("SAME", 224, 224, 112, 112, 3, 3, 2, 2) == (0, 0)
+    assert lowering.same_padding_offsets("SAME", 7, 7, 7, 7, 5, 5, 1, 1) == (2, 2)
+    assert lowering.same_padding_offsets("VALID", 7, 7, 5, 5, 3, 3, 1, 1) == (0, 0)
+
+
+def test_lowering_dispatch_sequence_with_oracle(oracle_built):
+    m = nets.mobilenet_v2(seed=3)
+    x = nets.make_input(m, 1)
+    out, rep = lowering.run_graph(m, x, oracle_built.run_kernel)
+    c = {}
+    for d in rep["dispatches"]:
+        c[d] = c.get(d, 0) + 1
+    # 36 conv (+ 35 relu6 post-ops: all but the 17 linear projections and the
+    # classifier), 17 depthwise (+17 relu6), 10 adds, 2 pool passes, reshape, softmax
+    assert c["conv2d.spv"] == 36 and c["depthwise_conv2d.spv"] == 17
+    assert c["relu6.spv"] == 36 - 17 - 1 + 17
+    assert c["add.spv"] == 10 and c["softmax1000.spv"] == 1
+    assert out.shape == (1, 1001) and abs(float(out.sum()) - 1.0) < 1e-5
