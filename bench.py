@@ -174,7 +174,8 @@ def run_spx(args) -> None:
 
     model = nets.MODELS[args.model](seed=0)
     B = args.batch
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()  # a real stream: the legacy default stream cannot be captured
+    torch.cuda.set_stream(stream)
     g = Graph(local, stream=stream.cuda_stream)
     ex = CnnExecutor(model, batch=B, graph=g)
     x = nets.make_input(model, B, seed=1000 + rank)  # this rank's shard of the global batch

@@ -74,6 +74,12 @@ int spx_device_count(void);
  * ordinal.  "intel" has no CUDA device and fails with SPX_ERR_NO_DEVICE. */
 int spx_select_device(const char* selector, int* ordinal);
 
+/* Process-wide options.  "gemm_path": 0 = automatic (tensor cores where the
+ * operands allow, exact-fp32 SIMT otherwise), 1 = SIMT only, 2 = tensor cores
+ * required (shapes they cannot take fail with SPX_ERR_UNSUPPORTED). */
+int spx_set_option(const char* name, int64_t value);
+int64_t spx_get_option(const char* name);
+
 /* ---- kernel registry (mirror of kernels.rs:12-238 + HLO kernels) ------- */
 int spx_kernel_count(void);
 /* Name of registry entry i (0 <= i < spx_kernel_count()), NULL if out of range. */

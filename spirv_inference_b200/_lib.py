@@ -80,6 +80,8 @@ _SIGS = {
     "spx_version": ([], c_char_p),
     "spx_device_count": ([], c_int),
     "spx_select_device": ([c_char_p, POINTER(c_int)], c_int),
+    "spx_set_option": ([c_char_p, c_int64], c_int),
+    "spx_get_option": ([c_char_p], c_int64),
     "spx_kernel_count": ([], c_int),
     "spx_kernel_name": ([c_int], c_char_p),
     "spx_kernel_push_count": ([c_char_p], c_int),
@@ -149,6 +151,14 @@ def lib():
 
 def exported_symbols() -> list[str]:
     return list(_SIGS)
+
+
+def set_option(name: str, value: int) -> None:
+    check(lib().spx_set_option(name.encode(), int(value)))
+
+
+def get_option(name: str) -> int:
+    return int(lib().spx_get_option(name.encode()))
 
 
 def last_error() -> str:

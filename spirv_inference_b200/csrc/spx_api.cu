@@ -40,6 +40,8 @@ int after_launch(int64_t* counter, const char* what) {
   return SPX_OK;
 }
 
+int g_gemm_path = 0;
+
 // ---- algorithm selection for dense contractions ---------------------------
 int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
                      const float* bias, const float* res, float* y, const spx_conv_params* p) {
@@ -50,6 +52,16 @@ int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* 
     return fail(SPX_ERR_INVALID_ARGUMENT, "conv2d_nhwc: weight_layout %d", p->weight_layout);
   if ((int64_t)p->n * p->oh * p->ow > INT32_MAX || (int64_t)p->kh * p->kw * p->ic > INT32_MAX)
     return fail(SPX_ERR_INVALID_ARGUMENT, "conv2d_nhwc: GEMM extent exceeds int32");
+  const bool pointwise = p->kh == 1 && p->kw == 1 && p->stride_h == 1 && p->stride_w == 1 &&
+                         p->pad_top == 0 && p->pad_left == 0 && p->oh == p->ih && p->ow == p->iw;
+  if (g_gemm_path != 1 && pointwise && p->weight_layout == SPX_WEIGHT_OHWI) {
+    const int M = p->n * p->oh * p->ow;
+    if (gemm_tc_eligible(x, p->ic, w, p->ic, M, p->oc, p->ic, y, p->oc))
+      return launch_gemm_tc(s, cnt, x, p->ic, w, p->ic, M, p->oc, p->ic, bias, res, y, p->oc,
+                            1.0f, p->activation);
+  }
+  if (g_gemm_path == 2)
+    return fail(SPX_ERR_UNSUPPORTED, "conv2d_nhwc: shape not eligible for the tensor-core path");
   return launch_conv_simt(s, cnt, x, w, bias, res, y, p);
 }
 
@@ -57,6 +69,13 @@ int launch_gemm(cudaStream_t s, int64_t* cnt, const float* a, const float* b, co
                 const float* res, float* c, const spx_gemm_params* p) {
   if (p->batch <= 0 || p->m <= 0 || p->n <= 0 || p->k <= 0)
     return fail(SPX_ERR_INVALID_ARGUMENT, "gemm: non-positive extent");
+  const bool single = p->batch == 1 && (p->batch_inner <= 1);
+  if (g_gemm_path != 1 && single && p->a_ks == 1 && p->b_ks == 1 &&
+      gemm_tc_eligible(a, p->a_ms, b, p->b_ns, p->m, p->n, p->k, c, p->c_ms))
+    return launch_gemm_tc(s, cnt, a, p->a_ms, b, p->b_ns, p->m, p->n, p->k, bias, res, c, p->c_ms,
+                          p->alpha, p->activation);
+  if (g_gemm_path == 2)
+    return fail(SPX_ERR_UNSUPPORTED, "gemm: operands not eligible for the tensor-core path");
   return launch_gemm_simt(s, cnt, a, b, bias, res, c, p);
 }
 
@@ -394,6 +413,29 @@ int spx_select_device(const char* selector, int* ordinal) {
   return SPX_OK;
 }
 
+int spx_set_option(const char* name, int64_t value) {
+  std::string n = name ? name : "";
+  if (n == "gemm_path") {
+    if (value < 0 || value > 2) return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_path must be 0..2");
+    g_gemm_path = (int)value;
+    return SPX_OK;
+  }
+  return fail(SPX_ERR_INVALID_ARGUMENT, "unknown option '%s'", n.c_str());
+}
+
+int64_t spx_get_option(const char* name) {
+  std::string n = name ? name : "";
+  if (n == "gemm_path") return g_gemm_path;
+  return -1;
+}
+
+static int device_status(const char* what) {
+  if (tc_take_status())
+    return fail(SPX_ERR_CUDA, "%s: a tensor-core pipeline wait timed out; tiles were abandoned",
+                what);
+  return SPX_OK;
+}
+
 int spx_kernel_count(void) { return kNumKernels; }
 const char* spx_kernel_name(int i) { return i >= 0 && i < kNumKernels ? kKernels[i].name : nullptr; }
 int spx_kernel_push_count(const char* name) {
@@ -462,6 +504,7 @@ int spx_run_kernel(const char* kernel, const float* input0, size_t input0_len,
                                        cudaMemcpyDeviceToHost, c.stream), "download output")))
     return rc;
   if ((rc = check_cuda(cudaStreamSynchronize(c.stream), "kernel execution"))) return rc;
+  if ((rc = device_status(k.c_str()))) return rc;
   if (info) {
     float ms = 0.0f;
     cudaEventElapsedTime(&ms, c.ev0, c.ev1);
@@ -532,7 +575,9 @@ void spx_graph_reset_launch_count(spx_graph* g) {
 
 int spx_graph_sync(spx_graph* g) {
   SPX_G(g);
-  return check_cuda(cudaStreamSynchronize(g->stream), "graph execution");
+  int rc = check_cuda(cudaStreamSynchronize(g->stream), "graph execution");
+  if (rc) return rc;
+  return device_status("graph execution");
 }
 
 int spx_graph_capture_begin(spx_graph* g) {

@@ -103,6 +103,20 @@ int launch_gemm_simt(cudaStream_t s, int64_t* cnt, const float* a, const float* 
 int launch_conv_simt(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
                      const float* bias, const float* res, float* y, const spx_conv_params* p);
 
+// tcgen05 3xTF32 GEMM (k_gemm_tc.cu): both operands K-contiguous.
+bool gemm_tc_eligible(const float* a, int64_t lda, const float* b, int64_t ldb, int M, int N,
+                      int K, const float* c, int64_t ldc);
+int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, const float* b,
+                   int64_t ldb, int M, int N, int K, const float* bias, const float* res, float* c,
+                   int64_t ldc, float alpha, int act);
+// Returns and clears the device status of the tensor-core pipeline (0 = ok,
+// 1 = a pipeline wait timed out and the kernel aborted its tiles).
+int tc_take_status();
+
+// Process-wide dense-contraction path: 0 auto, 1 SIMT only, 2 tensor cores
+// required (ineligible shapes fail with SPX_ERR_UNSUPPORTED).
+extern int g_gemm_path;
+
 // ---- reference-layout kernels used only by the drop-in boundary ---------
 // (NCHW layouts of the TFLite shader set, one output element per thread.)
 int launch_compat_dw_nchw(cudaStream_t s, int64_t* cnt, const float* x, const float* w,

@@ -89,7 +89,7 @@ def _cases():
                   [n, ch, ih, iw, oh, oh, k, k, s, s, 1, pt, pt, dil, dil, tot], 1e-5))
     c.append(("fully_connected", _r(5, 37), _r(11 * 37 + 11), 55, [5, 37, 11, 55], 1e-5))
     c.append(("fully_connected", _r(64, 1280), _r(1000 * 1280 + 1000), 64000,
-              [64, 1280, 1000, 64000], 1e-4))
+              [64, 1280, 1000, 64000], ("norm", 1280)))
     c.append(("hlo_conv_nhwc_hwio", _r(2, 9, 9, 6), _r(3 * 3 * 6 * 10), 2 * 5 * 5 * 10,
               [2, 9, 9, 6, 3, 3, 10, 5, 5, 2, 2, 1, 1, 500], 1e-5))
     c.append(("hlo_conv_nhwc_hwio", _r(1, 14, 14, 64), _r(64 * 96), 14 * 14 * 96,
@@ -127,6 +127,13 @@ def test_kernel_vs_oracle(gpu, oracle_built, case):
     got = spx_rk(kernel, in0, in1, nout, push)
     if tol is None:
         assert np.array_equal(got.view(np.int32), want.view(np.int32)), kernel
+    elif isinstance(tol, tuple):
+        # Dense contractions that may run on the tensor cores: the 3xTF32
+        # accumulate truncates, so the error grows with the K/8 accumulation
+        # steps.  Normwise bound: max|got - want| <= (2.5e-8 K + 1e-6) max|want|.
+        K = tol[1]
+        err = float(np.abs(got - want).max()) / float(np.abs(want).max())
+        assert err <= 2.5e-8 * K + 1e-6, (kernel, err)
     else:
         np.testing.assert_allclose(got, want, rtol=tol, atol=tol)
 

@@ -1,0 +1,84 @@
+"""GPU tests of the tcgen05 3xTF32 tensor-core GEMM (forced with
+gemm_path = 2) against float64 numpy and the exact-fp32 SIMT path."""
+import numpy as np
+import pytest
+
+from spirv_inference_b200 import _lib
+from spirv_inference_b200.graph import Graph
+
+pytestmark = pytest.mark.gpu
+RNG = np.random.default_rng(21)
+
+
+@pytest.fixture
+def g(gpu):
+    _lib.set_option("gemm_path", 2)
+    try:
+        with Graph(gpu) as graph:
+            yield graph
+    finally:
+        _lib.set_option("gemm_path", 0)
+
+
+def _r(*shape, scale=1.0):
+    return (RNG.uniform(-1, 1, size=shape) * scale).astype(np.float32)
+
+
+SHAPES = [  # M, N, K
+    (128, 16, 32), (200, 24, 16), (1000, 96, 24), (517, 144, 96), (4096, 240, 960),
+    (333, 1001, 1280), (2048, 1280, 320), (64, 1000, 1280), (130, 48, 36), (5, 8, 4),
+]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_tc_gemm_matches_fp64(g, M, N, K):
+    a = _r(M, K)
+    w = _r(N, K, scale=1.0 / np.sqrt(K))
+    bias = _r(N)
+    dc = g.alloc((M, N))
+    g.gemm(g.tensor(a), g.tensor(w), dc, m=M, n=N, k=K, a_strides=(0, K, 1), b_strides=(0, 1, K),
+           c_strides=(0, N), bias=g.tensor(bias))
+    out = dc.download()
+    ref = a.astype(np.float64) @ w.T.astype(np.float64) + bias
+    # 3xTF32: per-product relative error ~2^-21 -> well inside fp32-level tolerance
+    np.testing.assert_allclose(out, ref, rtol=2e-5, atol=2e-6 * np.sqrt(K))
+
+
+def test_tc_pointwise_conv_epilogue(g):
+    n, h, w, ic, oc = 2, 56, 56, 24, 144
+    x = _r(n, h, w, ic)
+    wt = _r(oc, 1, 1, ic, scale=0.3)
+    b = _r(oc)
+    res = _r(n, h, w, oc)
+    dy = g.alloc((n, h, w, oc))
+    g.conv2d_nhwc(g.tensor(x), g.tensor(wt), g.tensor(b), dy, activation=_lib.ACT_RELU6,
+                  residual=g.tensor(res))
+    ref = np.clip(x.reshape(-1, ic).astype(np.float64) @ wt.reshape(oc, ic).T + b
+                  + res.reshape(-1, oc), 0, 6).reshape(n, h, w, oc)
+    np.testing.assert_allclose(dy.download(), ref, rtol=2e-5, atol=2e-5)
+
+
+def test_tc_and_simt_agree(gpu):
+    M, N, K = 3000, 96, 144
+    a, w = _r(M, K), _r(N, K, scale=0.1)
+    outs = []
+    for path in (1, 2):
+        _lib.set_option("gemm_path", path)
+        try:
+            with Graph(gpu) as g:
+                dc = g.alloc((M, N))
+                g.gemm(g.tensor(a), g.tensor(w), dc, m=M, n=N, k=K, a_strides=(0, K, 1),
+                       b_strides=(0, 1, K), c_strides=(0, N))
+                outs.append(dc.download())
+        finally:
+            _lib.set_option("gemm_path", 0)
+    np.testing.assert_allclose(outs[0], outs[1], rtol=2e-5, atol=2e-5)
+
+
+def test_tc_ineligible_shape_reports_unsupported(g):
+    a, w = _r(10, 6), _r(8, 6)  # K = 6 is not a multiple of 4 (TMA row pitch)
+    dc = g.alloc((10, 8))
+    with pytest.raises(_lib.SpxError) as e:
+        g.gemm(g.tensor(a), g.tensor(w), dc, m=10, n=8, k=6, a_strides=(0, 6, 1),
+               b_strides=(0, 1, 6), c_strides=(0, 8))
+    assert e.value.code == _lib.SPX_ERR_UNSUPPORTED
