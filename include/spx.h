@@ -164,6 +164,16 @@ int spx_op_conv2d_nhwc(spx_graph* g, const float* x, const float* w,
                        const float* bias, const float* residual, float* y,
                        const spx_conv_params* p);
 
+/* Weights prepared once for the tensor-core path, which multiplies fp32 data
+ * as two tf32 terms (3xTF32): w_hi = tf32 round-to-nearest of w,
+ * w_lo = tf32(w - w_hi); n floats each, device buffers.  The *_split ops take
+ * w (used by every non-tensor-core path) plus w_hi / w_lo, so the weight
+ * split is not repeated for every output tile. */
+int spx_weights_split(spx_graph* g, const float* w, float* w_hi, float* w_lo, int64_t n);
+int spx_op_conv2d_nhwc_split(spx_graph* g, const float* x, const float* w, const float* w_hi,
+                             const float* w_lo, const float* bias, const float* residual, float* y,
+                             const spx_conv_params* p);
+
 /* Depthwise convolution (depth_multiplier 1), NHWC, weights [kh][kw][c]
  * (TFLite's [1,kh,kw,c]).  Follows depthwise_conv2d.comp:27-49 and the
  * lowering at scheduler.rs:428-548, with the activation fused. */
@@ -196,6 +206,10 @@ typedef struct spx_gemm_params {
 } spx_gemm_params;
 int spx_op_gemm(spx_graph* g, const float* a, const float* b, const float* bias,
                 const float* residual, float* c, const spx_gemm_params* p);
+/* spx_op_gemm with B also given pre-split (spx_weights_split). */
+int spx_op_gemm_split(spx_graph* g, const float* a, const float* b, const float* b_hi,
+                      const float* b_lo, const float* bias, const float* residual, float* c,
+                      const spx_gemm_params* p);
 
 /* Window pooling NHWC (max / sum / average), reduce_window semantics of
  * hlo_reduce_window_rank4.comp:25-49 and max_pool2d.comp:25-44.

@@ -108,6 +108,9 @@ _SIGS = {
     "spx_host_alloc_pinned": ([c_size_t, POINTER(c_void_p)], c_int),
     "spx_host_free_pinned": ([c_void_p], c_int),
     "spx_op_conv2d_nhwc": ([c_void_p] + [c_void_p] * 5 + [POINTER(ConvParams)], c_int),
+    "spx_weights_split": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int64], c_int),
+    "spx_op_conv2d_nhwc_split": ([c_void_p] + [c_void_p] * 7 + [POINTER(ConvParams)], c_int),
+    "spx_op_gemm_split": ([c_void_p] + [c_void_p] * 7 + [POINTER(GemmParams)], c_int),
     "spx_op_depthwise_conv2d_nhwc": ([c_void_p] + [c_void_p] * 4 + [POINTER(DwParams)], c_int),
     "spx_op_gemm": ([c_void_p] + [c_void_p] * 5 + [POINTER(GemmParams)], c_int),
     "spx_op_pool2d_nhwc": ([c_void_p, c_void_p, c_void_p, POINTER(PoolParams)], c_int),

@@ -1,0 +1,207 @@
+// Direct (non-GEMM) kernels for the bandwidth-bound spatial convolutions of
+// the CNN graphs, NHWC:
+//
+//  * conv_smallk: dense conv whose reduction K = kh*kw*ic is small (the
+//    3x3x3 stem of MobileNetV2 / EfficientNet-Lite0, conv2d.comp:26-50 as an
+//    NHWC kernel).  Weights [K][oc] sit in shared memory and are read as
+//    warp broadcasts; one thread computes all oc outputs of one pixel and
+//    writes them as contiguous 16-byte stores.  Input bytes are read once
+//    from HBM (tap overlap is served by L1), outputs written once.
+//
+//  * dw_rows: depthwise conv (depthwise_conv2d.comp:27-49) with a vertical
+//    sliding window: a thread owns 4 channels of one output column and R
+//    consecutive output rows, keeps the kh x kw x 4 weights in registers, and
+//    reads each input row of its window once instead of kh times.  Channel
+//    groups are the fastest-varying thread index so a warp reads contiguous
+//    runs of the NHWC rows.  32-bit index arithmetic.
+#include "spx_internal.cuh"
+
+namespace spx {
+namespace {
+
+template <int OC>
+__global__ void __launch_bounds__(128) conv_smallk_kernel(
+    const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ bias,
+    const float* __restrict__ res, float* __restrict__ y, int n, int ih, int iw, int ic, int oh,
+    int ow, int kh, int kw, int sh, int sw, int pt, int pl, int dh, int dw, int act,
+    int w_layout) {
+  extern __shared__ float ws[];  // [K][OC] then bias[OC]
+  const int K = kh * kw * ic;
+  for (int i = threadIdx.x; i < K * OC; i += blockDim.x) {
+    const int k = i / OC, o = i % OC;
+    // OHWI: w[o][k]; HWIO: w[k][o]  (k = (ky*kw + kx)*ic + ci in both)
+    ws[i] = w_layout == SPX_WEIGHT_OHWI ? w[(size_t)o * K + k] : w[(size_t)k * OC + o];
+  }
+  for (int o = threadIdx.x; o < OC; o += blockDim.x) ws[K * OC + o] = bias ? bias[o] : 0.0f;
+  __syncthreads();
+  const int total = n * oh * ow;
+  for (int pix = blockIdx.x * blockDim.x + threadIdx.x; pix < total; pix += gridDim.x * blockDim.x) {
+    const int ox = pix % ow;
+    const int t = pix / ow;
+    const int oy = t % oh;
+    const int img = t / oh;
+    float acc[OC];
+#pragma unroll
+    for (int o = 0; o < OC; ++o) acc[o] = ws[K * OC + o];
+    const float* xi = x + (size_t)img * ih * iw * ic;
+    for (int ky = 0; ky < kh; ++ky) {
+      const int iy = oy * sh + ky * dh - pt;
+      if (iy < 0 || iy >= ih) continue;
+      for (int kx = 0; kx < kw; ++kx) {
+        const int ix = ox * sw + kx * dw - pl;
+        if (ix < 0 || ix >= iw) continue;
+        const float* xp = xi + ((size_t)iy * iw + ix) * ic;
+        const float* wp = ws + ((ky * kw + kx) * ic) * OC;
+        for (int ci = 0; ci < ic; ++ci) {
+          const float v = __ldg(xp + ci);
+#pragma unroll
+          for (int o = 0; o < OC; ++o) acc[o] = fmaf(v, wp[ci * OC + o], acc[o]);
+        }
+      }
+    }
+    float* yp = y + (size_t)pix * OC;
+    const float* rp = res ? res + (size_t)pix * OC : nullptr;
+#pragma unroll
+    for (int o = 0; o < OC; o += 4) {
+      float4 v = make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
+      if (rp) {
+        const float4 r = *reinterpret_cast<const float4*>(rp + o);
+        v.x += r.x; v.y += r.y; v.z += r.z; v.w += r.w;
+      }
+      v.x = apply_act(act, v.x); v.y = apply_act(act, v.y);
+      v.z = apply_act(act, v.z); v.w = apply_act(act, v.w);
+      *reinterpret_cast<float4*>(yp + o) = v;
+    }
+  }
+}
+
+template <int KH, int KW, int SH, int R>
+__global__ void __launch_bounds__(256, 2) dw_rows_kernel(
+    const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ bias,
+    float* __restrict__ y, int n, int ih, int iw, int c, int oh, int ow, int sw, int pt, int pl,
+    int act, int row_blocks) {
+  const int cv = c >> 2;
+  const int total = n * row_blocks * ow * cv;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+    const int cg = idx % cv;
+    int t = idx / cv;
+    const int ox = t % ow;
+    t /= ow;
+    const int rb = t % row_blocks;
+    const int img = t / row_blocks;
+    const int ch = cg * 4;
+    float4 wr[KH][KW];
+#pragma unroll
+    for (int ky = 0; ky < KH; ++ky)
+#pragma unroll
+      for (int kx = 0; kx < KW; ++kx)
+        wr[ky][kx] = __ldg(reinterpret_cast<const float4*>(w + (ky * KW + kx) * c + ch));
+    const float4 b = bias ? __ldg(reinterpret_cast<const float4*>(bias + ch))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = b;
+    const int oy0 = rb * R;
+    const int iy0 = oy0 * SH - pt;
+    const float* xi = x + (size_t)img * ih * iw * c + ch;
+    // Input rows iy0 .. iy0 + (R-1)*SH + KH-1 feed output rows oy0 .. oy0+R-1.
+#pragma unroll
+    for (int j = 0; j < (R - 1) * SH + KH; ++j) {
+      const int iy = iy0 + j;
+      if (iy < 0 || iy >= ih) continue;
+      float4 row[KW];
+#pragma unroll
+      for (int kx = 0; kx < KW; ++kx) {
+        const int ix = ox * sw + kx - pl;
+        row[kx] = (ix >= 0 && ix < iw)
+                      ? __ldg(reinterpret_cast<const float4*>(xi + ((size_t)iy * iw + ix) * c))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int ky = j - r * SH;
+        if (ky < 0 || ky >= KH) continue;
+#pragma unroll
+        for (int kx = 0; kx < KW; ++kx) {
+          acc[r].x = fmaf(row[kx].x, wr[ky][kx].x, acc[r].x);
+          acc[r].y = fmaf(row[kx].y, wr[ky][kx].y, acc[r].y);
+          acc[r].z = fmaf(row[kx].z, wr[ky][kx].z, acc[r].z);
+          acc[r].w = fmaf(row[kx].w, wr[ky][kx].w, acc[r].w);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int oy = oy0 + r;
+      if (oy >= oh) break;
+      float4 v = acc[r];
+      v.x = apply_act(act, v.x); v.y = apply_act(act, v.y);
+      v.z = apply_act(act, v.z); v.w = apply_act(act, v.w);
+      *reinterpret_cast<float4*>(y + (((size_t)img * oh + oy) * ow + ox) * c + ch) = v;
+    }
+  }
+}
+
+bool al16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+template <int KH, int KW, int SH>
+int dw_dispatch_r(cudaStream_t s, const float* x, const float* w, const float* b, float* y,
+                  const spx_dw_params* p) {
+  constexpr int R = SH == 1 ? 4 : 2;
+  const int row_blocks = (p->oh + R - 1) / R;
+  const int64_t total = (int64_t)p->n * row_blocks * p->ow * (p->c / 4);
+  dw_rows_kernel<KH, KW, SH, R><<<grid_for(total, 256, 16), 256, 0, s>>>(
+      x, w, b, y, p->n, p->ih, p->iw, p->c, p->oh, p->ow, p->stride_w, p->pad_top, p->pad_left,
+      p->activation, row_blocks);
+  return SPX_OK;
+}
+
+}  // namespace
+
+// Returns SPX_OK after launching, or -1 when the shape is not covered (the
+// caller then uses the generic kernel).
+int try_dw_rows(cudaStream_t s, int64_t* cnt, const float* x, const float* w, const float* b,
+                float* y, const spx_dw_params* p) {
+  const bool dil1 = (p->dilation_h <= 1) && (p->dilation_w <= 1);
+  if (!dil1 || p->c % 4 || !al16(x) || !al16(w) || !al16(y) || (b && !al16(b))) return -1;
+  if ((int64_t)p->n * p->ih * p->iw * p->c >= INT32_MAX ||
+      (int64_t)p->n * p->oh * p->ow * p->c >= INT32_MAX)
+    return -1;
+  int rc = -1;
+  if (p->kh == 3 && p->kw == 3 && p->stride_h == 1) rc = dw_dispatch_r<3, 3, 1>(s, x, w, b, y, p);
+  else if (p->kh == 3 && p->kw == 3 && p->stride_h == 2) rc = dw_dispatch_r<3, 3, 2>(s, x, w, b, y, p);
+  else if (p->kh == 5 && p->kw == 5 && p->stride_h == 1) rc = dw_dispatch_r<5, 5, 1>(s, x, w, b, y, p);
+  else if (p->kh == 5 && p->kw == 5 && p->stride_h == 2) rc = dw_dispatch_r<5, 5, 2>(s, x, w, b, y, p);
+  if (rc < 0) return -1;
+  return after_launch(cnt, "depthwise_rows");
+}
+
+int try_conv_smallk(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
+                    const float* bias, const float* res, float* y, const spx_conv_params* p) {
+  const int K = p->kh * p->kw * p->ic;
+  if (K > 64 || (p->oc != 8 && p->oc != 16 && p->oc != 32 && p->oc != 64)) return -1;
+  if (!al16(y) || (res && !al16(res))) return -1;
+  if ((int64_t)p->n * p->oh * p->ow >= INT32_MAX / 64 ||
+      (int64_t)p->n * p->ih * p->iw * p->ic >= INT32_MAX)
+    return -1;
+  const int total = p->n * p->oh * p->ow;
+  const size_t smem = ((size_t)K * p->oc + p->oc) * sizeof(float);
+  const int grid = grid_for(total, 128, 16);
+  const int dh = p->dilation_h > 0 ? p->dilation_h : 1, dw = p->dilation_w > 0 ? p->dilation_w : 1;
+#define SPX_SMALLK(OCV)                                                                        \
+  conv_smallk_kernel<OCV><<<grid, 128, smem, s>>>(x, w, bias, res, y, p->n, p->ih, p->iw,      \
+                                                  p->ic, p->oh, p->ow, p->kh, p->kw,           \
+                                                  p->stride_h, p->stride_w, p->pad_top,        \
+                                                  p->pad_left, dh, dw, p->activation,          \
+                                                  p->weight_layout)
+  switch (p->oc) {
+    case 8: SPX_SMALLK(8); break;
+    case 16: SPX_SMALLK(16); break;
+    case 32: SPX_SMALLK(32); break;
+    default: SPX_SMALLK(64); break;
+  }
+#undef SPX_SMALLK
+  return after_launch(cnt, "conv_smallk");
+}
+
+}  // namespace spx

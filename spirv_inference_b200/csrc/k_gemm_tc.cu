@@ -6,25 +6,34 @@
 // weights (A = x as [M = n*h*w][K = ic], B = w as [N = oc][K]), and
 // fully_connected / linear layers (B = W[out][in]).
 //
-// Precision: every fp32 operand x is split on chip into hi = rna_tf32(x) and
-// lo = rna_tf32(x - hi); each k-step issues hi*hi + hi*lo + lo*hi into an fp32
-// TMEM accumulator.  Relative error per product is ~2^-21, the neglected
-// lo*lo term ~2^-22: fp32-level results, as the reference's fp32 kernels
-// (kernels/conv2d/glsl/conv2d.comp, fully_connected.comp) require.
+// Precision: every fp32 operand x is split into hi = rna_tf32(x) and
+// lo = rna_tf32(x - hi) (activations on chip, weights either on chip or once
+// at load); each k-step issues lo*hi + hi*lo + hi*hi into an fp32 TMEM
+// accumulator.  Relative error per product is ~2^-21 (the neglected lo*lo
+// term ~2^-22).  The tensor core's accumulate rounds toward zero, so the
+// remaining error grows with the K/8 accumulation steps: about 1e-5 of the
+// running-sum magnitude at K = 1000 (the kernel tests bound it by K).
 //
-// Structure (one CTA per SM, persistent over output tiles, 10 warps):
-//   warp 8      TMA producer: A tile 128 x 32 and B tile BN x 32 per k-block
-//               into an S-stage ring, 128-byte swizzle, mbarrier transaction
-//               counts.
-//   warps 4-7   converters: split A and B of a landed stage in place (hi) and
-//               into a second buffer (lo), then fence.proxy.async + arrive.
-//   warp 9      TMEM owner and MMA issuer (one thread): 12 UMMAs per k-block
-//               (4 k-steps x 3 products), commit frees the stage; a commit at
+// Structure: one CTA per SM, persistent over output tiles (n-tile fastest so
+// consecutive tiles share the A tile in L2), 18 warps:
+//   warp 16     TMA producer: per k-block an A tile 128 x 32 and either a B
+//               tile BN x 32 or, with pre-split weights, its hi and lo tiles,
+//               into an S-stage ring (128-byte swizzle, mbarrier tx counts).
+//   warps 8-15  converters: split A (and B unless pre-split) of a landed
+//               stage, hi in place and lo into a second buffer, then
+//               fence.proxy.async + arrive.
+//   warp 17     TMEM owner and MMA issuer (one thread): 12 UMMAs per k-block
+//               (4 k-steps x 3 products); a commit frees the stage; a commit at
 //               the end of a tile hands one of two TMEM accumulators
 //               (2 x BN columns) to the epilogue.
-//   warps 0-3   epilogue: tcgen05.ld 32 rows x 16 columns per warp, alpha,
-//               bias, residual, activation, store; then release the
-//               accumulator, so tile i's epilogue overlaps tile i+1's k-loop.
+//   warps 0-7   epilogue, 32 columns at a time (two warps per TMEM lane
+//               quarter, alternating chunks): each warp loads its 32 TMEM
+//               lanes x 32 columns, transposes them through a private padded
+//               smem tile (warp-synchronous, no block barrier) and then
+//               applies bias, residual and activation while reading and
+//               writing whole 128-byte row segments of C, so stores are
+//               coalesced.  Releasing the accumulator lets tile i's epilogue
+//               overlap tile i+1's k-loop.
 // Every wait is bounded (globaltimer); on timeout the CTA raises an abort flag,
 // records a device status, drains its own in-flight copies and MMAs, frees
 // TMEM and exits.  The host reads the status at the next sync.
@@ -42,8 +51,15 @@ namespace {
 
 constexpr int kBM = 128;         // UMMA M: output rows per tile
 constexpr int kBK = 32;          // fp32 elements per k-block (one 128-byte row)
-constexpr int kThreads = 320;    // 10 warps
-constexpr int kMaxStages = 6;
+constexpr int kEpiWarps = 8;     // two per TMEM lane quarter
+constexpr int kConvWarps = 8;
+constexpr int kConvThreads = kConvWarps * 32;
+constexpr int kProducerWarp = kEpiWarps + kConvWarps;
+constexpr int kMmaWarp = kProducerWarp + 1;
+constexpr int kThreads = (kMmaWarp + 1) * 32;  // 18 warps
+constexpr int kMaxStages = 8;
+constexpr int kEpiStride = 36;   // floats per row of a warp's transpose tile
+constexpr uint32_t kEpiBytes = kEpiWarps * 32 * kEpiStride * 4;  // 32 rows per warp
 constexpr uint32_t kATileBytes = kBM * kBK * 4;       // 16 KB
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 constexpr unsigned long long kDrainNs = 200000000ull;     // 0.2 s drain on abort
@@ -51,6 +67,7 @@ constexpr unsigned long long kDrainNs = 200000000ull;     // 0.2 s drain on abor
 struct TcArgs {
   int M, N, K, BN, n_tiles, m_tiles, k_blocks, stages;
   uint32_t idesc, tmem_cols, stage_bytes, b_bytes;
+  int presplit;  // B arrives as hi and lo tiles: converters split A only
   const float* bias;
   const float* res;
   float* c;
@@ -92,12 +109,20 @@ __device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
 // Bounded wait on the phase with the given parity.  Returns false when the
 // CTA is aborting (another role timed out) or this wait itself timed out.
 __device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag,
-                                         unsigned long long limit = kTimeoutNs) {
+                                         unsigned long long limit = kTimeoutNs,
+                                         int max_sleep_ns = 128) {
   if (bar_try(b, parity)) return true;
   const unsigned long long t0 = gtimer();
+  int sleep_ns = 16;
   for (;;) {
+    // Back off between polls so waiting warps leave issue slots and the
+    // shared-memory pipe to the warps doing work.
+    if (max_sleep_ns > 0) {
+      __nanosleep(sleep_ns);
+      sleep_ns = sleep_ns * 2 < max_sleep_ns ? sleep_ns * 2 : max_sleep_ns;
+    }
 #pragma unroll 1
-    for (int i = 0; i < 64; ++i)
+    for (int i = 0; i < 4; ++i)
       if (bar_try(b, parity)) return true;
     if (*abort_flag) return false;
     if (gtimer() - t0 > limit) {
@@ -150,48 +175,57 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 __device__ __forceinline__ float tf32_rna(float x) {
   uint32_t h;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
   return __uint_as_float(h);
 }
 
-// In-place hi / separate lo split of n16 16-byte vectors.
+// In-place hi / separate lo split of n16 16-byte vectors.  For finite x,
+// lo = x - hi is exact; for inf / nan the lo term is zeroed so the hi*hi
+// product carries the special value.
+__device__ __forceinline__ float split_lo(float x, float h) {
+  const float r = x - h;
+  return r == r ? tf32_rna(r) : 0.0f;
+}
 __device__ __forceinline__ void split_buffer(float4* hi, float4* lo, int n16, int tid, int nthr) {
+#pragma unroll 4
   for (int i = tid; i < n16; i += nthr) {
-    float4 v = hi[i];
-    float4 h = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
-    float4 l = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
-    l.x = isfinite(l.x) ? tf32_rna(l.x) : 0.0f;
-    l.y = isfinite(l.y) ? tf32_rna(l.y) : 0.0f;
-    l.z = isfinite(l.z) ? tf32_rna(l.z) : 0.0f;
-    l.w = isfinite(l.w) ? tf32_rna(l.w) : 0.0f;
+    const float4 v = hi[i];
+    const float4 h = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+    lo[i] = make_float4(split_lo(v.x, h.x), split_lo(v.y, h.y), split_lo(v.z, h.z),
+                        split_lo(v.w, h.w));
     hi[i] = h;
-    lo[i] = l;
   }
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
-                   const __grid_constant__ CUtensorMap tmB, const TcArgs p) {
+                   const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmBlo, const TcArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int S = p.stages;
-  uint64_t* full = (uint64_t*)(smem + (size_t)S * p.stage_bytes);
+  float* epi = (float*)(smem + (size_t)S * p.stage_bytes);  // kEpiWarps x 32 x kEpiStride
+  uint64_t* full = (uint64_t*)((uint8_t*)epi + kEpiBytes);
   uint64_t* conv = full + kMaxStages;
   uint64_t* empty = conv + kMaxStages;
   uint64_t* tfull = empty + kMaxStages;
@@ -204,18 +238,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       bar_init(&full[s], 1);
-      bar_init(&conv[s], 128);
+      bar_init(&conv[s], kConvThreads);
       bar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       bar_init(&tfull[a], 1);
-      bar_init(&tempty[a], 128);
+      bar_init(&tempty[a], kEpiWarps * 32);
     }
     bar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      su32(tmem_slot)),
                  "r"(p.tmem_cols));
@@ -227,21 +261,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const int total = p.m_tiles * p.n_tiles;
 
-  if (warp == 8) {
+  if (warp == kProducerWarp) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
       int s = 0;
       uint32_t ph = 0, armed = 0, armed_par = 0;
+      const uint32_t tx = kATileBytes + p.b_bytes * (p.presplit ? 2u : 1u);
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         const int mt = t / p.n_tiles, nt = t % p.n_tiles;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!bar_wait(&empty[s], ph ^ 1, abort_flag)) goto producer_done;
+          if (!bar_wait(&empty[s], ph ^ 1, abort_flag, kTimeoutNs, 64)) goto producer_done;
           uint8_t* st = smem + (size_t)s * p.stage_bytes;
-          bar_expect_tx(&full[s], kATileBytes + p.b_bytes);
+          bar_expect_tx(&full[s], tx);
           tma_load_2d(st, &tmA, &full[s], kb * kBK, mt * kBM);
           tma_load_2d(st + 2 * kATileBytes, &tmB, &full[s], kb * kBK, nt * p.BN);
+          if (p.presplit)
+            tma_load_2d(st + 2 * kATileBytes + p.b_bytes, &tmBlo, &full[s], kb * kBK, nt * p.BN);
           armed |= 1u << s;
           armed_par = (armed_par & ~(1u << s)) | (ph << s);
           if (++s == S) {
@@ -259,18 +294,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       int s = 0, acc = 0;
       uint32_t ph = 0, aph = 0;
       bool issued = false;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
-        if (!bar_wait(&tempty[acc], aph ^ 1, abort_flag)) goto mma_done;
+        if (!bar_wait(&tempty[acc], aph ^ 1, abort_flag, kTimeoutNs, 64)) goto mma_done;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(acc * p.BN);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!bar_wait(&conv[s], ph, abort_flag)) goto mma_done;
+          if (!bar_wait(&conv[s], ph, abort_flag, kTimeoutNs, 64)) goto mma_done;
           tc_fence_after();
           const uint32_t a_hi = su32(smem + (size_t)s * p.stage_bytes);
           const uint32_t a_lo = a_hi + kATileBytes;
@@ -303,18 +338,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         bar_wait(drain, 0, &never, kDrainNs);
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp >= kEpiWarps) {
     // ---------------- converters (hi/lo split) ----------------
-    const int ct = threadIdx.x - 128;
+    const int ct = threadIdx.x - kEpiWarps * 32;
     int s = 0;
     uint32_t ph = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       for (int kb = 0; kb < p.k_blocks; ++kb) {
-        if (!bar_wait(&full[s], ph, abort_flag)) goto conv_done;
+        if (!bar_wait(&full[s], ph, abort_flag, kTimeoutNs, 256)) goto conv_done;
         uint8_t* st = smem + (size_t)s * p.stage_bytes;
-        split_buffer((float4*)st, (float4*)(st + kATileBytes), kATileBytes / 16, ct, 128);
-        split_buffer((float4*)(st + 2 * kATileBytes),
-                     (float4*)(st + 2 * kATileBytes + p.b_bytes), p.b_bytes / 16, ct, 128);
+        split_buffer((float4*)st, (float4*)(st + kATileBytes), kATileBytes / 16, ct,
+                     kConvThreads);
+        if (!p.presplit)
+          split_buffer((float4*)(st + 2 * kATileBytes),
+                       (float4*)(st + 2 * kATileBytes + p.b_bytes), p.b_bytes / 16, ct,
+                       kConvThreads);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         bar_arrive(&conv[s]);
         if (++s == S) {
@@ -325,67 +363,92 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   conv_done:;
   } else {
-    // ---------------- epilogue ----------------
+    // ---------------- epilogue (warps 0 .. kEpiWarps-1) ----------------
+    // Warp w reads TMEM lane quarter w % 4 and takes every
+    // (kEpiWarps / 4)-th 32-column chunk starting at chunk w / 4.
     int acc = 0;
     uint32_t aph = 0;
-    const int row = threadIdx.x;  // 0..127 == TMEM lane
+    float* tile = epi + warp * 32 * kEpiStride;  // this warp's 32 x 32 transpose tile
+    const int sub_r = lane >> 3;                 // 0..3: row within a group of 4
+    const int sub_c = (lane & 7) * 4;            // first of 4 columns
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const int mt = t / p.n_tiles, nt = t % p.n_tiles;
-      if (!bar_wait(&tfull[acc], aph, abort_flag)) goto epi_done;
+      // Uniform per warp: every lane waits on the same barrier phase.
+      const bool ok = bar_wait(&tfull[acc], aph, abort_flag, kTimeoutNs, 128);
+      if (__any_sync(0xffffffffu, !ok)) break;
       tc_fence_after();
-      {
-        const int64_t m = (int64_t)mt * kBM + row;
-        const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * p.BN);
-        float* crow = p.c + m * p.ldc;
-        const float* rrow = p.res ? p.res + m * p.ldc : nullptr;
-        for (int c0 = 0; c0 < p.BN; c0 += 16) {
-          float v[16];
-          tmem_ld16(tbase + (uint32_t)c0, v);
-          const int n0 = nt * p.BN + c0;
-          if (m >= p.M || n0 >= p.N) continue;
-          if (p.vec4 && n0 + 16 <= p.N) {
+      const int quarter = warp & 3;
+      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.BN);
+      const int64_t row0 = (int64_t)mt * kBM + quarter * 32;
+      for (int c0 = (warp >> 2) * 32; c0 < p.BN; c0 += 32 * (kEpiWarps / 4)) {
+        float v[32];
+        tmem_ld32(tbase + (uint32_t)c0, v);  // lane = row, 32 consecutive columns
+        float4* trow = reinterpret_cast<float4*>(tile + lane * kEpiStride);
 #pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              float4 o;
-              float* op = &o.x;
-              float4 bv = p.bias ? *reinterpret_cast<const float4*>(p.bias + n0 + j)
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-              float4 rv = rrow ? *reinterpret_cast<const float4*>(rrow + n0 + j)
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
-              const float* bp = &bv.x;
-              const float* rp = &rv.x;
+        for (int q = 0; q < 8; ++q)
+          trow[q] = make_float4(v[4 * q] * p.alpha, v[4 * q + 1] * p.alpha,
+                                v[4 * q + 2] * p.alpha, v[4 * q + 3] * p.alpha);
+        __syncwarp();
+        const int n = nt * p.BN + c0 + sub_c;
+        float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (p.bias) {
+          float* bp = &b4.x;
+          if (p.vec4 && n + 3 < p.N) b4 = __ldg(reinterpret_cast<const float4*>(p.bias + n));
+          else
+            for (int e = 0; e < 4; ++e) bp[e] = n + e < p.N ? p.bias[n + e] : 0.0f;
+        }
 #pragma unroll
-              for (int q = 0; q < 4; ++q) op[q] = apply_act(p.act, v[j + q] * p.alpha + bp[q] + rp[q]);
-              *reinterpret_cast<float4*>(crow + n0 + j) = o;
-            }
+        for (int i = 0; i < 8; ++i) {
+          const int rr = i * 4 + sub_r;
+          const int64_t m = row0 + rr;
+          if (m >= p.M || n >= p.N) continue;
+          float4 o = *reinterpret_cast<const float4*>(tile + rr * kEpiStride + sub_c);
+          float* op = &o.x;
+          const float* bp = &b4.x;
+          float* crow = p.c + m * p.ldc;
+          if (p.vec4 && n + 3 < p.N) {
+            float4 r4 = p.res ? *reinterpret_cast<const float4*>(p.res + m * p.ldc + n)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float* rp = &r4.x;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) op[e] = apply_act(p.act, op[e] + bp[e] + rp[e]);
+            *reinterpret_cast<float4*>(crow + n) = o;
           } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int n = n0 + j;
-              if (n < p.N) {
-                float x = v[j] * p.alpha;
-                if (p.bias) x += p.bias[n];
-                if (rrow) x += rrow[n];
-                crow[n] = apply_act(p.act, x);
+            for (int e = 0; e < 4; ++e)
+              if (n + e < p.N) {
+                float x = op[e] + bp[e];
+                if (p.res) x += p.res[m * p.ldc + n + e];
+                crow[n + e] = apply_act(p.act, x);
               }
-            }
           }
         }
+        __syncwarp();
       }
       tc_fence_before();
       bar_arrive(&tempty[acc]);
       acc ^= 1;
       if (!acc) aph ^= 1;
     }
-  epi_done:;
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(p.tmem_cols));
+  }
+}
+
+// Pre-splits weights once at load: hi = rna_tf32(w), lo = rna_tf32(w - hi).
+__global__ void weights_split_kernel(const float* __restrict__ w, float* __restrict__ hi,
+                                     float* __restrict__ lo, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float x = w[i];
+    const float h = tf32_rna(x);
+    hi[i] = h;
+    lo[i] = split_lo(x, h);
   }
 }
 
@@ -447,20 +510,28 @@ bool gemm_tc_eligible(const float* a, int64_t lda, const float* b, int64_t ldb, 
 }
 
 int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, const float* b,
-                   int64_t ldb, int M, int N, int K, const float* bias, const float* res, float* c,
-                   int64_t ldc, float alpha, int act) {
+                   const float* b_lo, int64_t ldb, int M, int N, int K, const float* bias,
+                   const float* res, float* c, int64_t ldc, float alpha, int act) {
   TcArgs p = {};
   p.M = M;
   p.N = N;
   p.K = K;
-  const int nt = (N + 255) / 256;
-  p.BN = ((N + nt - 1) / nt + 15) / 16 * 16;
-  p.n_tiles = (N + p.BN - 1) / p.BN;
+  p.presplit = b_lo != nullptr;
+  // N tile: a multiple of 32 (the epilogue's chunk), at most 256 (UMMA N),
+  // halved while there are fewer than two tiles per SM.
+  const int nt0 = (N + 255) / 256;
+  p.BN = ((N + nt0 - 1) / nt0 + 31) / 32 * 32;
   p.m_tiles = (M + kBM - 1) / kBM;
+  while (p.BN > 32 && (int64_t)p.m_tiles * ((N + p.BN - 1) / p.BN) < 2 * sm_count())
+    p.BN = (p.BN / 2 + 31) / 32 * 32;
+  // At least two pipeline stages must fit next to the epilogue tiles.
+  const int budget = 227 * 1024 - 1024 - (int)kEpiBytes - 512;
+  while (p.BN > 32 && budget / (int)(2 * kATileBytes + 2 * (uint32_t)p.BN * kBK * 4) < 2)
+    p.BN = (p.BN / 2 + 31) / 32 * 32;
+  p.n_tiles = (N + p.BN - 1) / p.BN;
   p.k_blocks = (K + kBK - 1) / kBK;
   p.b_bytes = (uint32_t)p.BN * kBK * 4;
   p.stage_bytes = 2 * kATileBytes + 2 * p.b_bytes;
-  const int budget = 227 * 1024 - 1024 - 256;
   p.stages = budget / (int)p.stage_bytes;
   if (p.stages > kMaxStages) p.stages = kMaxStages;
   if (p.stages < 2) return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_tc: tile does not fit");
@@ -477,13 +548,15 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   p.ldc = ldc;
   p.alpha = alpha;
   p.act = act;
-  p.vec4 = (ldc % 4 == 0) && (((uintptr_t)c & 15) == 0) &&
-           (!res || ((uintptr_t)res & 15) == 0) && (!bias || ((uintptr_t)bias & 15) == 0);
-  CUtensorMap ma, mb;
+  auto al16 = [](const void* q) { return ((uintptr_t)q & 15) == 0; };
+  p.vec4 = (ldc % 4 == 0) && al16(c) && (!res || al16(res)) && (!bias || al16(bias));
+  CUtensorMap ma, mb, mblo;
   int rc;
   if ((rc = make_map(&ma, a, M, K, lda, kBM))) return rc;
   if ((rc = make_map(&mb, b, N, K, ldb, p.BN))) return rc;
-  const size_t smem = 1024 + (size_t)p.stages * p.stage_bytes + 256;
+  mblo = mb;
+  if (p.presplit && (rc = make_map(&mblo, b_lo, N, K, ldb, p.BN))) return rc;
+  const size_t smem = 1024 + (size_t)p.stages * p.stage_bytes + kEpiBytes + 512;
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
@@ -493,8 +566,15 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   if (attr_err != cudaSuccess) return check_cuda(attr_err, "gemm_tc: smem attribute");
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  gemm_tc_kernel<<<grid, kThreads, smem, s>>>(ma, mb, p);
+  gemm_tc_kernel<<<grid, kThreads, smem, s>>>(ma, mb, mblo, p);
   return after_launch(cnt, "gemm_tc");
+}
+
+int launch_weights_split(cudaStream_t s, int64_t* cnt, const float* w, float* hi, float* lo,
+                         int64_t n) {
+  if (n <= 0) return n == 0 ? SPX_OK : fail(SPX_ERR_INVALID_ARGUMENT, "weights_split: n < 0");
+  weights_split_kernel<<<grid_for(n, 256), 256, 0, s>>>(w, hi, lo, n);
+  return after_launch(cnt, "weights_split");
 }
 
 int tc_take_status() {

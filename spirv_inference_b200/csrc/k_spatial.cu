@@ -342,6 +342,10 @@ int launch_dw_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
   if (p.n <= 0 || p.c <= 0 || p.oh <= 0 || p.ow <= 0 || p.kh <= 0 || p.kw <= 0 || p.sh <= 0 ||
       p.sw <= 0 || p.ih <= 0 || p.iw <= 0)
     return fail(SPX_ERR_INVALID_ARGUMENT, "depthwise: bad shape");
+  {
+    int rc = try_dw_rows(s, cnt, x, w, bias, y, q);
+    if (rc != -1) return rc;
+  }
   int64_t pix = (int64_t)p.n * p.oh * p.ow;
   if (p.c % 4 == 0 && al16(x) && al16(w) && al16(y)) {
     int64_t total = pix * (p.c / 4);

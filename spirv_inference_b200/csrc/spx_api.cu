@@ -44,7 +44,8 @@ int g_gemm_path = 0;
 
 // ---- algorithm selection for dense contractions ---------------------------
 int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
-                     const float* bias, const float* res, float* y, const spx_conv_params* p) {
+                     const float* w_hi, const float* w_lo, const float* bias, const float* res,
+                     float* y, const spx_conv_params* p) {
   if (p->n <= 0 || p->ih <= 0 || p->iw <= 0 || p->ic <= 0 || p->oc <= 0 || p->oh <= 0 ||
       p->ow <= 0 || p->kh <= 0 || p->kw <= 0 || p->stride_h <= 0 || p->stride_w <= 0)
     return fail(SPX_ERR_INVALID_ARGUMENT, "conv2d_nhwc: non-positive shape parameter");
@@ -56,24 +57,35 @@ int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* 
                          p->pad_top == 0 && p->pad_left == 0 && p->oh == p->ih && p->ow == p->iw;
   if (g_gemm_path != 1 && pointwise && p->weight_layout == SPX_WEIGHT_OHWI) {
     const int M = p->n * p->oh * p->ow;
-    if (gemm_tc_eligible(x, p->ic, w, p->ic, M, p->oc, p->ic, y, p->oc))
-      return launch_gemm_tc(s, cnt, x, p->ic, w, p->ic, M, p->oc, p->ic, bias, res, y, p->oc,
-                            1.0f, p->activation);
+    const bool split = w_hi && w_lo;
+    const float* wb = split ? w_hi : w;
+    if (gemm_tc_eligible(x, p->ic, wb, p->ic, M, p->oc, p->ic, y, p->oc) &&
+        (!split || ((uintptr_t)w_lo & 15) == 0))
+      return launch_gemm_tc(s, cnt, x, p->ic, wb, split ? w_lo : nullptr, p->ic, M, p->oc, p->ic,
+                            bias, res, y, p->oc, 1.0f, p->activation);
   }
   if (g_gemm_path == 2)
     return fail(SPX_ERR_UNSUPPORTED, "conv2d_nhwc: shape not eligible for the tensor-core path");
+  if (!pointwise) {
+    int rc = try_conv_smallk(s, cnt, x, w, bias, res, y, p);
+    if (rc != -1) return rc;
+  }
   return launch_conv_simt(s, cnt, x, w, bias, res, y, p);
 }
 
-int launch_gemm(cudaStream_t s, int64_t* cnt, const float* a, const float* b, const float* bias,
-                const float* res, float* c, const spx_gemm_params* p) {
+int launch_gemm(cudaStream_t s, int64_t* cnt, const float* a, const float* b, const float* b_hi,
+                const float* b_lo, const float* bias, const float* res, float* c,
+                const spx_gemm_params* p) {
   if (p->batch <= 0 || p->m <= 0 || p->n <= 0 || p->k <= 0)
     return fail(SPX_ERR_INVALID_ARGUMENT, "gemm: non-positive extent");
   const bool single = p->batch == 1 && (p->batch_inner <= 1);
+  const bool split = b_hi && b_lo;
+  const float* bb = split ? b_hi : b;
   if (g_gemm_path != 1 && single && p->a_ks == 1 && p->b_ks == 1 &&
-      gemm_tc_eligible(a, p->a_ms, b, p->b_ns, p->m, p->n, p->k, c, p->c_ms))
-    return launch_gemm_tc(s, cnt, a, p->a_ms, b, p->b_ns, p->m, p->n, p->k, bias, res, c, p->c_ms,
-                          p->alpha, p->activation);
+      gemm_tc_eligible(a, p->a_ms, bb, p->b_ns, p->m, p->n, p->k, c, p->c_ms) &&
+      (!split || ((uintptr_t)b_lo & 15) == 0))
+    return launch_gemm_tc(s, cnt, a, p->a_ms, bb, split ? b_lo : nullptr, p->b_ns, p->m, p->n,
+                          p->k, bias, res, c, p->c_ms, p->alpha, p->activation);
   if (g_gemm_path == 2)
     return fail(SPX_ERR_UNSUPPORTED, "gemm: operands not eligible for the tensor-core path");
   return launch_gemm_simt(s, cnt, a, b, bias, res, c, p);
@@ -249,7 +261,8 @@ int dispatch_compat(DeviceCache& c, const std::string& k, const float* in0, size
     if ((rc = launch_transpose4(s, cnt, in1, c.buf[4], t_w))) return rc;
     spx_conv_params p = {N, IH, IW, IC, OC, OH, OW, KH, KW, q[9], q[10], q[12], q[13], 1, 1,
                          SPX_WEIGHT_OHWI, SPX_ACT_NONE};
-    if ((rc = launch_conv_nhwc(s, cnt, c.buf[3], c.buf[4], in1 + w_el, nullptr, c.buf[5], &p)))
+    if ((rc = launch_conv_nhwc(s, cnt, c.buf[3], c.buf[4], nullptr, nullptr, in1 + w_el, nullptr,
+                               c.buf[5], &p)))
       return rc;
     return launch_transpose4(s, cnt, c.buf[5], out, t_out);
   }
@@ -307,7 +320,7 @@ int dispatch_compat(DeviceCache& c, const std::string& k, const float* in0, size
     spx_gemm_params p = {};
     p.batch = 1; p.m = B; p.n = O; p.k = I; p.batch_inner = 1; p.b_inner_div = 1;
     p.a_ms = I; p.a_ks = 1; p.b_ks = 1; p.b_ns = I; p.c_ms = O; p.alpha = 1.0f;
-    return launch_gemm(s, cnt, in0, in1, in1 + (int64_t)O * I, nullptr, out, &p);
+    return launch_gemm(s, cnt, in0, in1, nullptr, nullptr, in1 + (int64_t)O * I, nullptr, out, &p);
   }
   if (k == "softmax10" || k == "softmax1000") {
     int classes = k == "softmax10" ? 10 : q[0];
@@ -330,7 +343,7 @@ int dispatch_compat(DeviceCache& c, const std::string& k, const float* in0, size
       return rc;
     spx_conv_params p = {q[0], q[1], q[2], q[3], q[6], q[7], q[8], q[4], q[5], q[9], q[10],
                          q[11], q[12], 1, 1, SPX_WEIGHT_HWIO, SPX_ACT_NONE};
-    return launch_conv_nhwc(s, cnt, in0, in1, nullptr, nullptr, out, &p);
+    return launch_conv_nhwc(s, cnt, in0, in1, nullptr, nullptr, nullptr, nullptr, out, &p);
   }
   if (k == "hlo_dot_rank2" || k == "hlo_dot_batched") {
     bool batched = k == "hlo_dot_batched";
@@ -347,7 +360,7 @@ int dispatch_compat(DeviceCache& c, const std::string& k, const float* in0, size
     p.a_bs = (int64_t)M * K; p.a_ms = K; p.a_ks = 1;
     p.b_bs = (int64_t)K * N; p.b_ks = N; p.b_ns = 1;
     p.c_bs = (int64_t)M * N; p.c_ms = N; p.alpha = 1.0f;
-    return launch_gemm(s, cnt, in0, in1, nullptr, nullptr, out, &p);
+    return launch_gemm(s, cnt, in0, in1, nullptr, nullptr, nullptr, nullptr, out, &p);
   }
   if (k == "hlo_reduce_rank4") {
     int64_t in_el = (int64_t)q[1] * q[2] * q[3] * q[4];
@@ -666,7 +679,22 @@ int spx_op_conv2d_nhwc(spx_graph* g, const float* x, const float* w, const float
                        const float* residual, float* y, const spx_conv_params* p) {
   SPX_G(g);
   if (!x || !w || !y || !p) return fail(SPX_ERR_INVALID_ARGUMENT, "conv2d_nhwc: null argument");
-  return launch_conv_nhwc(g->stream, &g->launches, x, w, bias, residual, y, p);
+  return launch_conv_nhwc(g->stream, &g->launches, x, w, nullptr, nullptr, bias, residual, y, p);
+}
+
+int spx_op_conv2d_nhwc_split(spx_graph* g, const float* x, const float* w, const float* w_hi,
+                             const float* w_lo, const float* bias, const float* residual, float* y,
+                             const spx_conv_params* p) {
+  SPX_G(g);
+  if (!x || !w || !w_hi || !w_lo || !y || !p)
+    return fail(SPX_ERR_INVALID_ARGUMENT, "conv2d_nhwc_split: null argument");
+  return launch_conv_nhwc(g->stream, &g->launches, x, w, w_hi, w_lo, bias, residual, y, p);
+}
+
+int spx_weights_split(spx_graph* g, const float* w, float* w_hi, float* w_lo, int64_t n) {
+  SPX_G(g);
+  if (!w || !w_hi || !w_lo) return fail(SPX_ERR_INVALID_ARGUMENT, "weights_split: null argument");
+  return launch_weights_split(g->stream, &g->launches, w, w_hi, w_lo, n);
 }
 
 int spx_op_depthwise_conv2d_nhwc(spx_graph* g, const float* x, const float* w, const float* bias,
@@ -680,7 +708,16 @@ int spx_op_gemm(spx_graph* g, const float* a, const float* b, const float* bias,
                 const float* residual, float* c, const spx_gemm_params* p) {
   SPX_G(g);
   if (!a || !b || !c || !p) return fail(SPX_ERR_INVALID_ARGUMENT, "gemm: null argument");
-  return launch_gemm(g->stream, &g->launches, a, b, bias, residual, c, p);
+  return launch_gemm(g->stream, &g->launches, a, b, nullptr, nullptr, bias, residual, c, p);
+}
+
+int spx_op_gemm_split(spx_graph* g, const float* a, const float* b, const float* b_hi,
+                      const float* b_lo, const float* bias, const float* residual, float* c,
+                      const spx_gemm_params* p) {
+  SPX_G(g);
+  if (!a || !b || !b_hi || !b_lo || !c || !p)
+    return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_split: null argument");
+  return launch_gemm(g->stream, &g->launches, a, b, b_hi, b_lo, bias, residual, c, p);
 }
 
 int spx_op_pool2d_nhwc(spx_graph* g, const float* x, float* y, const spx_pool_params* p) {

@@ -65,10 +65,14 @@ int launch_unary(cudaStream_t s, int64_t* cnt, int op, const float* x, float* y,
                  float alpha);
 int launch_binary(cudaStream_t s, int64_t* cnt, int op, const float* a, const float* b,
                   float* y, const spx_bcast_params* p);
+// w_hi / w_lo (both or neither): the weights pre-split by launch_weights_split,
+// used when the tensor-core path runs; w itself feeds every other path.
 int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
-                     const float* bias, const float* res, float* y, const spx_conv_params* p);
-int launch_gemm(cudaStream_t s, int64_t* cnt, const float* a, const float* b,
-                const float* bias, const float* res, float* c, const spx_gemm_params* p);
+                     const float* w_hi, const float* w_lo, const float* bias, const float* res,
+                     float* y, const spx_conv_params* p);
+int launch_gemm(cudaStream_t s, int64_t* cnt, const float* a, const float* b, const float* b_hi,
+                const float* b_lo, const float* bias, const float* res, float* c,
+                const spx_gemm_params* p);
 int launch_dw_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
                    const float* bias, float* y, const spx_dw_params* p);
 int launch_pool_nhwc(cudaStream_t s, int64_t* cnt, const float* x, float* y,
@@ -103,12 +107,22 @@ int launch_gemm_simt(cudaStream_t s, int64_t* cnt, const float* a, const float* 
 int launch_conv_simt(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
                      const float* bias, const float* res, float* y, const spx_conv_params* p);
 
+// Direct kernels (k_direct.cu).  Return -1 when the shape is not covered.
+int try_dw_rows(cudaStream_t s, int64_t* cnt, const float* x, const float* w, const float* b,
+                float* y, const spx_dw_params* p);
+int try_conv_smallk(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
+                    const float* bias, const float* res, float* y, const spx_conv_params* p);
+
 // tcgen05 3xTF32 GEMM (k_gemm_tc.cu): both operands K-contiguous.
 bool gemm_tc_eligible(const float* a, int64_t lda, const float* b, int64_t ldb, int M, int N,
                       int K, const float* c, int64_t ldc);
+// b_lo != nullptr: B is given pre-split (b = tf32 hi terms, b_lo = lo terms,
+// from launch_weights_split); otherwise B is split on chip.
 int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, const float* b,
-                   int64_t ldb, int M, int N, int K, const float* bias, const float* res, float* c,
-                   int64_t ldc, float alpha, int act);
+                   const float* b_lo, int64_t ldb, int M, int N, int K, const float* bias,
+                   const float* res, float* c, int64_t ldc, float alpha, int act);
+int launch_weights_split(cudaStream_t s, int64_t* cnt, const float* w, float* hi, float* lo,
+                         int64_t n);
 // Returns and clears the device status of the tensor-core pipeline (0 = ok,
 // 1 = a pipeline wait timed out and the kernel aborted its tiles).
 int tc_take_status();

@@ -26,11 +26,13 @@ from .nets import Model
 
 class CnnExecutor:
     def __init__(self, model: Model, batch: int, device: int = 0, graph: Graph | None = None,
-                 fuse_residual: bool = True):
+                 fuse_residual: bool = True, presplit: bool = True):
         self.model = model
         self.batch = batch
         self.g = graph or Graph(device)
         self.fuse_residual = fuse_residual
+        self.presplit = presplit
+        self._splits: dict = {}
         self.w: dict[str, DeviceTensor] = {}
         for name, arr in model.weights.items():
             self.w[name] = self.g.tensor(arr)
@@ -40,6 +42,14 @@ class CnnExecutor:
         self._captured = False
 
     # -- planning ------------------------------------------------------------
+    def _split(self, wname: str):
+        """Tensor-core (3xTF32) hi / lo terms of a weight, made once at load."""
+        if not self.presplit:
+            return None
+        if wname not in self._splits:
+            self._splits[wname] = self.g.weights_split(self.w[wname])
+        return self._splits[wname]
+
     def _buf(self, name: str) -> DeviceTensor:
         if name not in self.t:
             self.t[name] = self.g.alloc((self.batch,) + tuple(self.model.shapes[name]))
@@ -83,10 +93,12 @@ class CnnExecutor:
                 ih, iw = x.shape[1], x.shape[2]
                 oh, ow = y.shape[1], y.shape[2]
                 pt, pl = same_padding_offsets(a["padding"], ih, iw, oh, ow, kh, kw, *a["stride"])
+                pointwise = (kh, kw) == (1, 1) and tuple(a["stride"]) == (1, 1)
+                split = self._split(op.inputs[1]) if pointwise else None
                 self._plan.append(("conv", dict(x=x, w=w, bias=self.w[op.inputs[2]], y=y,
                                                 stride=a["stride"], pad=(pt, pl),
                                                 activation=a.get("activation", 0),
-                                                residual=res)))
+                                                residual=res, w_split=split)))
             elif op.type == "DEPTHWISE_CONV_2D":
                 x, y = self._buf(op.inputs[0]), self._buf(op.output)
                 w = self.w[op.inputs[1]]
@@ -115,7 +127,8 @@ class CnnExecutor:
                 w = self.w[op.inputs[1]]
                 out, inp = w.shape
                 self._plan.append(("fc", dict(x=x, w=w, bias=self.w[op.inputs[2]], y=y, m=self.batch,
-                                              n=out, k=inp, activation=a.get("activation", 0))))
+                                              n=out, k=inp, activation=a.get("activation", 0),
+                                              w_split=self._split(op.inputs[1]))))
             elif op.type == "SOFTMAX":
                 x, y = self._buf(op.inputs[0]), self._buf(op.output)
                 self._plan.append(("softmax", dict(x=x, y=y, rows=self.batch,
@@ -132,7 +145,8 @@ class CnnExecutor:
         for kind, p in self._plan:
             if kind == "conv":
                 g.conv2d_nhwc(p["x"], p["w"], p["bias"], p["y"], stride=p["stride"], pad=p["pad"],
-                              activation=p["activation"], residual=p["residual"])
+                              activation=p["activation"], residual=p["residual"],
+                              w_split=p["w_split"])
             elif kind == "dw":
                 g.depthwise_nhwc(p["x"], p["w"], p["bias"], p["y"], stride=p["stride"],
                                  pad=p["pad"], dilation=p["dilation"], activation=p["activation"])
@@ -143,7 +157,7 @@ class CnnExecutor:
             elif kind == "fc":
                 g.gemm(p["x"], p["w"], p["y"], m=p["m"], n=p["n"], k=p["k"],
                        a_strides=(0, p["k"], 1), b_strides=(0, 1, p["k"]), c_strides=(0, p["n"]),
-                       bias=p["bias"], activation=p["activation"])
+                       bias=p["bias"], activation=p["activation"], b_split=p["w_split"])
             elif kind == "softmax":
                 g.softmax_rows(p["x"], p["y"], p["rows"], p["cols"])
 

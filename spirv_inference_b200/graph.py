@@ -148,8 +148,15 @@ class Graph:
     def _p(t):
         return ctypes.c_void_p(t.ptr) if t is not None else None
 
+    def weights_split(self, w) -> tuple:
+        """Pre-splits weights for the tensor-core path: returns (hi, lo)."""
+        hi, lo = self.alloc(w.shape), self.alloc(w.shape)
+        check(self._l.spx_weights_split(self.h, self._p(w), self._p(hi), self._p(lo), w.size))
+        return hi, lo
+
     def conv2d_nhwc(self, x, w, bias, y, *, stride=(1, 1), pad=(0, 0), dilation=(1, 1),
-                    weight_layout=_lib.WEIGHT_OHWI, activation=_lib.ACT_NONE, residual=None):
+                    weight_layout=_lib.WEIGHT_OHWI, activation=_lib.ACT_NONE, residual=None,
+                    w_split=None):
         n, ih, iw, ic = x.shape
         _, oh, ow, oc = y.shape
         if weight_layout == _lib.WEIGHT_OHWI:
@@ -158,8 +165,13 @@ class Graph:
             kh, kw = w.shape[0], w.shape[1]
         p = _lib.ConvParams(n, ih, iw, ic, oc, oh, ow, kh, kw, stride[0], stride[1], pad[0],
                             pad[1], dilation[0], dilation[1], weight_layout, activation)
-        check(self._l.spx_op_conv2d_nhwc(self.h, self._p(x), self._p(w), self._p(bias),
-                                         self._p(residual), self._p(y), ctypes.byref(p)))
+        if w_split is not None:
+            check(self._l.spx_op_conv2d_nhwc_split(
+                self.h, self._p(x), self._p(w), self._p(w_split[0]), self._p(w_split[1]),
+                self._p(bias), self._p(residual), self._p(y), ctypes.byref(p)))
+        else:
+            check(self._l.spx_op_conv2d_nhwc(self.h, self._p(x), self._p(w), self._p(bias),
+                                             self._p(residual), self._p(y), ctypes.byref(p)))
 
     def depthwise_nhwc(self, x, w, bias, y, *, stride=(1, 1), pad=(0, 0), dilation=(1, 1),
                        activation=_lib.ACT_NONE):
@@ -173,14 +185,19 @@ class Graph:
 
     def gemm(self, a, b, c, *, m, n, k, batch=1, a_strides, b_strides, c_strides, bias=None,
              residual=None, alpha=1.0, activation=_lib.ACT_NONE, batch_inner=1, b_inner_div=1,
-             inner_strides=(0, 0, 0)):
+             inner_strides=(0, 0, 0), b_split=None):
         """C[b][m][n] = act(alpha * A.B + bias + R).  *_strides = (batch, row/k, k/col)."""
         p = _lib.GemmParams(batch, m, n, k, batch_inner, b_inner_div, a_strides[0], a_strides[1],
                             a_strides[2], b_strides[0], b_strides[1], b_strides[2], c_strides[0],
                             c_strides[1], inner_strides[0], inner_strides[1], inner_strides[2],
                             alpha, activation)
-        check(self._l.spx_op_gemm(self.h, self._p(a), self._p(b), self._p(bias),
-                                  self._p(residual), self._p(c), ctypes.byref(p)))
+        if b_split is not None:
+            check(self._l.spx_op_gemm_split(self.h, self._p(a), self._p(b), self._p(b_split[0]),
+                                            self._p(b_split[1]), self._p(bias),
+                                            self._p(residual), self._p(c), ctypes.byref(p)))
+        else:
+            check(self._l.spx_op_gemm(self.h, self._p(a), self._p(b), self._p(bias),
+                                      self._p(residual), self._p(c), ctypes.byref(p)))
 
     def linear(self, x, w_t, y, bias=None, activation=_lib.ACT_NONE, residual=None):
         """y[m][n] = x[m][k] @ w_t[k][n] (+bias, +residual), row-major 2-D views."""

@@ -39,6 +39,8 @@ CONV_CASES = [
     (2, 7, 7, 320, 1280, 1, 1, 0, 1, _lib.ACT_RELU6, False, _lib.WEIGHT_OHWI),
     (4, 1, 1, 1280, 1001, 1, 1, 0, 1, _lib.ACT_NONE, False, _lib.WEIGHT_OHWI),
     (1, 30, 30, 64, 16, 3, 2, 1, 1, _lib.ACT_RELU, True, _lib.WEIGHT_HWIO),
+    (2, 10, 11, 4, 16, 3, 1, 1, 1, _lib.ACT_RELU, True, _lib.WEIGHT_HWIO),   # direct small-K
+    (1, 13, 13, 3, 64, 3, 2, 1, 1, _lib.ACT_RELU6, False, _lib.WEIGHT_OHWI),  # direct small-K
 ]
 
 
@@ -67,7 +69,11 @@ def test_conv2d_nhwc(g, case):
 @pytest.mark.parametrize("n,ih,c,k,s,dil,act", [(2, 14, 32, 3, 1, 1, _lib.ACT_RELU6),
                                                (1, 15, 96, 3, 2, 1, _lib.ACT_RELU6),
                                                (2, 9, 5, 5, 1, 1, _lib.ACT_NONE),
-                                               (1, 12, 8, 3, 1, 2, _lib.ACT_RELU)])
+                                               (1, 12, 8, 3, 1, 2, _lib.ACT_RELU),
+                                               (2, 15, 40, 5, 2, 1, _lib.ACT_RELU6),
+                                               (1, 14, 112, 5, 1, 1, _lib.ACT_RELU6),
+                                               (3, 7, 160, 3, 1, 1, _lib.ACT_NONE),
+                                               (1, 13, 24, 3, 2, 1, _lib.ACT_RELU6)])
 def test_depthwise_nhwc(g, n, ih, c, k, s, dil, act):
     eff = (k - 1) * dil + 1
     # TFLite SAME: floor(total/2) on top/left

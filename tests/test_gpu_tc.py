@@ -82,3 +82,27 @@ def test_tc_ineligible_shape_reports_unsupported(g):
         g.gemm(g.tensor(a), g.tensor(w), dc, m=10, n=8, k=6, a_strides=(0, 6, 1),
                b_strides=(0, 1, 6), c_strides=(0, 8))
     assert e.value.code == _lib.SPX_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("M,N,K", [(1000, 96, 24), (4096, 240, 960), (333, 1001, 1280),
+                                   (12544, 160, 960), (256, 1280, 320)])
+def test_tc_presplit_weights_match_on_chip_split(g, M, N, K):
+    a = _r(M, K)
+    w = _r(N, K, scale=1.0 / np.sqrt(K))
+    res = _r(M, N)
+    da, dw, dr = g.tensor(a), g.tensor(w), g.tensor(res)
+    hi, lo = g.weights_split(dw)
+    h, l = hi.download(), lo.download()
+    assert np.all((h.view(np.uint32) & 0x1FFF) == 0) and np.all((l.view(np.uint32) & 0x1FFF) == 0)
+    np.testing.assert_allclose(h.astype(np.float64) + l, w, rtol=2 ** -21, atol=0)
+    outs = []
+    for split in (None, (hi, lo)):
+        dc = g.alloc((M, N))
+        g.gemm(da, dw, dc, m=M, n=N, k=K, a_strides=(0, K, 1), b_strides=(0, 1, K),
+               c_strides=(0, N), residual=dr, activation=_lib.ACT_RELU, b_split=split)
+        outs.append(dc.download())
+    # the same tf32 terms enter the same MMAs: identical results
+    np.testing.assert_array_equal(outs[0], outs[1])
+    ref = np.maximum(a.astype(np.float64) @ w.T.astype(np.float64) + res, 0)
+    err = np.abs(outs[1] - ref).max() / np.abs(ref).max()
+    assert err <= 2.5e-8 * K + 1e-6, err
