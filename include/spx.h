@@ -111,6 +111,25 @@ int spx_run_kernel(const char* kernel, const float* input0, size_t input0_len,
                    size_t output_elements, const int32_t* push, size_t push_len,
                    int device, spx_kernel_output_info* info);
 
+/* Allocation-free form of the "conv2d" dispatch above.  No counterpart in
+ * the reference: it exists for callers that cannot let a library allocate
+ * device memory (hosts whose own pool allocator owns the whole GPU, or
+ * latency-critical loops where cudaMalloc's implicit device synchronisation is
+ * not acceptable).  x, w and y are caller-owned DEVICE buffers with the
+ * reference layouts (x NCHW, w OIHW followed by oc biases, y NCHW); push holds
+ * the same 15 push constants as "conv2d".  Work is recorded on `stream`
+ * (a cudaStream_t; NULL = legacy default stream) and the call returns without
+ * waiting.  The NHWC / OHWI staging lives in one fixed 16 MiB device array
+ * inside the library (every GPU that loads libspx holds it until exit);
+ * convolutions whose input + weights + output exceed 4 Mi floats are rejected
+ * with SPX_ERR_INVALID_ARGUMENT.  The first call on each device looks up the
+ * array's device address; make that first call before any stream capture.
+ * All calls share the array: calls that can overlap on the GPU (other
+ * streams, other host threads) race and must be serialised by the caller.
+ * No cudaMalloc, cudaFree or allocating library routine is called. */
+int spx_conv2d_nchw_noalloc(const float* x, const float* w, float* y, const int32_t* push,
+                            size_t push_len, void* stream);
+
 /* ---- 2. device-resident graph API -------------------------------------- */
 typedef struct spx_graph spx_graph;
 

@@ -88,6 +88,7 @@ _SIGS = {
     "spx_kernel_local_size": ([c_char_p], c_int),
     "spx_run_kernel": ([c_char_p, _FP, c_size_t, _FP, c_size_t, _FP, c_size_t, _IP, c_size_t,
                         c_int, POINTER(KernelOutputInfo)], c_int),
+    "spx_conv2d_nchw_noalloc": ([c_void_p, c_void_p, c_void_p, _IP, c_size_t, c_void_p], c_int),
     "spx_graph_create": ([c_int, POINTER(c_void_p)], c_int),
     "spx_graph_create_on_stream": ([c_int, c_void_p, POINTER(c_void_p)], c_int),
     "spx_graph_destroy": ([c_void_p], c_int),
