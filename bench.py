@@ -102,6 +102,7 @@ def cpu_baseline(model, seconds: float = 10.0, max_images: int = 64) -> dict:
     host cores), one image per pass, until `seconds` have elapsed."""
     from oracle import oracle
     from spirv_inference_b200 import lowering, nets
+    oracle.use_all_host_cores()
     x = nets.make_input(model, 1, seed=4321)
     lowering.run_graph(model, x, oracle.run_kernel)  # warm
     n, t0 = 0, time.perf_counter()
@@ -115,10 +116,8 @@ def cpu_baseline(model, seconds: float = 10.0, max_images: int = 64) -> dict:
 
 
 def dist_setup():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
+    from spirv_inference_b200.sharding import dist_env
+    return dist_env()
 
 
 def run_reference(args) -> None:
@@ -128,6 +127,7 @@ def run_reference(args) -> None:
     from oracle import oracle
     from spirv_inference_b200 import lowering, nets
     model = nets.MODELS[args.model](seed=0)
+    oracle.use_all_host_cores()
     per_step = args.ref_images
     x = nets.make_input(model, per_step, seed=4321)
     for _ in range(args.warmup):
@@ -178,7 +178,8 @@ def run_spx(args) -> None:
     torch.cuda.set_stream(stream)
     g = Graph(local, stream=stream.cuda_stream)
     ex = CnnExecutor(model, batch=B, graph=g)
-    x = nets.make_input(model, B, seed=1000 + rank)  # this rank's shard of the global batch
+    from spirv_inference_b200.sharding import shard_seed as _seed
+    x = nets.make_input(model, B, seed=_seed(1000, rank))  # this rank's shard of the global batch
     g.upload(ex.input, x)
     ex.capture()
 
@@ -188,12 +189,10 @@ def run_spx(args) -> None:
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
+    from spirv_inference_b200.sharding import max_over_ranks as _mor, shard_seed, throughput
+
     def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], device="cuda", dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        return float(t.item())
+        return _mor(v, device="cuda")
 
     # ---- device-resident throughput (value) ----
     for _ in range(max(args.warmup, 3)):
@@ -210,7 +209,7 @@ def run_spx(args) -> None:
     launches = g.launch_count
     ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
     barrier()
-    value = world * B / (ms / 1e3)
+    value = throughput(B, world, ms)
 
     # ---- per-kernel timing of one eager pass (roofline) ----
     costs = ex.op_costs()
@@ -249,8 +248,16 @@ def run_spx(args) -> None:
     per_launch_bytes = d["bytes"] / d["launches"]
     per_launch_s = d["ms"] / d["launches"] / 1e3
     ach = per_launch_bytes / per_launch_s / 1e9
+    # DRAM traffic per launch, from the committed ncu capture of this kernel
+    # (profiles/gemm_tc_expand_16to96_b64.md): dram read + write = 300.4 MB
+    # against 359.6 MB algorithmic for that launch (ratio 0.835; the balance
+    # was still in L2 when the kernel ended).  Scaled to this class's average
+    # algorithmic bytes per launch; only meaningful for the GEMM class.
+    traffic = round(per_launch_bytes * (300.4 / 359.6)) if top == "conv1x1" else None
     roofline = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"],
-                "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None,
+                "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": traffic,
+                "traffic_source": "ncu capture of one gemm_tc launch (expand 16->96, batch 64), "
+                                  "dram bytes / algorithmic bytes scaled to the class average",
                 "kernel": top, "peak_source": peaks["source"],
                 "note": "achieved = algorithmic bytes per launch / CUDA-event launch time, "
                         "averaged over the class's launches in one eager pass"}
@@ -289,7 +296,7 @@ def run_spx(args) -> None:
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
     barrier()
-    e2e_value = world * B / (e2e_ms / 1e3)
+    e2e_value = throughput(B, world, e2e_ms)
 
     if rank == 0:
         line = {

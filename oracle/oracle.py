@@ -36,6 +36,8 @@ def lib():
                                         ctypes.c_size_t]
         l.oracle_run_kernel.restype = ctypes.c_int
         l.oracle_num_threads.restype = ctypes.c_int
+        l.oracle_set_threads.argtypes = [ctypes.c_int]
+        l.oracle_set_threads.restype = None
         _lib = l
     return _lib
 
@@ -60,6 +62,15 @@ def run_kernel(kernel: str, input0, input1, output_elements: int, push) -> np.nd
     if rc != 0:
         raise ValueError(f"oracle rejected {kernel!r} push={list(q)}")
     return out
+
+
+def use_all_host_cores() -> int:
+    """Sets the OpenMP team to every core this process may run on (launchers
+    such as torchrun export OMP_NUM_THREADS=1) and returns the count."""
+    import os
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    lib().oracle_set_threads(int(n or 1))
+    return num_threads()
 
 
 def num_threads() -> int:

@@ -415,6 +415,10 @@ int oracle_num_threads(void);
 #ifdef _OPENMP
 #include <omp.h>
 int oracle_num_threads(void) { return omp_get_max_threads(); }
+extern "C" void oracle_set_threads(int n) {
+  if (n > 0) omp_set_num_threads(n);
+}
 #else
+extern "C" void oracle_set_threads(int n) { (void)n; }
 int oracle_num_threads(void) { return 1; }
 #endif
