@@ -6,11 +6,12 @@ pure-Python or CPU fallback for any operator.
 from __future__ import annotations
 
 import ctypes
+import os
 from ctypes import POINTER, Structure, c_char, c_char_p, c_double, c_float, c_int, c_int32
 from ctypes import c_int64, c_size_t, c_uint32, c_void_p
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "libspx.so"
+LIB_PATH = Path(os.environ.get("SPX_LIBRARY") or Path(__file__).resolve().parent / "libspx.so")
 
 SPX_OK = 0
 SPX_ERR_INVALID_ARGUMENT = 1

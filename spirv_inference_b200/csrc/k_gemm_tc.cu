@@ -47,6 +47,19 @@ namespace spx {
 
 __device__ int g_tc_status = 0;
 
+#ifdef SPX_TC_TRACE
+// Development-only pipeline trace of CTA 0 (not compiled into the library).
+__device__ unsigned long long g_tc_trace[8][64];
+#define TC_TRACE(ev, i)                                                     \
+  do {                                                                      \
+    if (blockIdx.x == 0 && (i) < 64) g_tc_trace[ev][i] = gtimer();          \
+  } while (0)
+#else
+#define TC_TRACE(ev, i) \
+  do {                  \
+  } while (0)
+#endif
+
 namespace {
 
 constexpr int kBM = 128;         // UMMA M: output rows per tile
@@ -59,7 +72,11 @@ constexpr int kMmaWarp = kProducerWarp + 1;
 constexpr int kThreads = (kMmaWarp + 1) * 32;  // 18 warps
 constexpr int kMaxStages = 8;
 constexpr int kEpiStride = 36;   // floats per row of a warp's transpose tile
-constexpr uint32_t kEpiBytes = kEpiWarps * 32 * kEpiStride * 4;  // 32 rows per warp
+// Per-warp epilogue slot (1024-aligned): a 32 x 32 fp32 TMA staging tile in
+// 128-byte-swizzled layout (4 KB), or the padded transpose tile of the
+// fallback path (32 x kEpiStride floats).
+constexpr uint32_t kEpiSlot = 5120;
+constexpr uint32_t kEpiBytes = kEpiWarps * kEpiSlot;
 constexpr uint32_t kATileBytes = kBM * kBK * 4;       // 16 KB
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 constexpr unsigned long long kDrainNs = 200000000ull;     // 0.2 s drain on abort
@@ -68,6 +85,7 @@ struct TcArgs {
   int M, N, K, BN, n_tiles, m_tiles, k_blocks, stages;
   uint32_t idesc, tmem_cols, stage_bytes, b_bytes;
   int presplit;  // B arrives as hi and lo tiles: converters split A only
+  int tma_store; // C (and the residual) move through TMA, 32 x 32 boxes per warp
   const float* bias;
   const float* res;
   float* c;
@@ -175,6 +193,24 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x,
+                                             int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(x), "r"(y), "r"(su32(src))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 __device__ __forceinline__ float tf32_rna(float x) {
   uint32_t h;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
@@ -220,17 +256,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmBlo, const TcArgs p) {
+                   const __grid_constant__ CUtensorMap tmBlo,
+                   const __grid_constant__ CUtensorMap tmC,
+                   const __grid_constant__ CUtensorMap tmR, const TcArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int S = p.stages;
-  float* epi = (float*)(smem + (size_t)S * p.stage_bytes);  // kEpiWarps x 32 x kEpiStride
-  uint64_t* full = (uint64_t*)((uint8_t*)epi + kEpiBytes);
+  uint8_t* epi = smem + (size_t)S * p.stage_bytes;  // kEpiWarps slots of kEpiSlot bytes
+  uint64_t* full = (uint64_t*)(epi + kEpiBytes);
   uint64_t* conv = full + kMaxStages;
   uint64_t* empty = conv + kMaxStages;
   uint64_t* tfull = empty + kMaxStages;
   uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
+  uint64_t* rfull = tempty + 2;  // per epilogue warp: residual box landed
+  uint64_t* drain = rfull + kEpiWarps;
   uint32_t* tmem_slot = (uint32_t*)(drain + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
@@ -245,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bar_init(&tfull[a], 1);
       bar_init(&tempty[a], kEpiWarps * 32);
     }
+    for (int w = 0; w < kEpiWarps; ++w) bar_init(&rfull[w], 1);
     bar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -273,6 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!bar_wait(&empty[s], ph ^ 1, abort_flag, kTimeoutNs, 64)) goto producer_done;
           uint8_t* st = smem + (size_t)s * p.stage_bytes;
           bar_expect_tx(&full[s], tx);
+          if (kb == 0) TC_TRACE(0, (t - blockIdx.x) / gridDim.x);
           tma_load_2d(st, &tmA, &full[s], kb * kBK, mt * kBM);
           tma_load_2d(st + 2 * kATileBytes, &tmB, &full[s], kb * kBK, nt * p.BN);
           if (p.presplit)
@@ -302,10 +343,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool issued = false;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         if (!bar_wait(&tempty[acc], aph ^ 1, abort_flag, kTimeoutNs, 64)) goto mma_done;
+        TC_TRACE(2, (t - blockIdx.x) / gridDim.x);
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(acc * p.BN);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!bar_wait(&conv[s], ph, abort_flag, kTimeoutNs, 64)) goto mma_done;
+          if (kb == 0) TC_TRACE(3, (t - blockIdx.x) / gridDim.x);
           tc_fence_after();
           const uint32_t a_hi = su32(smem + (size_t)s * p.stage_bytes);
           const uint32_t a_lo = a_hi + kATileBytes;
@@ -328,6 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         umma_commit(&tfull[acc]);
+        TC_TRACE(4, (t - blockIdx.x) / gridDim.x);
         acc ^= 1;
         if (!acc) aph ^= 1;
       }
@@ -346,6 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       for (int kb = 0; kb < p.k_blocks; ++kb) {
         if (!bar_wait(&full[s], ph, abort_flag, kTimeoutNs, 256)) goto conv_done;
+        if (kb == 0 && ct == 0) TC_TRACE(7, (t - blockIdx.x) / gridDim.x);
         uint8_t* st = smem + (size_t)s * p.stage_bytes;
         split_buffer((float4*)st, (float4*)(st + kATileBytes), kATileBytes / 16, ct,
                      kConvThreads);
@@ -355,6 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                        kConvThreads);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         bar_arrive(&conv[s]);
+        if (kb == 0 && ct == 0) TC_TRACE(1, (t - blockIdx.x) / gridDim.x);
         if (++s == S) {
           s = 0;
           ph ^= 1;
@@ -362,19 +408,87 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   conv_done:;
+  } else if (p.tma_store) {
+    // ---------------- epilogue via TMA (warps 0 .. kEpiWarps-1) ----------------
+    // Warp w reads TMEM lane quarter w % 4 (lane = tile row) and takes every
+    // (kEpiWarps / 4)-th 32-column chunk starting at chunk w / 4.  Per chunk:
+    // lane 0 frees the warp's staging tile (previous store has read it) and
+    // TMA-loads the residual box into it; lanes add bias / residual, apply the
+    // activation, write their row back 128-byte swizzled; lane 0 TMA-stores
+    // the 32 x 32 box.  No block-wide barrier; stores run asynchronously.
+    int acc = 0;
+    uint32_t aph = 0, rph = 0;
+    uint8_t* stg = epi + warp * kEpiSlot;
+    float4* srow = reinterpret_cast<float4*>(stg + lane * 128);
+    const int sw = lane & 7;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const int mt = t / p.n_tiles, nt = t % p.n_tiles;
+      ok = bar_wait(&tfull[acc], aph, abort_flag, kTimeoutNs, 128) && ok;
+      if (threadIdx.x == 0) TC_TRACE(5, (t - blockIdx.x) / gridDim.x);
+      if (__any_sync(0xffffffffu, !ok)) break;
+      tc_fence_after();
+      const int quarter = warp & 3;
+      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.BN);
+      const int row0 = mt * kBM + quarter * 32;
+      for (int c0 = (warp >> 2) * 32; c0 < p.BN; c0 += 32 * (kEpiWarps / 4)) {
+        const int n0 = nt * p.BN + c0;
+        if (n0 >= p.N) break;  // uniform across the warp
+        if (lane == 0) {
+          bulk_wait_read0();
+          if (p.res) {
+            bar_expect_tx(&rfull[warp], 32 * 32 * 4);
+            tma_load_2d(stg, &tmR, &rfull[warp], n0, row0);
+          }
+        }
+        __syncwarp();
+        float v[32];
+        tmem_ld32(tbase + (uint32_t)c0, v);
+        if (p.res) {
+          ok = bar_wait(&rfull[warp], rph, abort_flag) && ok;
+          rph ^= 1;
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int nq = n0 + 4 * q;
+          float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (p.bias && nq < p.N) b4 = __ldg(reinterpret_cast<const float4*>(p.bias + nq));
+          const float4 r4 = p.res ? srow[q ^ sw] : make_float4(0.f, 0.f, 0.f, 0.f);
+          float4 o;
+          o.x = apply_act(p.act, v[4 * q + 0] * p.alpha + b4.x + r4.x);
+          o.y = apply_act(p.act, v[4 * q + 1] * p.alpha + b4.y + r4.y);
+          o.z = apply_act(p.act, v[4 * q + 2] * p.alpha + b4.z + r4.z);
+          o.w = apply_act(p.act, v[4 * q + 3] * p.alpha + b4.w + r4.w);
+          srow[q ^ sw] = o;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, stg, n0, row0);
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      bar_arrive(&tempty[acc]);
+      if (threadIdx.x == 0) TC_TRACE(6, (t - blockIdx.x) / gridDim.x);
+      acc ^= 1;
+      if (!acc) aph ^= 1;
+    }
+    if (lane == 0) bulk_wait_all();
   } else {
     // ---------------- epilogue (warps 0 .. kEpiWarps-1) ----------------
     // Warp w reads TMEM lane quarter w % 4 and takes every
     // (kEpiWarps / 4)-th 32-column chunk starting at chunk w / 4.
     int acc = 0;
     uint32_t aph = 0;
-    float* tile = epi + warp * 32 * kEpiStride;  // this warp's 32 x 32 transpose tile
+    float* tile = reinterpret_cast<float*>(epi + warp * kEpiSlot);  // 32 x kEpiStride tile
     const int sub_r = lane >> 3;                 // 0..3: row within a group of 4
     const int sub_c = (lane & 7) * 4;            // first of 4 columns
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const int mt = t / p.n_tiles, nt = t % p.n_tiles;
       // Uniform per warp: every lane waits on the same barrier phase.
       const bool ok = bar_wait(&tfull[acc], aph, abort_flag, kTimeoutNs, 128);
+      if (threadIdx.x == 0) TC_TRACE(5, (t - blockIdx.x) / gridDim.x);
       if (__any_sync(0xffffffffu, !ok)) break;
       tc_fence_after();
       const int quarter = warp & 3;
@@ -426,6 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       bar_arrive(&tempty[acc]);
+      if (threadIdx.x == 0) TC_TRACE(6, (t - blockIdx.x) / gridDim.x);
       acc ^= 1;
       if (!acc) aph ^= 1;
     }
@@ -550,12 +665,18 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   p.act = act;
   auto al16 = [](const void* q) { return ((uintptr_t)q & 15) == 0; };
   p.vec4 = (ldc % 4 == 0) && al16(c) && (!res || al16(res)) && (!bias || al16(bias));
+  p.tma_store = p.vec4;
   CUtensorMap ma, mb, mblo;
   int rc;
   if ((rc = make_map(&ma, a, M, K, lda, kBM))) return rc;
   if ((rc = make_map(&mb, b, N, K, ldb, p.BN))) return rc;
   mblo = mb;
   if (p.presplit && (rc = make_map(&mblo, b_lo, N, K, ldb, p.BN))) return rc;
+  CUtensorMap mc = ma, mr = ma;
+  if (p.tma_store) {
+    if ((rc = make_map(&mc, c, M, N, ldc, 32))) return rc;
+    if (res && (rc = make_map(&mr, res, M, N, ldc, 32))) return rc;
+  }
   const size_t smem = 1024 + (size_t)p.stages * p.stage_bytes + kEpiBytes + 512;
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
@@ -566,7 +687,7 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   if (attr_err != cudaSuccess) return check_cuda(attr_err, "gemm_tc: smem attribute");
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  gemm_tc_kernel<<<grid, kThreads, smem, s>>>(ma, mb, mblo, p);
+  gemm_tc_kernel<<<grid, kThreads, smem, s>>>(ma, mb, mblo, mc, mr, p);
   return after_launch(cnt, "gemm_tc");
 }
 
@@ -576,6 +697,12 @@ int launch_weights_split(cudaStream_t s, int64_t* cnt, const float* w, float* hi
   weights_split_kernel<<<grid_for(n, 256), 256, 0, s>>>(w, hi, lo, n);
   return after_launch(cnt, "weights_split");
 }
+
+#ifdef SPX_TC_TRACE
+extern "C" int spx_tc_trace_fetch(unsigned long long* out) {
+  return cudaMemcpyFromSymbol(out, g_tc_trace, sizeof(g_tc_trace)) == cudaSuccess ? 0 : 3;
+}
+#endif
 
 int tc_take_status() {
   int v = 0;
