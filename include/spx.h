@@ -76,7 +76,9 @@ int spx_select_device(const char* selector, int* ordinal);
 
 /* Process-wide options.  "gemm_path": 0 = automatic (tensor cores where the
  * operands allow, exact-fp32 SIMT otherwise), 1 = SIMT only, 2 = tensor cores
- * required (shapes they cannot take fail with SPX_ERR_UNSUPPORTED). */
+ * required (shapes they cannot take fail with SPX_ERR_UNSUPPORTED).
+ * "dw_path": 0 = automatic (TMA-tiled depthwise where the shape allows),
+ * 1 = the register sliding-window depthwise kernel only. */
 int spx_set_option(const char* name, int64_t value);
 int64_t spx_get_option(const char* name);
 

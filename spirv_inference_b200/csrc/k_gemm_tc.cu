@@ -417,6 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // activation, write their row back 128-byte swizzled; lane 0 TMA-stores
     // the 32 x 32 box.  No block-wide barrier; stores run asynchronously.
     int acc = 0;
+    int issuer = 31;  // lane that issued the last store from this warp's staging
     uint32_t aph = 0, rph = 0;
     uint8_t* stg = epi + warp * kEpiSlot;
     float4* srow = reinterpret_cast<float4*>(stg + lane * 128);
@@ -434,8 +435,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c0 = (warp >> 2) * 32; c0 < p.BN; c0 += 32 * (kEpiWarps / 4)) {
         const int n0 = nt * p.BN + c0;
         if (n0 >= p.N) break;  // uniform across the warp
-        if (lane == 0) {
-          bulk_wait_read0();
+        // The lane that issued the previous store waits until it has read the
+        // staging tile; the next store is issued by the following lane, so no
+        // lane's proxy fence has to wait behind its own in-flight store.
+        if (lane == issuer) bulk_wait_read0();
+        const int next = (issuer + 1) & 31;
+        if (lane == next) {
           if (p.res) {
             bar_expect_tx(&rfull[warp], 32 * 32 * 4);
             tma_load_2d(stg, &tmR, &rfull[warp], n0, row0);
@@ -463,10 +468,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
-        if (lane == 0) {
+        if (lane == next) {
           tma_store_2d(&tmC, stg, n0, row0);
           bulk_commit();
         }
+        issuer = next;
       }
       tc_fence_before();
       bar_arrive(&tempty[acc]);
@@ -474,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc ^= 1;
       if (!acc) aph ^= 1;
     }
-    if (lane == 0) bulk_wait_all();
+    bulk_wait_all();  // every lane that issued stores waits for them
   } else {
     // ---------------- epilogue (warps 0 .. kEpiWarps-1) ----------------
     // Warp w reads TMEM lane quarter w % 4 and takes every

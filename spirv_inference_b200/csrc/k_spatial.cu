@@ -343,7 +343,9 @@ int launch_dw_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
       p.sw <= 0 || p.ih <= 0 || p.iw <= 0)
     return fail(SPX_ERR_INVALID_ARGUMENT, "depthwise: bad shape");
   {
-    int rc = try_dw_rows(s, cnt, x, w, bias, y, q);
+    int rc = g_dw_path != 1 ? try_dw_tma(s, cnt, x, w, bias, y, q) : -1;
+    if (rc != -1) return rc;
+    rc = try_dw_rows(s, cnt, x, w, bias, y, q);
     if (rc != -1) return rc;
   }
   int64_t pix = (int64_t)p.n * p.oh * p.ow;

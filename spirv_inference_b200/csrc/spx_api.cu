@@ -41,6 +41,7 @@ int after_launch(int64_t* counter, const char* what) {
 }
 
 int g_gemm_path = 0;
+int g_dw_path = 0;
 
 // ---- algorithm selection for dense contractions ---------------------------
 int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
@@ -428,6 +429,11 @@ int spx_select_device(const char* selector, int* ordinal) {
 
 int spx_set_option(const char* name, int64_t value) {
   std::string n = name ? name : "";
+  if (n == "dw_path") {
+    if (value < 0 || value > 1) return fail(SPX_ERR_INVALID_ARGUMENT, "dw_path must be 0..1");
+    g_dw_path = (int)value;
+    return SPX_OK;
+  }
   if (n == "gemm_path") {
     if (value < 0 || value > 2) return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_path must be 0..2");
     g_gemm_path = (int)value;
@@ -439,10 +445,13 @@ int spx_set_option(const char* name, int64_t value) {
 int64_t spx_get_option(const char* name) {
   std::string n = name ? name : "";
   if (n == "gemm_path") return g_gemm_path;
+  if (n == "dw_path") return g_dw_path;
   return -1;
 }
 
 static int device_status(const char* what) {
+  if (dw_take_status())
+    return fail(SPX_ERR_CUDA, "%s: a depthwise tile load wait timed out", what);
   if (tc_take_status())
     return fail(SPX_ERR_CUDA, "%s: a tensor-core pipeline wait timed out; tiles were abandoned",
                 what);

@@ -113,6 +113,12 @@ int try_dw_rows(cudaStream_t s, int64_t* cnt, const float* x, const float* w, co
 int try_conv_smallk(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
                     const float* bias, const float* res, float* y, const spx_conv_params* p);
 
+// TMA-tiled depthwise (k_dw_tma.cu); -1 when the shape is not covered.
+int try_dw_tma(cudaStream_t s, int64_t* cnt, const float* x, const float* w, const float* b,
+               float* y, const spx_dw_params* p);
+// Returns and clears the depthwise kernel's device status (1 = a wait timed out).
+int dw_take_status();
+
 // tcgen05 3xTF32 GEMM (k_gemm_tc.cu): both operands K-contiguous.
 bool gemm_tc_eligible(const float* a, int64_t lda, const float* b, int64_t ldb, int M, int N,
                       int K, const float* c, int64_t ldc);
@@ -130,6 +136,9 @@ int tc_take_status();
 // Process-wide dense-contraction path: 0 auto, 1 SIMT only, 2 tensor cores
 // required (ineligible shapes fail with SPX_ERR_UNSUPPORTED).
 extern int g_gemm_path;
+// Depthwise path: 0 automatic (TMA tiles where the shape allows), 1 register
+// sliding-window kernel only.
+extern int g_dw_path;
 
 // ---- reference-layout kernels used only by the drop-in boundary ---------
 // (NCHW layouts of the TFLite shader set, one output element per thread.)

@@ -73,7 +73,12 @@ def test_conv2d_nhwc(g, case):
                                                (2, 15, 40, 5, 2, 1, _lib.ACT_RELU6),
                                                (1, 14, 112, 5, 1, 1, _lib.ACT_RELU6),
                                                (3, 7, 160, 3, 1, 1, _lib.ACT_NONE),
-                                               (1, 13, 24, 3, 2, 1, _lib.ACT_RELU6)])
+                                               (1, 13, 24, 3, 2, 1, _lib.ACT_RELU6),
+                                               (2, 15, 144, 3, 2, 1, _lib.ACT_RELU6),
+                                               (1, 20, 64, 5, 2, 1, _lib.ACT_RELU6),
+                                               (2, 9, 32, 5, 1, 1, _lib.ACT_NONE),
+                                               (3, 17, 48, 3, 1, 1, _lib.ACT_RELU),
+                                               (1, 56, 144, 3, 1, 1, _lib.ACT_RELU6)])
 def test_depthwise_nhwc(g, n, ih, c, k, s, dil, act):
     eff = (k - 1) * dil + 1
     # TFLite SAME: floor(total/2) on top/left
