@@ -61,17 +61,20 @@ __global__ void __launch_bounds__(128) conv_smallk_kernel(
     }
     float* yp = y + (size_t)pix * OC;
     const float* rp = res ? res + (size_t)pix * OC : nullptr;
+    with_act(act, [&](auto tag) {
+      constexpr int A = decltype(tag)::value;
 #pragma unroll
-    for (int o = 0; o < OC; o += 4) {
-      float4 v = make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
-      if (rp) {
-        const float4 r = *reinterpret_cast<const float4*>(rp + o);
-        v.x += r.x; v.y += r.y; v.z += r.z; v.w += r.w;
+      for (int o = 0; o < OC; o += 4) {
+        float4 v = make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
+        if (rp) {
+          const float4 r = *reinterpret_cast<const float4*>(rp + o);
+          v.x += r.x; v.y += r.y; v.z += r.z; v.w += r.w;
+        }
+        v.x = act_c<A>(v.x); v.y = act_c<A>(v.y);
+        v.z = act_c<A>(v.z); v.w = act_c<A>(v.w);
+        *reinterpret_cast<float4*>(yp + o) = v;
       }
-      v.x = apply_act(act, v.x); v.y = apply_act(act, v.y);
-      v.z = apply_act(act, v.z); v.w = apply_act(act, v.w);
-      *reinterpret_cast<float4*>(yp + o) = v;
-    }
+    });
   }
 }
 
@@ -130,15 +133,19 @@ __global__ void __launch_bounds__(256, 2) dw_rows_kernel(
         }
       }
     }
+    with_act(act, [&](auto tag) {
+      constexpr int A = decltype(tag)::value;
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int oy = oy0 + r;
-      if (oy >= oh) break;
-      float4 v = acc[r];
-      v.x = apply_act(act, v.x); v.y = apply_act(act, v.y);
-      v.z = apply_act(act, v.z); v.w = apply_act(act, v.w);
-      *reinterpret_cast<float4*>(y + (((size_t)img * oh + oy) * ow + ox) * c + ch) = v;
-    }
+      for (int r = 0; r < R; ++r) {
+        const int oy = oy0 + r;
+        if (oy < oh) {
+          float4 v = acc[r];
+          v.x = act_c<A>(v.x); v.y = act_c<A>(v.y);
+          v.z = act_c<A>(v.z); v.w = act_c<A>(v.w);
+          *reinterpret_cast<float4*>(y + (((size_t)img * oh + oy) * ow + ox) * c + ch) = v;
+        }
+      }
+    });
   }
 }
 

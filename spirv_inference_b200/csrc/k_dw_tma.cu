@@ -165,18 +165,21 @@ __global__ void __launch_bounds__(256, KH == 3 ? 2 : 1)
     __syncthreads();  // every thread is done reading buf[b]
     if (tid == 0 && t + 2 * (int)gridDim.x < total) issue(t + 2 * gridDim.x, b);
     const int ox = tx * TW + ox_l;
+    with_act(act, [&](auto tag) {
+      constexpr int A = decltype(tag)::value;
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int oy = ty * TH + rb * R + r;
-      if (oy < oh && ox < ow) {
-        float4 v = acc[r];
-        v.x = apply_act(act, v.x);
-        v.y = apply_act(act, v.y);
-        v.z = apply_act(act, v.z);
-        v.w = apply_act(act, v.w);
-        *reinterpret_cast<float4*>(y + (((size_t)img * oh + oy) * ow + ox) * c + ch) = v;
+      for (int r = 0; r < R; ++r) {
+        const int oy = ty * TH + rb * R + r;
+        if (oy < oh && ox < ow) {
+          float4 v = acc[r];
+          v.x = act_c<A>(v.x);
+          v.y = act_c<A>(v.y);
+          v.z = act_c<A>(v.z);
+          v.w = act_c<A>(v.w);
+          *reinterpret_cast<float4*>(y + (((size_t)img * oh + oy) * ow + ox) * c + ch) = v;
+        }
       }
-    }
+    });
     b ^= 1;
   }
   if (s_abort && tid == 0) {  // let this CTA's own copies land before it exits

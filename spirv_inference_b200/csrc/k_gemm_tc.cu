@@ -453,19 +453,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = bar_wait(&rfull[warp], rph, abort_flag) && ok;
           rph ^= 1;
         }
+        with_act(p.act, [&](auto tag) {
+          constexpr int A = decltype(tag)::value;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int nq = n0 + 4 * q;
-          float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (p.bias && nq < p.N) b4 = __ldg(reinterpret_cast<const float4*>(p.bias + nq));
-          const float4 r4 = p.res ? srow[q ^ sw] : make_float4(0.f, 0.f, 0.f, 0.f);
-          float4 o;
-          o.x = apply_act(p.act, v[4 * q + 0] * p.alpha + b4.x + r4.x);
-          o.y = apply_act(p.act, v[4 * q + 1] * p.alpha + b4.y + r4.y);
-          o.z = apply_act(p.act, v[4 * q + 2] * p.alpha + b4.z + r4.z);
-          o.w = apply_act(p.act, v[4 * q + 3] * p.alpha + b4.w + r4.w);
-          srow[q ^ sw] = o;
-        }
+          for (int q = 0; q < 8; ++q) {
+            const int nq = n0 + 4 * q;
+            float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (p.bias && nq < p.N) b4 = __ldg(reinterpret_cast<const float4*>(p.bias + nq));
+            const float4 r4 = p.res ? srow[q ^ sw] : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 o;
+            o.x = act_c<A>(v[4 * q + 0] * p.alpha + b4.x + r4.x);
+            o.y = act_c<A>(v[4 * q + 1] * p.alpha + b4.y + r4.y);
+            o.z = act_c<A>(v[4 * q + 2] * p.alpha + b4.z + r4.z);
+            o.w = act_c<A>(v[4 * q + 3] * p.alpha + b4.w + r4.w);
+            srow[q ^ sw] = o;
+          }
+        });
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == next) {
@@ -526,21 +529,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           float* op = &o.x;
           const float* bp = &b4.x;
           float* crow = p.c + m * p.ldc;
-          if (p.vec4 && n + 3 < p.N) {
-            float4 r4 = p.res ? *reinterpret_cast<const float4*>(p.res + m * p.ldc + n)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float* rp = &r4.x;
+          with_act(p.act, [&](auto tag) {
+            constexpr int A = decltype(tag)::value;
+            if (p.vec4 && n + 3 < p.N) {
+              float4 r4 = p.res ? *reinterpret_cast<const float4*>(p.res + m * p.ldc + n)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+              const float* rp = &r4.x;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) op[e] = apply_act(p.act, op[e] + bp[e] + rp[e]);
-            *reinterpret_cast<float4*>(crow + n) = o;
-          } else {
-            for (int e = 0; e < 4; ++e)
-              if (n + e < p.N) {
-                float x = op[e] + bp[e];
-                if (p.res) x += p.res[m * p.ldc + n + e];
-                crow[n + e] = apply_act(p.act, x);
-              }
-          }
+              for (int e = 0; e < 4; ++e) op[e] = act_c<A>(op[e] + bp[e] + rp[e]);
+              *reinterpret_cast<float4*>(crow + n) = o;
+            } else {
+              for (int e = 0; e < 4; ++e)
+                if (n + e < p.N) {
+                  float x = op[e] + bp[e];
+                  if (p.res) x += p.res[m * p.ldc + n + e];
+                  crow[n + e] = act_c<A>(x);
+                }
+            }
+          });
         }
         __syncwarp();
       }

@@ -59,6 +59,40 @@ __device__ __forceinline__ float apply_act(int act, float v) {
   }
 }
 
+// Compile-time activation: epilogues dispatch on the runtime code once per
+// tile or chunk (with_act) so the per-element code is a single specialised
+// expression instead of a multi-way branch over every activation.
+template <int A>
+__device__ __forceinline__ float act_c(float v) {
+  if constexpr (A == SPX_ACT_RELU) return v > 0.0f ? v : 0.0f;
+  else if constexpr (A == SPX_ACT_RELU6) return fminf(v > 0.0f ? v : 0.0f, 6.0f);
+  else if constexpr (A == SPX_ACT_RELU_N1_TO_1) return fminf(fmaxf(v, -1.0f), 1.0f);
+  else if constexpr (A == SPX_ACT_TANH) return tanhf(v);
+  else if constexpr (A == SPX_ACT_GELU_ERF) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+  else if constexpr (A == SPX_ACT_GELU_TANH) {
+    float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+    return 0.5f * v * (1.0f + tanhf(u));
+  } else if constexpr (A == SPX_ACT_SILU) return v / (1.0f + expf(-v));
+  else return v;
+}
+template <int A>
+struct ActTag {
+  static constexpr int value = A;
+};
+template <class F>
+__device__ __forceinline__ void with_act(int act, F&& f) {
+  switch (act) {
+    case SPX_ACT_RELU: f(ActTag<SPX_ACT_RELU>{}); break;
+    case SPX_ACT_RELU6: f(ActTag<SPX_ACT_RELU6>{}); break;
+    case SPX_ACT_RELU_N1_TO_1: f(ActTag<SPX_ACT_RELU_N1_TO_1>{}); break;
+    case SPX_ACT_TANH: f(ActTag<SPX_ACT_TANH>{}); break;
+    case SPX_ACT_GELU_ERF: f(ActTag<SPX_ACT_GELU_ERF>{}); break;
+    case SPX_ACT_GELU_TANH: f(ActTag<SPX_ACT_GELU_TANH>{}); break;
+    case SPX_ACT_SILU: f(ActTag<SPX_ACT_SILU>{}); break;
+    default: f(ActTag<SPX_ACT_NONE>{}); break;
+  }
+}
+
 // ---- launchers (each returns SPX_OK or an error code) -------------------
 // All take the stream to record on and a launch counter (may be null).
 int launch_unary(cudaStream_t s, int64_t* cnt, int op, const float* x, float* y, int64_t n,
