@@ -266,6 +266,9 @@ bool a16(const void* q) { return ((uintptr_t)q & 15) == 0; }
 int try_dw_tma(cudaStream_t s, int64_t* cnt, const float* x, const float* w, const float* b,
                float* y, const spx_dw_params* p) {
   if (p->dilation_h > 1 || p->dilation_w > 1 || p->stride_h != p->stride_w) return -1;
+  // Output tiles are 8 x 16 (stride 1) or 4 x 16 pixels: on maps smaller than
+  // 14 x 14 most of a tile would be padding; the register kernel serves those.
+  if (p->oh < 14 || p->ow < 14) return -1;
   if (!a16(x) || !a16(w) || !a16(y) || (b && !a16(b))) return -1;
   if ((int64_t)p->n * p->oh * p->ow * p->c >= INT32_MAX) return -1;
   if ((int64_t)p->n * (p->oh / 8 + 1) * (p->ow / 8 + 1) * (p->c / 8) >= INT32_MAX) return -1;

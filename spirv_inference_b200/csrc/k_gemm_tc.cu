@@ -649,7 +649,13 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   const int nt0 = (N + 255) / 256;
   p.BN = ((N + nt0 - 1) / nt0 + 31) / 32 * 32;
   p.m_tiles = (M + kBM - 1) / kBM;
-  while (p.BN > 32 && (int64_t)p.m_tiles * ((N + p.BN - 1) / p.BN) < 2 * sm_count())
+  // More, narrower tiles only pay while the k-loop is short: every n-tile
+  // re-splits the same A tiles and narrow UMMAs cost nearly as much to issue
+  // as wide ones.
+  const int kb_total = (K + kBK - 1) / kBK;
+  // With very few tiles (tiny M) narrower tiles win regardless of K.
+  while (p.BN > 32 && (int64_t)p.m_tiles * ((N + p.BN - 1) / p.BN) <
+                          (kb_total <= 4 ? 2 * sm_count() : sm_count() / 2))
     p.BN = (p.BN / 2 + 31) / 32 * 32;
   // At least two pipeline stages must fit next to the epilogue tiles.
   const int budget = 227 * 1024 - 1024 - (int)kEpiBytes - 512;
