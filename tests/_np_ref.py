@@ -110,3 +110,59 @@ def resize_bilinear_nchw(x, oh, ow, align_corners, half_pixel):
     top = xd[:, :, y0][:, :, :, x0] * (1 - xl) + xd[:, :, y0][:, :, :, x1] * xl
     bot = xd[:, :, y1][:, :, :, x0] * (1 - xl) + xd[:, :, y1][:, :, :, x1] * xl
     return top * (1 - yl) + bot * yl
+
+
+def eval_hlo_f64(g, feeds):
+    """Independent float64 evaluation of an spirv_inference_b200.hlo graph."""
+    vals = {}
+    for op in g.ops:
+        oc, a = op.opcode, op.attrs
+        ins = [vals[o] for o in op.operands]
+        if oc == "parameter":
+            vals[op.name] = np.asarray(feeds.get(op.name, g.params.get(op.name)), np.float64).reshape(op.shape)
+            continue
+        if oc == "constant":
+            vals[op.name] = np.array(a["value"], np.float64)
+            continue
+        if oc == "broadcast":
+            view = [1] * len(op.shape)
+            for sa, oa in enumerate(a["dimensions"]):
+                view[oa] = ins[0].shape[sa]
+            r = np.broadcast_to(ins[0].reshape(view), op.shape)
+        elif oc == "reshape":
+            r = ins[0].reshape(op.shape)
+        elif oc == "transpose":
+            r = np.transpose(ins[0], a["dimensions"])
+        elif oc == "pad":
+            r = np.pad(ins[0], a["padding"], constant_values=float(ins[1]))
+        elif oc == "convolution":
+            r = conv_nhwc(ins[0], ins[1], a["stride"], (a["pad"][0][0], a["pad"][1][0]), op.shape[1:3])
+        elif oc == "reduce-window":
+            r = pool_nhwc(ins[0], a["size"], a["stride"], (a["pad"][0][0], a["pad"][1][0]), op.shape[1:3],
+                          1 if a["kind"] == "max" else 0)
+        elif oc == "reduce":
+            f = np.max if a["kind"] == "max" else np.sum
+            r = f(ins[0], axis=tuple(a["dimensions"]))
+        elif oc == "dot":
+            x, y = ins
+            lb, rb = list(a["lhs_batch_dims"]), list(a["rhs_batch_dims"])
+            lc, rc = list(a["lhs_contracting_dims"]), list(a["rhs_contracting_dims"])
+            lf = [d for d in range(x.ndim) if d not in lb + lc]
+            rf = [d for d in range(y.ndim) if d not in rb + rc]
+            xt = np.transpose(x, lb + lf + lc)
+            yt = np.transpose(y, rb + rc + rf)
+            Bs = [x.shape[d] for d in lb]
+            M, K, N = int(np.prod([x.shape[d] for d in lf])), x.shape[lc[0]], int(np.prod([y.shape[d] for d in rf]))
+            r = (xt.reshape(-1, M, K) @ yt.reshape(-1, K, N)).reshape(op.shape)
+        else:
+            fns = {"add": np.add, "subtract": np.subtract, "multiply": np.multiply, "divide": np.divide,
+                   "maximum": np.maximum, "minimum": np.minimum, "power": np.power}
+            una = {"exponential": np.exp, "log": np.log, "sqrt": np.sqrt, "rsqrt": lambda v: 1 / np.sqrt(v),
+                   "negate": np.negative, "abs": np.abs, "tanh": np.tanh,
+                   "logistic": lambda v: 1 / (1 + np.exp(-v))}
+            if oc in fns:
+                r = fns[oc](ins[0], ins[1])
+            else:
+                r = una[oc](ins[0])
+        vals[op.name] = np.asarray(r, np.float64).reshape(op.shape)
+    return vals[g.output]

@@ -1,0 +1,72 @@
+"""GPU parity of the HLO path: the device executor (views + fusion) and the
+drop-in per-op lowering through spx_run_kernel, both against the reference
+executor semantics (hlo.run_hlo) on the CPU oracle."""
+import numpy as np
+import pytest
+
+from spirv_inference_b200 import dispatch, hlo, nets_hlo
+from spirv_inference_b200.executor_hlo import HloExecutor
+
+pytestmark = pytest.mark.gpu
+
+
+def spx_rk(kernel, in0, in1, nout, push):
+    return dispatch.run_kernel(0, dispatch.KernelRun("t", kernel, in0, in1, nout, 0, push)).values
+
+
+def _normerr(got, ref):
+    return float(np.abs(got - ref).max() / np.abs(ref).max())
+
+
+CASES = {
+    "resnet50_hw64_b2": lambda: (nets_hlo.resnet50(seed=1, batch=2, hw=64),
+                                 nets_hlo.make_image_batch(2, 64, seed=5)),
+    "bert_s16_l2_b2": lambda: (nets_hlo.bert_encoder(seed=2, batch=2, seq=16, layers=2),
+                               nets_hlo.bert_embed(2, np.arange(32).reshape(2, 16) * 911 % 30522)),
+    "bert_block_fixture": lambda: nets_hlo.bert_block_fixture(),
+}
+
+
+@pytest.fixture(scope="module")
+def oracle_runs(oracle_built):
+    out = {}
+    for name, make in CASES.items():
+        g, x = make()
+        ref, _ = hlo.run_hlo(g, {g.inputs[0]: x}, oracle_built.run_kernel)
+        out[name] = (g, x, ref)
+    return out
+
+
+@pytest.mark.parametrize("name", list(CASES))
+@pytest.mark.parametrize("fuse", [True, False])
+def test_hlo_executor_matches_oracle(gpu, oracle_runs, name, fuse):
+    g, x, ref = oracle_runs[name]
+    ex = HloExecutor(g, device=gpu, fuse=fuse)
+    try:
+        got = ex.forward({g.inputs[0]: x})
+    finally:
+        ex.close()
+    assert got.shape == ref.shape
+    # logits / activations: <= 1e-3 relative (north-star gate), fp32 here gives ~1e-5
+    assert _normerr(got, ref) <= 1e-4, _normerr(got, ref)
+    if name.startswith("resnet"):
+        np.testing.assert_array_equal(np.argmax(got, 1), np.argmax(ref, 1))
+
+
+def test_hlo_fusion_reduces_kernels(gpu, oracle_runs):
+    g, x, _ = oracle_runs["bert_s16_l2_b2"]
+    fused, plain = HloExecutor(g, device=gpu), HloExecutor(g, device=gpu, fuse=False)
+    try:
+        assert fused.kernels_per_run < plain.kernels_per_run / 2
+        kinds = {s[0] for s in fused.plan}
+        assert {"gemm", "softmax", "layernorm"} <= kinds
+    finally:
+        fused.close()
+        plain.close()
+
+
+def test_hlo_dropin_lowering_matches_oracle(gpu, oracle_runs):
+    g, x, ref = oracle_runs["resnet50_hw64_b2"]
+    got, rep = hlo.run_hlo(g, {g.inputs[0]: x}, spx_rk)
+    assert _normerr(got, ref) <= 1e-4
+    assert rep["dispatches"].count("hlo_conv_nhwc_hwio.spv") == 53
