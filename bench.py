@@ -35,6 +35,34 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "MobileNetV2 fp32 images/sec"
 UNIT = "images/s"
+# Other configs of the same hot path, --model selects.
+METRICS = {
+    "mobilenet_v2": ("MobileNetV2 fp32 images/sec", "images/s"),
+    "efficientnet_lite0": ("EfficientNet-Lite0 fp32 images/sec", "images/s"),
+    "resnet50": ("ResNet-50 fp32 images/sec (HLO path)", "images/s"),
+    "bert": ("BERT-base encoder fp32 sequences/sec (HLO path, seq 128)", "sequences/s"),
+}
+DEFAULT_BATCH = {"mobilenet_v2": 256, "efficientnet_lite0": 64, "resnet50": 256, "bert": 32}
+
+
+def build_model(name: str, batch: int, graph, seed_rank: int):
+    """(executor, host input) for a config; inputs are this rank's shard."""
+    from spirv_inference_b200 import nets, nets_hlo
+    from spirv_inference_b200.sharding import shard_seed
+    if name in ("mobilenet_v2", "efficientnet_lite0"):
+        from spirv_inference_b200.executor import CnnExecutor
+        model = nets.MODELS[name](seed=0)
+        ex = CnnExecutor(model, batch=batch, graph=graph)
+        return ex, nets.make_input(model, batch, seed=shard_seed(1000, seed_rank))
+    from spirv_inference_b200.executor_hlo import HloExecutor
+    if name == "resnet50":
+        g = nets_hlo.resnet50(seed=0, batch=batch)
+        x = nets_hlo.make_image_batch(batch, seed=shard_seed(1000, seed_rank))
+    else:
+        g = nets_hlo.bert_encoder(seed=0, batch=batch, seq=128)
+        rng = np.random.default_rng(shard_seed(1000, seed_rank))
+        x = nets_hlo.bert_embed(0, rng.integers(0, 30522, (batch, 128)))
+    return HloExecutor(g, graph=graph), x
 
 
 def _peaks() -> dict:
@@ -97,22 +125,41 @@ class ClockSampler:
                 "samples": len(self.rows)}
 
 
-def cpu_baseline(model, seconds: float = 10.0, max_images: int = 64) -> dict:
-    """The reference scheduler semantics on the CPU oracle (OpenMP over the
-    host cores), one image per pass, until `seconds` have elapsed."""
+def reference_pass(name: str, batch: int):
+    """One pass of the reference executor semantics on the CPU oracle:
+    the TFLite scheduler lowering (lowering.run_graph) or the HLO executor
+    lowering (hlo.run_hlo), with the oracle as the kernel boundary."""
     from oracle import oracle
-    from spirv_inference_b200 import lowering, nets
+    from spirv_inference_b200 import hlo, lowering, nets, nets_hlo
+    if name in ("mobilenet_v2", "efficientnet_lite0"):
+        model = nets.MODELS[name](seed=0)
+        x = nets.make_input(model, batch, seed=4321)
+        return lambda: lowering.run_graph(model, x, oracle.run_kernel)
+    if name == "resnet50":
+        g = nets_hlo.resnet50(seed=0, batch=batch)
+        feeds = {g.inputs[0]: nets_hlo.make_image_batch(batch, seed=4321)}
+    else:
+        g = nets_hlo.bert_encoder(seed=0, batch=batch, seq=128)
+        ids = np.random.default_rng(4321).integers(0, 30522, (batch, 128))
+        feeds = {g.inputs[0]: nets_hlo.bert_embed(0, ids)}
+    return lambda: hlo.run_hlo(g, feeds, oracle.run_kernel)
+
+
+def cpu_baseline(name: str, seconds: float = 10.0, max_images: int = 64) -> dict:
+    """The reference semantics on the CPU oracle (OpenMP over all host
+    cores), one image / sequence per pass, until `seconds` have elapsed."""
+    from oracle import oracle
     oracle.use_all_host_cores()
-    x = nets.make_input(model, 1, seed=4321)
-    lowering.run_graph(model, x, oracle.run_kernel)  # warm
+    step = reference_pass(name, 1)
+    step()  # warm
     n, t0 = 0, time.perf_counter()
     while n < max_images and (time.perf_counter() - t0) < seconds:
-        lowering.run_graph(model, x, oracle.run_kernel)
+        step()
         n += 1
     dt = time.perf_counter() - t0
     return {"value": n / dt, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
-            "sample": f"{n} single-image {model.name} passes through the reference scheduler "
-                      f"lowering on the C++ oracle ({dt:.1f} s)"}
+            "sample": f"{n} single-{'sequence' if name == 'bert' else 'image'} {name} passes "
+                      f"through the reference executor semantics on the C++ oracle ({dt:.1f} s)"}
 
 
 def dist_setup():
@@ -125,16 +172,16 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     from oracle import oracle
-    from spirv_inference_b200 import lowering, nets
-    model = nets.MODELS[args.model](seed=0)
+    global METRIC, UNIT
+    METRIC, UNIT = METRICS[args.model]
     oracle.use_all_host_cores()
     per_step = args.ref_images
-    x = nets.make_input(model, per_step, seed=4321)
+    step = reference_pass(args.model, per_step)
     for _ in range(args.warmup):
-        lowering.run_graph(model, x, oracle.run_kernel)
+        step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        lowering.run_graph(model, x, oracle.run_kernel)
+        step()
     dt = time.perf_counter() - t0
     v = per_step * args.steps / dt
     line = {
@@ -168,18 +215,15 @@ def run_spx(args) -> None:
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    from spirv_inference_b200 import nets
-    from spirv_inference_b200.executor import CnnExecutor
     from spirv_inference_b200.graph import Graph
 
-    model = nets.MODELS[args.model](seed=0)
+    global METRIC, UNIT
+    METRIC, UNIT = METRICS[args.model]
     B = args.batch
     stream = torch.cuda.Stream()  # a real stream: the legacy default stream cannot be captured
     torch.cuda.set_stream(stream)
     g = Graph(local, stream=stream.cuda_stream)
-    ex = CnnExecutor(model, batch=B, graph=g)
-    from spirv_inference_b200.sharding import shard_seed as _seed
-    x = nets.make_input(model, B, seed=_seed(1000, rank))  # this rank's shard of the global batch
+    ex, x = build_model(args.model, B, g, rank)  # x: this rank's shard of the global batch
     g.upload(ex.input, x)
     ex.capture()
 
@@ -316,7 +360,7 @@ def run_spx(args) -> None:
             "clocks": clk.summary(),
         }
         if not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(model, seconds=args.cpu_seconds)
+            line["cpu_baseline"] = cpu_baseline(args.model, seconds=args.cpu_seconds)
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
@@ -330,13 +374,14 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["spx", "reference"], default="spx")
-    ap.add_argument("--model", default="mobilenet_v2", choices=["mobilenet_v2",
-                                                               "efficientnet_lite0"])
-    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--model", default="mobilenet_v2", choices=list(METRICS))
+    ap.add_argument("--batch", type=int, default=None, help="per-GPU batch (config default)")
     ap.add_argument("--ref-images", type=int, default=2, help="images per reference-arm step")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.batch is None:
+        args.batch = DEFAULT_BATCH[args.model]
     if args.impl == "reference":
         run_reference(args)
     else:

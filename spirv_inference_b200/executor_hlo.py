@@ -298,7 +298,8 @@ class HloExecutor:
             if fn is None:
                 raise NotImplementedError(f"HLO op {op.opcode} has no device lowering")
             fn(op)
-        self.output = self._contig(self.v[self.hg.output])
+        self.output_view = self._contig(self.v[self.hg.output])
+        self.output = self.output_view.t
 
     def _set(self, name: str, view: View):
         self.v[name] = view
@@ -617,6 +618,52 @@ class HloExecutor:
     def kernels_per_run(self) -> int:
         return len(self.plan)
 
+    def op_costs(self) -> list[dict]:
+        """Algorithmic flops / HBM bytes per planned kernel (fp32; inputs,
+        weights, bias, residual read once, output written once)."""
+        out = []
+        for st in self.plan:
+            k = st[0]
+            if k == "conv":
+                p = st[1]
+                x, w, y = p["x"], p["w"], p["y"]
+                kk = int(np.prod(w.shape)) // y.shape[-1]
+                f = 2 * y.size * kk
+                b = x.size + w.size + y.size + (y.size if p["residual"] is not None else 0)
+                label = f"conv{'1x1' if kk == x.shape[-1] else 'kxk'}"
+            elif k == "gemm":
+                p = st[1]
+                bt = p["batch"] * p["batch_inner"]
+                f = 2 * bt * p["m"] * p["n"] * p["k"]
+                b = bt * (p["m"] * p["k"] + p["m"] * p["n"]) + p["b"].size + \
+                    (p["c"].size if p["residual"] is not None else 0)
+                label = "gemm" if p["bias"] is not None else "attn_gemm"
+            elif k in ("softmax", "layernorm"):
+                n = st[1].size
+                f, b, label = 5 * n, 2 * n, k
+            elif k == "binary":
+                n = st[4].size
+                f, b, label = n, 3 * n, "elementwise"
+            elif k in ("pool", "gap", "reduce", "pad4", "unary"):
+                src = st[1] if k != "unary" else st[2]
+                dst = st[2] if k != "unary" else st[3]
+                f, b, label = src.size, src.size + dst.size, k
+            else:
+                f, b, label = 0, 0, k
+            out.append({"kind": k, "label": label, "flops": int(f), "bytes": int(4 * b)})
+        return out
+
+    def record_op(self, i: int) -> None:
+        plan, self.plan = self.plan, [self.plan[i]]
+        try:
+            self.record()
+        finally:
+            self.plan = plan
+
+    @property
+    def input(self):
+        return next(iter(self.inputs.values())).t
+
     def capture(self):
         self.g.sync()
         self.g.capture_begin()
@@ -634,7 +681,7 @@ class HloExecutor:
         for name, v in self.inputs.items():
             self.g.upload(v.t, np.asarray(feeds[name], np.float32).reshape(v.shape))
         self.run()
-        return self.g.download(self.output.t).reshape(self.hg.op(self.hg.output).shape)
+        return self.g.download(self.output).reshape(self.hg.op(self.hg.output).shape)
 
     def close(self):
         self.g.close()
