@@ -322,6 +322,56 @@ int spx_op_argmax_rows(spx_graph* g, const float* x, int32_t* idx, float* val, i
 /* y = silu(gate) * up, elementwise over n values. */
 int spx_op_swiglu(spx_graph* g, const float* gate, const float* up, float* y, int64_t n);
 
+/* ---- TinyLlama decode with a KV cache -------------------------------------
+ * The reference runs every decode step as a full forward pass over a padded
+ * 64-token window with a causal mask (source/xla_hlo/tools/export_llama.py:
+ * 269-365, run_llama_spirv.py:190-260, one hlo_dot_batched dispatch per
+ * matmul).  These entries replace those dispatches with a cached decode:
+ * new tokens' K/V are appended to a per-layer cache and attention reads the
+ * cache.  Positions live in device memory (`state`) so a whole decode step
+ * can be captured once and replayed.
+ *
+ * Shapes: qkv rows are [q heads | k heads | v heads] x head_dim; the caches
+ * are [batch][kv_heads][max_seq][head_dim]; q / attention output are
+ * [batch * q_len][q_heads][head_dim].  state[0] is the number of tokens
+ * already in the cache (the position of the first new token), state[1] the
+ * number of generated tokens. */
+typedef struct spx_kv_params {
+  int32_t batch, q_len, q_heads, kv_heads, head_dim, max_seq;
+} spx_kv_params;
+/* RoPE (rotate-half, x * cos + rotate_half(x) * sin with the reference's
+ * [max_seq][head_dim] cos / sin tables, run_llama_spirv.py:87-97) on q and k,
+ * q written to q_out, k and v appended at positions state[0] + t. */
+int spx_op_rope_kv_append(spx_graph* g, const float* qkv, int64_t ld_qkv, const float* cos_table,
+                          const float* sin_table, const int32_t* state, float* q_out,
+                          float* k_cache, float* v_cache, const spx_kv_params* p);
+/* Causal grouped-query attention of the q_len new tokens over the cache
+ * (key j visible to the token at position state[0] + t when j <= that
+ * position); softmax(q k^T * scale) v per head.  head_dim must be 64. */
+int spx_op_attention_kv(spx_graph* g, const float* q, const float* k_cache, const float* v_cache,
+                        float* out, const int32_t* state, const spx_kv_params* p, float scale);
+/* Fused SwiGLU projection for m <= 8 rows: c[r][j] = silu(a[r] . w[j]) *
+ * (a[r] . w[j + f]) for j < f, w = [gate rows | up rows] x k (row stride
+ * ldw).  Returns SPX_ERR_INVALID_ARGUMENT for m > 8 (use spx_op_gemm +
+ * spx_op_swiglu_rows there). */
+int spx_op_swiglu_linear(spx_graph* g, const float* a, int64_t lda, const float* w, int64_t ldw,
+                         int32_t m, int32_t f, int32_t k, float* c, int64_t ldc);
+/* y[r][j] = silu(gu[r][j]) * gu[r][j + f], gu row stride ld. */
+int spx_op_swiglu_rows(spx_graph* g, const float* gu, int64_t ld, float* y, int64_t ldy,
+                       int32_t rows, int32_t f);
+/* Greedy bookkeeping: hist[state[1]][b] = ids[b] (when state[1] <
+ * hist_cap), then state[0] += advance and state[1] += 1. */
+int spx_op_token_commit(spx_graph* g, const int32_t* ids, int32_t* hist, int32_t* state,
+                        int32_t batch, int32_t advance, int32_t hist_cap);
+/* Vocab-parallel argmax: packed[r] = (max value, index + col_offset) of row
+ * r (first maximum wins), as two floats, the index as its int32 bits.
+ * argmax_merge picks, per row, the largest value over `parts` such arrays
+ * laid out [parts][rows] (ties: smallest index) into ids. */
+int spx_op_argmax_partial(spx_graph* g, const float* x, int64_t ldx, int32_t rows, int32_t cols,
+                          int32_t col_offset, float* packed);
+int spx_op_argmax_merge(spx_graph* g, const float* packed, int32_t parts, int32_t rows,
+                        int32_t* ids);
+
 /* Rank-4 constant pad (pad.comp with the reference's 13 push constants
  * od0..3, id0..3, pl0..3, total) and rank-4 permutation (transpose.comp's
  * 13 push constants in0..3, out0..3, p0..3, total). */

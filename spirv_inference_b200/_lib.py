@@ -62,6 +62,11 @@ class GemmParams(Structure):
                 + [("alpha", c_float), ("activation", c_int32)])
 
 
+class KvParams(Structure):
+    _fields_ = [(n, c_int32) for n in ("batch", "q_len", "q_heads", "kv_heads", "head_dim",
+                                       "max_seq")]
+
+
 class PoolParams(Structure):
     _fields_ = [(n, c_int32) for n in (
         "n", "ih", "iw", "c", "oh", "ow", "kh", "kw", "stride_h", "stride_w", "pad_top",
@@ -132,6 +137,18 @@ _SIGS = {
     "spx_op_embedding": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32], c_int),
     "spx_op_argmax_rows": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32], c_int),
     "spx_op_swiglu": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int64], c_int),
+    "spx_op_rope_kv_append": ([c_void_p, c_void_p, c_int64] + [c_void_p] * 6
+                              + [POINTER(KvParams)], c_int),
+    "spx_op_attention_kv": ([c_void_p] + [c_void_p] * 5 + [POINTER(KvParams), c_float], c_int),
+    "spx_op_swiglu_linear": ([c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32,
+                              c_int32, c_void_p, c_int64], c_int),
+    "spx_op_swiglu_rows": ([c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32],
+                           c_int),
+    "spx_op_token_commit": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32],
+                            c_int),
+    "spx_op_argmax_partial": ([c_void_p, c_void_p, c_int64, c_int32, c_int32, c_int32,
+                               c_void_p], c_int),
+    "spx_op_argmax_merge": ([c_void_p, c_void_p, c_int32, c_int32, c_void_p], c_int),
     "spx_op_pad4": ([c_void_p, c_void_p, c_void_p, c_float, _IP], c_int),
     "spx_op_transpose4": ([c_void_p, c_void_p, c_void_p, _IP], c_int),
 }

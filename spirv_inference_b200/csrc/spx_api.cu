@@ -82,6 +82,12 @@ int launch_gemm(cudaStream_t s, int64_t* cnt, const float* a, const float* b, co
   const bool single = p->batch == 1 && (p->batch_inner <= 1);
   const bool split = b_hi && b_lo;
   const float* bb = split ? b_hi : b;
+  // A handful of rows (decode, small-batch FC): stream the weights once on
+  // CUDA cores; a 128-row tensor-core tile would be almost all padding.
+  if (g_gemm_path == 0 && single && !split && p->a_ks == 1 && p->b_ks == 1 && c &&
+      p->c_ms >= p->n && gemm_rows_eligible(a, p->a_ms, b, p->b_ns, p->m, p->k))
+    return launch_gemm_rows(s, cnt, a, p->a_ms, b, p->b_ns, p->m, p->n, p->k, bias, res, c,
+                            p->c_ms, p->alpha, p->activation, 0);
   if (g_gemm_path != 1 && single && p->a_ks == 1 && p->b_ks == 1 &&
       gemm_tc_eligible(a, p->a_ms, bb, p->b_ns, p->m, p->n, p->k, c, p->c_ms) &&
       (!split || ((uintptr_t)b_lo & 15) == 0))
@@ -810,6 +816,63 @@ int spx_op_argmax_rows(spx_graph* g, const float* x, int32_t* idx, float* val, i
   SPX_G(g);
   if (!x || !idx) return fail(SPX_ERR_INVALID_ARGUMENT, "argmax: null");
   return launch_argmax_rows(g->stream, &g->launches, x, idx, val, rows, cols);
+}
+
+int spx_op_rope_kv_append(spx_graph* g, const float* qkv, int64_t ld_qkv, const float* cos_table,
+                          const float* sin_table, const int32_t* state, float* q_out,
+                          float* k_cache, float* v_cache, const spx_kv_params* p) {
+  SPX_G(g);
+  if (!qkv || !cos_table || !sin_table || !state || !q_out || !k_cache || !v_cache || !p)
+    return fail(SPX_ERR_INVALID_ARGUMENT, "rope_kv_append: null");
+  return launch_rope_kv_append(g->stream, &g->launches, qkv, ld_qkv, cos_table, sin_table, state,
+                               q_out, k_cache, v_cache, p->batch, p->q_len, p->q_heads,
+                               p->kv_heads, p->head_dim, p->max_seq);
+}
+
+int spx_op_attention_kv(spx_graph* g, const float* q, const float* k_cache, const float* v_cache,
+                        float* out, const int32_t* state, const spx_kv_params* p, float scale) {
+  SPX_G(g);
+  if (!q || !k_cache || !v_cache || !out || !state || !p)
+    return fail(SPX_ERR_INVALID_ARGUMENT, "attention_kv: null");
+  return launch_attention_kv(g->stream, &g->launches, q, k_cache, v_cache, out, state, p->batch,
+                             p->q_len, p->q_heads, p->kv_heads, p->head_dim, p->max_seq, scale);
+}
+
+int spx_op_swiglu_linear(spx_graph* g, const float* a, int64_t lda, const float* w, int64_t ldw,
+                         int32_t m, int32_t f, int32_t k, float* c, int64_t ldc) {
+  SPX_G(g);
+  if (!a || !w || !c) return fail(SPX_ERR_INVALID_ARGUMENT, "swiglu_linear: null");
+  if (f <= 0 || ldc < f) return fail(SPX_ERR_INVALID_ARGUMENT, "swiglu_linear: bad shape");
+  return launch_gemm_rows(g->stream, &g->launches, a, lda, w, ldw, m, f, k, nullptr, nullptr, c,
+                          ldc, 1.0f, SPX_ACT_NONE, (int64_t)f);
+}
+
+int spx_op_swiglu_rows(spx_graph* g, const float* gu, int64_t ld, float* y, int64_t ldy,
+                       int32_t rows, int32_t f) {
+  SPX_G(g);
+  if (!gu || !y) return fail(SPX_ERR_INVALID_ARGUMENT, "swiglu_rows: null");
+  return launch_swiglu_rows(g->stream, &g->launches, gu, ld, y, ldy, rows, f);
+}
+
+int spx_op_token_commit(spx_graph* g, const int32_t* ids, int32_t* hist, int32_t* state,
+                        int32_t batch, int32_t advance, int32_t hist_cap) {
+  SPX_G(g);
+  if (!ids || !hist || !state) return fail(SPX_ERR_INVALID_ARGUMENT, "token_commit: null");
+  return launch_token_commit(g->stream, &g->launches, ids, hist, state, batch, advance, hist_cap);
+}
+
+int spx_op_argmax_partial(spx_graph* g, const float* x, int64_t ldx, int32_t rows, int32_t cols,
+                          int32_t col_offset, float* packed) {
+  SPX_G(g);
+  if (!x || !packed) return fail(SPX_ERR_INVALID_ARGUMENT, "argmax_partial: null");
+  return launch_argmax_partial(g->stream, &g->launches, x, ldx, rows, cols, col_offset, packed);
+}
+
+int spx_op_argmax_merge(spx_graph* g, const float* packed, int32_t parts, int32_t rows,
+                        int32_t* ids) {
+  SPX_G(g);
+  if (!packed || !ids) return fail(SPX_ERR_INVALID_ARGUMENT, "argmax_merge: null");
+  return launch_argmax_merge(g->stream, &g->launches, packed, parts, rows, ids);
 }
 
 int spx_op_swiglu(spx_graph* g, const float* gate, const float* up, float* y, int64_t n) {

@@ -92,6 +92,20 @@ __device__ __forceinline__ void with_act(int act, F&& f) {
     default: f(ActTag<SPX_ACT_NONE>{}); break;
   }
 }
+// Host-side twin: picks the kernel instantiation for a runtime code.
+template <class F>
+inline void host_with_act(int act, F&& f) {
+  switch (act) {
+    case SPX_ACT_RELU: f(ActTag<SPX_ACT_RELU>{}); break;
+    case SPX_ACT_RELU6: f(ActTag<SPX_ACT_RELU6>{}); break;
+    case SPX_ACT_RELU_N1_TO_1: f(ActTag<SPX_ACT_RELU_N1_TO_1>{}); break;
+    case SPX_ACT_TANH: f(ActTag<SPX_ACT_TANH>{}); break;
+    case SPX_ACT_GELU_ERF: f(ActTag<SPX_ACT_GELU_ERF>{}); break;
+    case SPX_ACT_GELU_TANH: f(ActTag<SPX_ACT_GELU_TANH>{}); break;
+    case SPX_ACT_SILU: f(ActTag<SPX_ACT_SILU>{}); break;
+    default: f(ActTag<SPX_ACT_NONE>{}); break;
+  }
+}
 
 // ---- launchers (each returns SPX_OK or an error code) -------------------
 // All take the stream to record on and a launch counter (may be null).
@@ -130,6 +144,26 @@ int launch_argmax_rows(cudaStream_t s, int64_t* cnt, const float* x, int32_t* id
                        int rows, int cols);
 int launch_swiglu(cudaStream_t s, int64_t* cnt, const float* gate, const float* up, float* y,
                   int64_t n);
+// Decode path (k_decode.cu).
+bool gemm_rows_eligible(const float* a, int64_t lda, const float* w, int64_t ldw, int M, int K);
+int launch_gemm_rows(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, const float* w,
+                     int64_t ldw, int M, int N, int K, const float* bias, const float* res,
+                     float* c, int64_t ldc, float alpha, int act, int64_t pair_off);
+int launch_rope_kv_append(cudaStream_t s, int64_t* cnt, const float* qkv, int64_t ld_qkv,
+                          const float* cos_t, const float* sin_t, const int32_t* pos,
+                          float* q_out, float* kc, float* vc, int B, int T, int Hq, int Hkv,
+                          int D, int max_seq);
+int launch_attention_kv(cudaStream_t s, int64_t* cnt, const float* q, const float* kc,
+                        const float* vc, float* out, const int32_t* pos, int B, int T, int Hq,
+                        int Hkv, int D, int max_seq, float scale);
+int launch_token_commit(cudaStream_t s, int64_t* cnt, const int32_t* ids, int32_t* hist,
+                        int32_t* state, int B, int advance, int hist_cap);
+int launch_argmax_partial(cudaStream_t s, int64_t* cnt, const float* x, int64_t ldx, int rows,
+                          int cols, int col_offset, float* packed);
+int launch_argmax_merge(cudaStream_t s, int64_t* cnt, const float* packed, int parts, int rows,
+                        int32_t* ids);
+int launch_swiglu_rows(cudaStream_t s, int64_t* cnt, const float* gu, int64_t ld, float* y,
+                       int64_t ldy, int rows, int f);
 int launch_pad4(cudaStream_t s, int64_t* cnt, const float* x, float* y, float pad_value,
                 const int32_t* push);
 int launch_transpose4(cudaStream_t s, int64_t* cnt, const float* x, float* y,

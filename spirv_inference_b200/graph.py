@@ -266,6 +266,38 @@ class Graph:
     def swiglu(self, gate, up, y, n):
         check(self._l.spx_op_swiglu(self.h, self._p(gate), self._p(up), self._p(y), n))
 
+    # -- decode path -------------------------------------------------------
+    def rope_kv_append(self, qkv, ld_qkv, cos_t, sin_t, state, q_out, k_cache, v_cache, *,
+                       batch, q_len, q_heads, kv_heads, head_dim, max_seq):
+        p = _lib.KvParams(batch, q_len, q_heads, kv_heads, head_dim, max_seq)
+        check(self._l.spx_op_rope_kv_append(self.h, self._p(qkv), ld_qkv, self._p(cos_t),
+                                            self._p(sin_t), self._p(state), self._p(q_out),
+                                            self._p(k_cache), self._p(v_cache), ctypes.byref(p)))
+
+    def attention_kv(self, q, k_cache, v_cache, out, state, *, batch, q_len, q_heads, kv_heads,
+                     head_dim, max_seq, scale):
+        p = _lib.KvParams(batch, q_len, q_heads, kv_heads, head_dim, max_seq)
+        check(self._l.spx_op_attention_kv(self.h, self._p(q), self._p(k_cache), self._p(v_cache),
+                                          self._p(out), self._p(state), ctypes.byref(p), scale))
+
+    def swiglu_linear(self, a, lda, w, ldw, m, f, k, c, ldc):
+        check(self._l.spx_op_swiglu_linear(self.h, self._p(a), lda, self._p(w), ldw, m, f, k,
+                                           self._p(c), ldc))
+
+    def swiglu_rows(self, gu, ld, y, ldy, rows, f):
+        check(self._l.spx_op_swiglu_rows(self.h, self._p(gu), ld, self._p(y), ldy, rows, f))
+
+    def token_commit(self, ids, hist, state, batch, advance, hist_cap):
+        check(self._l.spx_op_token_commit(self.h, self._p(ids), self._p(hist), self._p(state),
+                                          batch, advance, hist_cap))
+
+    def argmax_partial(self, x, ldx, rows, cols, col_offset, packed):
+        check(self._l.spx_op_argmax_partial(self.h, self._p(x), ldx, rows, cols, col_offset,
+                                            self._p(packed)))
+
+    def argmax_merge(self, packed, parts, rows, ids):
+        check(self._l.spx_op_argmax_merge(self.h, self._p(packed), parts, rows, self._p(ids)))
+
     def pad4(self, x, y, pad_value, push):
         q = (ctypes.c_int32 * 13)(*push)
         check(self._l.spx_op_pad4(self.h, self._p(x), self._p(y), pad_value, q))
