@@ -41,8 +41,12 @@ METRICS = {
     "efficientnet_lite0": ("EfficientNet-Lite0 fp32 images/sec", "images/s"),
     "resnet50": ("ResNet-50 fp32 images/sec (HLO path)", "images/s"),
     "bert": ("BERT-base encoder fp32 sequences/sec (HLO path, seq 128)", "sequences/s"),
+    "tinyllama": ("TinyLlama-1.1B fp32 greedy tokens/sec (prompt 32, 20 new tokens, KV cache)",
+                  "tokens/s"),
 }
-DEFAULT_BATCH = {"mobilenet_v2": 256, "efficientnet_lite0": 64, "resnet50": 256, "bert": 32}
+DEFAULT_BATCH = {"mobilenet_v2": 256, "efficientnet_lite0": 64, "resnet50": 256, "bert": 32,
+                 "tinyllama": 1}
+LLAMA_PROMPT, LLAMA_NEW = 32, 20
 
 
 def build_model(name: str, batch: int, graph, seed_rank: int):
@@ -368,6 +372,237 @@ def run_spx(args) -> None:
     ex.close()
 
 
+# ---------------------------------------------------------------------------
+# TinyLlama decode: greedy generation of 20 tokens
+# after a 32-token prompt, batch 1 or 64, tensor-parallel over the N GPUs.
+
+def _llama_config(args, world) -> dict:
+    return {"workload": f"tinyllama 1.1B fp32 greedy decode, batch {args.batch}, prompt "
+                        f"{LLAMA_PROMPT}, {LLAMA_NEW} new tokens (1 prefill + "
+                        f"{LLAMA_NEW - 1} cached decode steps)",
+            "global_batch": args.batch, "seq_len": LLAMA_PROMPT + LLAMA_NEW - 1,
+            "parallelism": f"tp{world}" + (" (NCCL all-reduce x2 per layer)" if world > 1 else ""),
+            "l2": "weights (4.4 GB / tp degree) larger than L2: every step streams them",
+            "cuda_graph": world == 1}
+
+
+def _llama_weights():
+    from spirv_inference_b200 import llama
+    return llama.make_weights(llama.TINYLLAMA, seed=0, generator="torch")
+
+
+def llama_cpu_step(W, batch: int = 1, n_tokens: int = 1):
+    """The reference's decode loop on the CPU (oracle/llama_ref.generate_full:
+    full 64-position re-computation per token), numpy / BLAS on all host
+    cores.  One call generates `n_tokens` tokens for each of `batch` prompts."""
+    from oracle import llama_ref
+    from spirv_inference_b200 import llama
+    cfg = llama.TINYLLAMA
+    rope = llama.rope_tables(cfg, cfg.max_seq)
+    prompt = llama.make_prompt(cfg, batch, LLAMA_PROMPT, seed=4321)
+    return lambda: [llama_ref.generate_full(cfg, W, prompt[b], n_tokens, rope)
+                    for b in range(batch)]
+
+
+def llama_cpu_baseline(W, seconds: float) -> dict:
+    step = llama_cpu_step(W, 1, 1)
+    n, t0 = 0, time.perf_counter()
+    while n < 1 or (time.perf_counter() - t0) < seconds:
+        step()
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n} greedy token(s) of one sequence through the reference's decode loop "
+                      f"(full 64-position llama_step per token, numpy fp32 BLAS; {dt:.1f} s)"}
+
+
+def run_llama_reference(args) -> None:
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    W = _llama_weights()
+    step = llama_cpu_step(W, 1, 1)
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    UNIT_ = METRICS["tinyllama"][1]
+    print(json.dumps({
+        "impl": "reference", "metric": METRICS["tinyllama"][0], "value": v, "unit": UNIT_,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000 * dt / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded uniform prompt ids, seeded N(0,0.02) weights)",
+        "config": _llama_config(args, world),
+        "cpu_baseline": {"value": v, "unit": UNIT_, "cores": os.cpu_count(), "kind": "port",
+                         "sample": "1 greedy token of one sequence per step through the "
+                                   "reference's decode loop (full 64-position re-computation, "
+                                   "numpy fp32 BLAS)"},
+        "e2e": {"value": v, "unit": UNIT_, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_llama_spx(args) -> None:
+    import torch
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    from spirv_inference_b200 import llama
+    from spirv_inference_b200.sharding import max_over_ranks as _mor
+
+    B = args.batch
+    METRIC_, UNIT_ = METRICS["tinyllama"]
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    W = _llama_weights()
+    dec = llama.LlamaDecoder(llama.TINYLLAMA, W, B, LLAMA_PROMPT, LLAMA_NEW, device=local,
+                             stream=stream.cuda_stream, rank=rank, world=world)
+    prompt = llama.make_prompt(llama.TINYLLAMA, B, LLAMA_PROMPT, seed=4321)
+    dec.upload_prompt(prompt)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        dec.run()
+    barrier()
+    g = dec.g
+    g.reset_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            dec.run()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = g.launch_count
+    ms = _mor(e0.elapsed_time(e1), device="cuda") / args.steps
+    barrier()
+    value = B * LLAMA_NEW / (ms / 1e3)
+    toks = dec.tokens()
+
+    # Per-op timing of one eager prefill + decode step (events between ops).
+    marks = []
+
+    def mark(label, nbytes, flops):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        marks.append((label, nbytes, flops, ev))
+
+    cap = dec.capture
+    dec.capture = False
+    decode_classes: dict[str, dict] = {}
+    prefill_ms = decode_ms = 0.0
+    for phase in ("prefill", "decode"):
+        marks.clear()
+        start = torch.cuda.Event(enable_timing=True)
+        if phase == "prefill":
+            dec.g.zero(dec.state)
+            dec._host_pos = 0
+            start.record(stream)
+            dec._mark = mark
+            dec._forward(dec.prompt_ids, LLAMA_PROMPT)
+        else:
+            for _ in range(8):          # decode at a mid-sequence position
+                dec._forward(dec.ids, 1)
+            start.record(stream)
+            dec._mark = mark
+            dec._forward(dec.ids, 1)
+        dec._mark = None
+        torch.cuda.synchronize()
+        prev = start
+        for label, nb, fl, ev in marks:
+            t = prev.elapsed_time(ev)
+            prev = ev
+            if phase == "decode":
+                d = decode_classes.setdefault(label, {"ms": 0.0, "bytes": 0.0, "flops": 0.0,
+                                                      "launches": 0})
+                d["ms"] += t
+                d["bytes"] += nb
+                d["flops"] += fl
+                d["launches"] += 1
+        total = start.elapsed_time(marks[-1][3])
+        if phase == "prefill":
+            prefill_ms = total
+        else:
+            decode_ms = total
+    dec.capture = cap
+    peaks = _peaks()
+    lin = decode_classes["linear"]
+    per_launch_bytes = lin["bytes"] / lin["launches"]
+    ach = lin["bytes"] / (lin["ms"] / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None,
+                "kernel": "linear (gemm_rows / swiglu_linear at batch <= 8, tensor-core GEMM "
+                          "above) in one eager decode step",
+                "bytes_per_launch": round(per_launch_bytes),
+                "peak_source": peaks["source"],
+                "note": "achieved = algorithmic bytes (weights + activations) per launch / "
+                        "CUDA-event time, averaged over the step's projection launches"}
+    per_class = {k: {"ms": round(d["ms"], 4), "launches": d["launches"],
+                     "share": round(d["ms"] / decode_ms, 4),
+                     "achieved_gbs": round(d["bytes"] / (d["ms"] / 1e3) / 1e9, 1)}
+                 for k, d in sorted(decode_classes.items(), key=lambda kv: -kv[1]["ms"])}
+    step_bytes = sum(d["bytes"] for d in decode_classes.values())
+
+    # End to end through the public API: pinned prompt upload, generation,
+    # token download, every step.
+    host_prompt = torch.from_numpy(prompt.copy()).pin_memory()
+    host_tok = torch.empty((LLAMA_NEW, B), dtype=torch.int32).pin_memory()
+
+    def e2e_step():
+        g.upload_async(dec.prompt_ids, host_prompt.data_ptr(), prompt.nbytes)
+        dec.run()
+        g.download_async(host_tok.data_ptr(), dec.hist, host_tok.numel() * 4)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = _mor(e0.elapsed_time(e1), device="cuda") / args.steps
+    barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC_, "value": round(value, 2), "unit": UNIT_, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded uniform prompt ids, seeded N(0,0.02) weights)",
+            "config": _llama_config(args, world),
+            "e2e": {"value": round(B * LLAMA_NEW / (e2e_ms / 1e3), 2), "unit": UNIT_,
+                    "h2d_bytes_per_step": int(prompt.nbytes),
+                    "d2h_bytes_per_step": int(host_tok.numel() * 4),
+                    "ms_per_step": round(e2e_ms, 4)},
+            "roofline": roofline,
+            "prefill_ms": round(prefill_ms, 4), "decode_step_ms_eager": round(decode_ms, 4),
+            "decode_step_bytes": round(step_bytes),
+            "decode_step_roofline_ms": round(step_bytes / (peaks["hbm_gbs"] * 1e9) * 1e3, 4),
+            "per_kernel_class_decode": per_class,
+            "gpu_launches": int(launches),
+            "tokens_first_sequence": toks[0].tolist(),
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = llama_cpu_baseline(W, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    dec.close()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -382,7 +617,9 @@ def main():
     args = ap.parse_args()
     if args.batch is None:
         args.batch = DEFAULT_BATCH[args.model]
-    if args.impl == "reference":
+    if args.model == "tinyllama":
+        run_llama_reference(args) if args.impl == "reference" else run_llama_spx(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_spx(args)

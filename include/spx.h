@@ -306,7 +306,8 @@ int spx_op_reduce_rank4(spx_graph* g, const float* x, float* y, const int32_t pu
 int spx_op_layernorm(spx_graph* g, const float* x, const float* residual, float* x_out,
                      const float* gamma, const float* beta, float* y, int32_t rows,
                      int32_t cols, float eps);
-/* Row RMSNorm: y = x / sqrt(mean(x^2) + eps) * gamma. */
+/* Row RMSNorm: y = x / sqrt(mean(x^2) + eps) * gamma (gamma may be NULL:
+ * no gain). */
 int spx_op_rmsnorm(spx_graph* g, const float* x, const float* gamma, float* y, int32_t rows,
                    int32_t cols, float eps);
 /* Rotary embedding (rotate-half form) in place on [tokens][heads][head_dim];
@@ -350,19 +351,31 @@ int spx_op_rope_kv_append(spx_graph* g, const float* qkv, int64_t ld_qkv, const 
  * position); softmax(q k^T * scale) v per head.  head_dim must be 64. */
 int spx_op_attention_kv(spx_graph* g, const float* q, const float* k_cache, const float* v_cache,
                         float* out, const int32_t* state, const spx_kv_params* p, float scale);
-/* Fused SwiGLU projection for m <= 8 rows: c[r][j] = silu(a[r] . w[j]) *
- * (a[r] . w[j + f]) for j < f, w = [gate rows | up rows] x k (row stride
- * ldw).  Returns SPX_ERR_INVALID_ARGUMENT for m > 8 (use spx_op_gemm +
+/* Fused SwiGLU projection for m <= 8 rows: c[r][j] = silu(a'[r] . w[j]) *
+ * (a'[r] . w[j + f]) for j < f, w = [gate rows | up rows] x k (row stride
+ * ldw).  a' = a, or with rms_eps >= 0 the gain-free RMSNorm of a
+ * (a / sqrt(mean(a^2) + rms_eps); fold the norm's gain into w).  Returns
+ * SPX_ERR_INVALID_ARGUMENT for m > 8 (use spx_op_rmsnorm + spx_op_gemm +
  * spx_op_swiglu_rows there). */
 int spx_op_swiglu_linear(spx_graph* g, const float* a, int64_t lda, const float* w, int64_t ldw,
-                         int32_t m, int32_t f, int32_t k, float* c, int64_t ldc);
+                         int32_t m, int32_t f, int32_t k, float rms_eps, float* c, int64_t ldc);
+/* c[r][j] = x'[r] . w[j] (+ residual[r][j]) for m <= 8 rows, x' the
+ * gain-free RMSNorm of x when rms_eps >= 0 (x itself otherwise).  With
+ * argmax_keys (m zero-initialised 64-bit keys) each row's greedy argmax is
+ * folded in: keys[r] = max over j of (order-preserving bits of c[r][j],
+ * ~j), so the largest value wins and ties go to the smallest j;
+ * spx_op_token_commit decodes and resets them. */
+int spx_op_rms_linear(spx_graph* g, const float* x, int64_t ldx, const float* w, int64_t ldw,
+                      int32_t m, int32_t n, int32_t k, float rms_eps, const float* residual,
+                      float* c, int64_t ldc, uint64_t* argmax_keys);
 /* y[r][j] = silu(gu[r][j]) * gu[r][j + f], gu row stride ld. */
 int spx_op_swiglu_rows(spx_graph* g, const float* gu, int64_t ld, float* y, int64_t ldy,
                        int32_t rows, int32_t f);
-/* Greedy bookkeeping: hist[state[1]][b] = ids[b] (when state[1] <
- * hist_cap), then state[0] += advance and state[1] += 1. */
-int spx_op_token_commit(spx_graph* g, const int32_t* ids, int32_t* hist, int32_t* state,
-                        int32_t batch, int32_t advance, int32_t hist_cap);
+/* Greedy bookkeeping: (with argmax_keys: ids[b] = the column of keys[b],
+ * keys[b] = 0), hist[state[1]][b] = ids[b] (when state[1] < hist_cap),
+ * then state[0] += advance and state[1] += 1. */
+int spx_op_token_commit(spx_graph* g, int32_t* ids, int32_t* hist, int32_t* state,
+                        int32_t batch, int32_t advance, int32_t hist_cap, uint64_t* argmax_keys);
 /* Vocab-parallel argmax: packed[r] = (max value, index + col_offset) of row
  * r (first maximum wins), as two floats, the index as its int32 bits.
  * argmax_merge picks, per row, the largest value over `parts` such arrays

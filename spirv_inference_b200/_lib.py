@@ -141,11 +141,13 @@ _SIGS = {
                               + [POINTER(KvParams)], c_int),
     "spx_op_attention_kv": ([c_void_p] + [c_void_p] * 5 + [POINTER(KvParams), c_float], c_int),
     "spx_op_swiglu_linear": ([c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32,
-                              c_int32, c_void_p, c_int64], c_int),
+                              c_int32, c_float, c_void_p, c_int64], c_int),
+    "spx_op_rms_linear": ([c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32,
+                           c_int32, c_float, c_void_p, c_void_p, c_int64, c_void_p], c_int),
     "spx_op_swiglu_rows": ([c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32],
                            c_int),
-    "spx_op_token_commit": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32],
-                            c_int),
+    "spx_op_token_commit": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
+                             c_void_p], c_int),
     "spx_op_argmax_partial": ([c_void_p, c_void_p, c_int64, c_int32, c_int32, c_int32,
                                c_void_p], c_int),
     "spx_op_argmax_merge": ([c_void_p, c_void_p, c_int32, c_int32, c_void_p], c_int),

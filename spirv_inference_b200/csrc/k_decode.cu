@@ -47,17 +47,20 @@ template <int MR, bool PAIR, int A>
 __global__ void __launch_bounds__(kRowsWarps * 32) gemm_rows_kernel(
     const float* __restrict__ a, int64_t lda, const float* __restrict__ w, int64_t ldw, int M,
     int N, int K, const float* __restrict__ bias, const float* __restrict__ res, float* c,
-    int64_t ldc, float alpha, int64_t pair_off) {
+    int64_t ldc, float alpha, int64_t pair_off, float rms_eps,
+    unsigned long long* __restrict__ amax) {
   const int lane = threadIdx.x & 31;
   const int n = blockIdx.x * kRowsWarps + (threadIdx.x >> 5);
   if (n >= N) return;
   const int k4 = K >> 2;
   const float4* wr = reinterpret_cast<const float4*>(w + (int64_t)n * ldw);
   const float4* wu = reinterpret_cast<const float4*>(w + ((int64_t)n + pair_off) * ldw);
-  float acc[MR], accu[PAIR ? MR : 1];
+  const bool rms = rms_eps >= 0.0f;
+  float acc[MR], accu[PAIR ? MR : 1], ss[MR];
 #pragma unroll
   for (int m = 0; m < MR; ++m) {
     acc[m] = 0.0f;
+    ss[m] = 0.0f;
     if constexpr (PAIR) accu[m] = 0.0f;
   }
   for (int i0 = lane; i0 < k4; i0 += 32 * kRowsUnroll) {
@@ -78,6 +81,7 @@ __global__ void __launch_bounds__(kRowsWarps * 32) gemm_rows_kernel(
             const float4 av = __ldg(reinterpret_cast<const float4*>(a + m * lda) + i);
             acc[m] = dot4(av, wv[j], acc[m]);
             if constexpr (PAIR) accu[m] = dot4(av, uv[j], accu[m]);
+            if (rms) ss[m] = dot4(av, av, ss[m]);
           }
         }
       }
@@ -87,6 +91,13 @@ __global__ void __launch_bounds__(kRowsWarps * 32) gemm_rows_kernel(
   for (int m = 0; m < MR; ++m) {
     acc[m] = warp_sum32(acc[m]);
     if constexpr (PAIR) accu[m] = warp_sum32(accu[m]);
+    if (rms) {
+      // RMSNorm of the A row folded in: (x / rms(x)) . w = (x . w) / rms(x)
+      // (the norm's gain is folded into the weights by the caller).
+      const float inv = 1.0f / sqrtf(warp_sum32(ss[m]) / (float)K + rms_eps);
+      acc[m] *= inv;
+      if constexpr (PAIR) accu[m] *= inv;
+    }
   }
   // Lane m writes row m.
 #pragma unroll
@@ -103,6 +114,14 @@ __global__ void __launch_bounds__(kRowsWarps * 32) gemm_rows_kernel(
         v = act_c<A>(v);
       }
       c[(int64_t)m * ldc + n] = v;
+      if (amax) {
+        // Greedy argmax fused into the lm_head: one 64-bit key per row,
+        // (order-preserving bits of v, ~n), so atomicMax keeps the largest
+        // value and, among equal values, the smallest column.
+        const uint32_t u = __float_as_uint(v);
+        const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+        atomicMax(amax + m, ((unsigned long long)ord << 32) | (0xFFFFFFFFu - (uint32_t)n));
+      }
     }
   }
 }
@@ -261,11 +280,19 @@ __global__ void __launch_bounds__(kAttWarps * 32) attention_kv_kernel(
 
 // ---------------------------------------------------------------------------
 // state[0] = position (tokens in the cache), state[1] = generated count.
-__global__ void token_commit_kernel(const int32_t* __restrict__ ids, int32_t* __restrict__ hist,
-                                    int32_t* state, int B, int advance, int hist_cap) {
+// With `keys` (fused lm_head argmax), ids[b] is decoded from keys[b] first
+// and the key is reset for the next step.
+__global__ void token_commit_kernel(int32_t* __restrict__ ids, int32_t* __restrict__ hist,
+                                    int32_t* state, int B, int advance, int hist_cap,
+                                    unsigned long long* __restrict__ keys) {
   const int step = state[1];
-  for (int b = threadIdx.x; b < B; b += blockDim.x)
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    if (keys) {
+      ids[b] = (int32_t)(0xFFFFFFFFu - (uint32_t)(keys[b] & 0xFFFFFFFFull));
+      keys[b] = 0ull;
+    }
     if (step < hist_cap) hist[(int64_t)step * B + b] = ids[b];
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
     state[0] += advance;
@@ -342,16 +369,17 @@ __global__ void swiglu_rows_kernel(const float* __restrict__ gu, int64_t ld, flo
 template <int MR, bool PAIR>
 void rows_launch(cudaStream_t s, int act, const float* a, int64_t lda, const float* w,
                  int64_t ldw, int M, int N, int K, const float* bias, const float* res, float* c,
-                 int64_t ldc, float alpha, int64_t pair_off) {
+                 int64_t ldc, float alpha, int64_t pair_off, float rms_eps,
+                 unsigned long long* amax) {
   const int grid = (N + kRowsWarps - 1) / kRowsWarps;
   if constexpr (PAIR) {
     gemm_rows_kernel<MR, true, SPX_ACT_NONE><<<grid, kRowsWarps * 32, 0, s>>>(
-        a, lda, w, ldw, M, N, K, bias, res, c, ldc, alpha, pair_off);
+        a, lda, w, ldw, M, N, K, bias, res, c, ldc, alpha, pair_off, rms_eps, nullptr);
   } else {
     host_with_act(act, [&](auto tag) {
       constexpr int A = decltype(tag)::value;
       gemm_rows_kernel<MR, false, A><<<grid, kRowsWarps * 32, 0, s>>>(
-          a, lda, w, ldw, M, N, K, bias, res, c, ldc, alpha, pair_off);
+          a, lda, w, ldw, M, N, K, bias, res, c, ldc, alpha, pair_off, rms_eps, amax);
     });
   }
 }
@@ -367,7 +395,8 @@ bool gemm_rows_eligible(const float* a, int64_t lda, const float* w, int64_t ldw
 
 int launch_gemm_rows(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, const float* w,
                      int64_t ldw, int M, int N, int K, const float* bias, const float* res,
-                     float* c, int64_t ldc, float alpha, int act, int64_t pair_off) {
+                     float* c, int64_t ldc, float alpha, int act, int64_t pair_off,
+                     float rms_eps, unsigned long long* amax) {
   if (!gemm_rows_eligible(a, lda, w, ldw, M, K) || N <= 0)
     return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_rows: operands not eligible");
   const bool pair = pair_off > 0;
@@ -375,9 +404,9 @@ int launch_gemm_rows(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, 
   const int mr = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
 #define SPX_ROWS(MRV)                                                                          \
   (pair ? rows_launch<MRV, true>(s, act, a, lda, w, ldw, M, N, K, bias, res, c, ldc, alpha,    \
-                                 pair_off)                                                     \
+                                 pair_off, rms_eps, nullptr)                                   \
         : rows_launch<MRV, false>(s, act, a, lda, w, ldw, M, N, K, bias, res, c, ldc, alpha,   \
-                                  pair_off))
+                                  pair_off, rms_eps, amax))
   switch (mr) {
     case 1: SPX_ROWS(1); break;
     case 2: SPX_ROWS(2); break;
@@ -434,10 +463,11 @@ int launch_attention_kv(cudaStream_t s, int64_t* cnt, const float* q, const floa
   return after_launch(cnt, "attention_kv");
 }
 
-int launch_token_commit(cudaStream_t s, int64_t* cnt, const int32_t* ids, int32_t* hist,
-                        int32_t* state, int B, int advance, int hist_cap) {
+int launch_token_commit(cudaStream_t s, int64_t* cnt, int32_t* ids, int32_t* hist,
+                        int32_t* state, int B, int advance, int hist_cap,
+                        unsigned long long* keys) {
   if (B <= 0 || hist_cap <= 0) return fail(SPX_ERR_INVALID_ARGUMENT, "token_commit: bad shape");
-  token_commit_kernel<<<1, 256, 0, s>>>(ids, hist, state, B, advance, hist_cap);
+  token_commit_kernel<<<1, 256, 0, s>>>(ids, hist, state, B, advance, hist_cap, keys);
   return after_launch(cnt, "token_commit");
 }
 

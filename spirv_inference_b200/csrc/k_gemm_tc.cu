@@ -567,6 +567,238 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ===========================================================================
+// Few-row GEMM on tensor cores, operands swapped: C[m][n] for M <= 128 rows
+// (decode / small-batch linear layers) computed as D[n][m] = W[n][:] . X[m][:]
+// so the 128-row UMMA M dimension runs over the weight rows and the batch is
+// the UMMA N dimension (16..128).  Weights stream through the CTA exactly
+// once; the k range is split over a thread-block cluster along grid.y and the
+// partial tiles are summed through distributed shared memory (fixed order,
+// deterministic), each CTA of the cluster reducing and storing its share of
+// the batch rows.
+//   warps 0-3  converters (split W and X tiles to hi / lo), then epilogue:
+//              TMEM lanes = weight rows -> partial tile red[m][128] in smem
+//   warp 4     TMA producer (W box 128 x 32, X box Mp x 32)
+//   warp 5     TMEM owner, MMA issuer
+constexpr int kSkThreads = 192;
+constexpr int kSkProducer = 4;
+constexpr int kSkMma = 5;
+
+struct SkArgs {
+  int M, N, K, Mp, k_blocks, kb_per_split, splits, stages;
+  uint32_t idesc, tmem_cols, stage_bytes, x_bytes;
+  const float* bias;
+  const float* res;
+  float* c;
+  int64_t ldc;
+  float alpha;
+  int act;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of `local`'s twin in the shared memory of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t peer_addr(const void* local, uint32_t rank) {
+  uint32_t a;
+  asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(su32(local)), "r"(rank));
+  return a;
+}
+// Plain (non-volatile) loads so a thread's loads from the peers overlap;
+// ordering against the peers' writes comes from the cluster barrier.
+__device__ __forceinline__ float ld_cluster(uint32_t addr) {
+  float v;
+  asm("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+
+__global__ void __launch_bounds__(kSkThreads)
+    gemm_tc_skinny_kernel(const __grid_constant__ CUtensorMap tmW,
+                          const __grid_constant__ CUtensorMap tmX, const SkArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int S = p.stages;
+  uint64_t* full = (uint64_t*)(smem + (size_t)S * p.stage_bytes);
+  uint64_t* conv = full + kMaxStages;
+  uint64_t* empty = conv + kMaxStages;
+  uint64_t* tfull = empty + kMaxStages;
+  uint64_t* drain = tfull + 1;
+  uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  float* red = reinterpret_cast<float*>(smem);  // [Mp][128] partial, after the k-loop
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = blockIdx.x;
+  const int split = (int)cluster_rank();
+  const int kb0 = split * p.kb_per_split;
+  const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+  const int nkb = kb1 > kb0 ? kb1 - kb0 : 0;
+  const uint32_t w_bytes = kATileBytes;  // 128 rows x 32 fp32
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      bar_init(&full[s], 1);
+      bar_init(&conv[s], 128);
+      bar_init(&empty[s], 1);
+    }
+    bar_init(tfull, 1);
+    bar_init(drain, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kSkMma) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     su32(tmem_slot)),
+                 "r"(p.tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool have_acc = false;
+
+  if (warp == kSkProducer) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0, armed = 0, armed_par = 0;
+      for (int i = 0; i < nkb; ++i) {
+        if (!bar_wait(&empty[s], ph ^ 1, abort_flag, kTimeoutNs, 64)) break;
+        uint8_t* st = smem + (size_t)s * p.stage_bytes;
+        bar_expect_tx(&full[s], w_bytes + p.x_bytes);
+        tma_load_2d(st, &tmW, &full[s], (kb0 + i) * kBK, nt * kBM);
+        tma_load_2d(st + 2 * w_bytes, &tmX, &full[s], (kb0 + i) * kBK, 0);
+        armed |= 1u << s;
+        armed_par = (armed_par & ~(1u << s)) | (ph << s);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+      if (*abort_flag) {
+        for (int i = 0; i < S; ++i)
+          if (armed & (1u << i)) {
+            volatile int never = 0;
+            bar_wait(&full[i], (armed_par >> i) & 1, &never, kDrainNs);
+          }
+      }
+    }
+  } else if (warp == kSkMma) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      bool issued = false;
+      for (int i = 0; i < nkb; ++i) {
+        if (!bar_wait(&conv[s], ph, abort_flag, kTimeoutNs, 64)) break;
+        tc_fence_after();
+        const uint32_t w_hi = su32(smem + (size_t)s * p.stage_bytes);
+        const uint32_t w_lo = w_hi + w_bytes;
+        const uint32_t x_hi = w_hi + 2 * w_bytes;
+        const uint32_t x_lo = x_hi + p.x_bytes;
+#pragma unroll
+        for (int k = 0; k < kBK / 8; ++k) {
+          const uint32_t off = k * 32;
+          const uint64_t dwh = sdesc(w_hi + off), dwl = sdesc(w_lo + off);
+          const uint64_t dxh = sdesc(x_hi + off), dxl = sdesc(x_lo + off);
+          umma_tf32(tmem, dwl, dxh, p.idesc, (i | k) ? 1u : 0u);
+          umma_tf32(tmem, dwh, dxl, p.idesc, 1u);
+          umma_tf32(tmem, dwh, dxh, p.idesc, 1u);
+        }
+        issued = true;
+        umma_commit(&empty[s]);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+      if (issued) umma_commit(tfull);
+      if (*abort_flag && issued) {
+        umma_commit(drain);
+        volatile int never = 0;
+        bar_wait(drain, 0, &never, kDrainNs);
+      }
+    }
+  } else {
+    // converters, then the TMEM -> smem partial
+    const int ct = threadIdx.x;
+    int s = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    for (int i = 0; i < nkb && ok; ++i) {
+      ok = bar_wait(&full[s], ph, abort_flag, kTimeoutNs, 256);
+      if (!ok) break;
+      uint8_t* st = smem + (size_t)s * p.stage_bytes;
+      split_buffer((float4*)st, (float4*)(st + w_bytes), w_bytes / 16, ct, 128);
+      split_buffer((float4*)(st + 2 * w_bytes), (float4*)(st + 2 * w_bytes + p.x_bytes),
+                   p.x_bytes / 16, ct, 128);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      bar_arrive(&conv[s]);
+      if (++s == S) {
+        s = 0;
+        ph ^= 1;
+      }
+    }
+    if (nkb > 0) ok = bar_wait(tfull, 0, abort_flag, kTimeoutNs, 128) && ok;
+    have_acc = nkb > 0 && ok;
+    // Every lane of the warp takes the same branch only when all agree.
+    have_acc = __all_sync(0xffffffffu, have_acc);
+    tc_fence_after();
+    const int row = warp * 32 + lane;  // weight row within the tile
+    for (int c0 = 0; c0 < p.Mp; c0 += 32) {
+      float v[32];
+      if (have_acc) {
+        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c0 + j < p.Mp) red[(c0 + j) * kBM + row] = v[j];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // every partial of the cluster is in shared memory
+  if (threadIdx.x < 128) {
+    const int row = threadIdx.x;
+    const int n = nt * kBM + row;
+    if (n < p.N) {
+      const float b = p.bias ? p.bias[n] : 0.0f;
+      with_act(p.act, [&](auto tag) {
+        constexpr int A = decltype(tag)::value;
+        uint32_t base[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          base[q] = q < p.splits ? peer_addr(red + row, (uint32_t)q) : 0u;
+        for (int m = split; m < p.M; m += p.splits) {
+          float part[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            part[q] = q < p.splits ? ld_cluster(base[q] + (uint32_t)(m * kBM * 4)) : 0.0f;
+          float acc = 0.0f;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc += part[q];  // fixed order: deterministic
+          float v = acc * p.alpha + b;
+          if (p.res) v += p.res[(int64_t)m * p.ldc + n];
+          p.c[(int64_t)m * p.ldc + n] = act_c<A>(v);
+        }
+      });
+    }
+  }
+  cluster_sync_all();  // peers finished reading this CTA's partial
+  if (warp == kSkMma) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(p.tmem_cols));
+  }
+}
+
 // Pre-splits weights once at load: hi = rna_tf32(w), lo = rna_tf32(w - hi).
 __global__ void weights_split_kernel(const float* __restrict__ w, float* __restrict__ hi,
                                      float* __restrict__ lo, int64_t n) {
@@ -707,6 +939,78 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   const int grid = tiles < sm_count() ? tiles : sm_count();
   gemm_tc_kernel<<<grid, kThreads, smem, s>>>(ma, mb, mblo, mc, mr, p);
   return after_launch(cnt, "gemm_tc");
+}
+
+bool gemm_tc_skinny_eligible(const float* a, int64_t lda, const float* w, int64_t ldw, int M,
+                             int N, int K) {
+  auto al16 = [](const void* q) { return ((uintptr_t)q & 15) == 0; };
+  return M >= 1 && M <= 128 && N > 0 && K > 0 && K % 4 == 0 && lda % 4 == 0 && ldw % 4 == 0 &&
+         lda >= K && ldw >= K && al16(a) && al16(w);
+}
+
+int launch_gemm_tc_skinny(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda,
+                          const float* w, int64_t ldw, int M, int N, int K, const float* bias,
+                          const float* res, float* c, int64_t ldc, float alpha, int act) {
+  if (!gemm_tc_skinny_eligible(a, lda, w, ldw, M, N, K) || ldc < N || !c)
+    return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_tc_skinny: operands not eligible");
+  SkArgs p = {};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.Mp = (M + 15) / 16 * 16;
+  p.k_blocks = (K + kBK - 1) / kBK;
+  const int tiles = (N + kBM - 1) / kBM;
+  // Two CTAs per SM; split k over a cluster until the grid fills them.
+  int splits = (2 * sm_count()) / tiles;
+  if (splits > 8) splits = 8;
+  if (splits > p.k_blocks) splits = p.k_blocks;
+  if (splits < 1) splits = 1;
+  p.kb_per_split = (p.k_blocks + splits - 1) / splits;
+  p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
+  p.x_bytes = (uint32_t)p.Mp * kBK * 4;
+  p.stage_bytes = 2 * kATileBytes + 2 * p.x_bytes;
+  p.stages = p.Mp <= 64 ? 2 : 3;
+  uint32_t cols = 32;
+  while (cols < (uint32_t)p.Mp) cols <<= 1;
+  p.tmem_cols = cols;
+  p.idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(p.Mp >> 3) << 17) |
+            ((uint32_t)(kBM >> 4) << 24);
+  p.bias = bias;
+  p.res = res;
+  p.c = c;
+  p.ldc = ldc;
+  p.alpha = alpha;
+  p.act = act;
+  CUtensorMap mw, mx;
+  int rc;
+  if ((rc = make_map(&mw, w, N, K, ldw, kBM))) return rc;
+  if ((rc = make_map(&mx, a, M, K, lda, p.Mp))) return rc;
+  size_t smem = 1024 + (size_t)p.stages * p.stage_bytes + 256;
+  const size_t red_bytes = (size_t)p.Mp * kBM * 4;
+  if (red_bytes > (size_t)p.stages * p.stage_bytes)
+    return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_tc_skinny: partial tile does not fit");
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(gemm_tc_skinny_kernel,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  });
+  if (attr_err != cudaSuccess) return check_cuda(attr_err, "gemm_tc_skinny: smem attribute");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles, p.splits, 1);
+  cfg.blockDim = dim3(kSkThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = p.splits;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_skinny_kernel, mw, mx, p);
+  if (e != cudaSuccess) return check_cuda(e, "gemm_tc_skinny launch");
+  return after_launch(cnt, "gemm_tc_skinny");
 }
 
 int launch_weights_split(cudaStream_t s, int64_t* cnt, const float* w, float* hi, float* lo,

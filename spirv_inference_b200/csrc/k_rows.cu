@@ -77,17 +77,48 @@ __global__ void layernorm_kernel(const float* __restrict__ x, const float* __res
   }
 }
 
-// RMSNorm (Llama): x / sqrt(mean(x^2) + eps) * gamma.
-__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
-                               float* __restrict__ y, int rows, int cols, float eps) {
-  const int lane = threadIdx.x & 31;
-  const int wpb = blockDim.x >> 5;
-  for (int r = blockIdx.x * wpb + (threadIdx.x >> 5); r < rows; r += gridDim.x * wpb) {
+// RMSNorm (Llama): x / sqrt(mean(x^2) + eps) * gamma (gamma optional).
+// One 256-thread block per row; 16-byte accesses when the row allows.
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x,
+                                                      const float* __restrict__ gamma,
+                                                      float* __restrict__ y, int rows, int cols,
+                                                      float eps) {
+  __shared__ float part[8];
+  const bool vec = (cols & 3) == 0 && (((uintptr_t)x | (uintptr_t)y |
+                                        (gamma ? (uintptr_t)gamma : 0)) & 15) == 0;
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* xr = x + (int64_t)r * cols;
+    float* yr = y + (int64_t)r * cols;
     float q = 0.0f;
-    for (int j = lane; j < cols; j += 32) q += xr[j] * xr[j];
-    float inv = 1.0f / sqrtf(warp_sum(q) / (float)cols + eps);
-    for (int j = lane; j < cols; j += 32) y[(int64_t)r * cols + j] = gamma[j] * (xr[j] * inv);
+    if (vec) {
+      for (int j = threadIdx.x; j < cols / 4; j += blockDim.x) {
+        const float4 v = reinterpret_cast<const float4*>(xr)[j];
+        q += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+    } else {
+      for (int j = threadIdx.x; j < cols; j += blockDim.x) q += xr[j] * xr[j];
+    }
+    q = warp_sum(q);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = q;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += part[w];
+    const float inv = 1.0f / sqrtf(tot / (float)cols + eps);
+    if (vec) {
+      for (int j = threadIdx.x; j < cols / 4; j += blockDim.x) {
+        float4 v = reinterpret_cast<const float4*>(xr)[j];
+        v.x *= inv; v.y *= inv; v.z *= inv; v.w *= inv;
+        if (gamma) {
+          const float4 gv = reinterpret_cast<const float4*>(gamma)[j];
+          v.x = gv.x * v.x; v.y = gv.y * v.y; v.z = gv.z * v.z; v.w = gv.w * v.w;
+        }
+        reinterpret_cast<float4*>(yr)[j] = v;
+      }
+    } else {
+      for (int j = threadIdx.x; j < cols; j += blockDim.x)
+        yr[j] = gamma ? gamma[j] * (xr[j] * inv) : xr[j] * inv;
+    }
+    __syncthreads();
   }
 }
 
@@ -122,9 +153,24 @@ __global__ void argmax_rows_kernel(const float* __restrict__ x, int32_t* __restr
     const float* xr = x + (int64_t)r * cols;
     float best = -3.4028234663852886e+38f;
     int bi = 0x7fffffff;
-    for (int j = threadIdx.x; j < cols; j += blockDim.x) {
-      float v = xr[j];
-      if (v > best || (v == best && j < bi)) { best = v; bi = j; }
+    if ((cols & 3) == 0 && ((uintptr_t)x & 15) == 0) {
+      // 16-byte loads, four in flight per thread; a thread's columns rise
+      // within each vector, so strict > keeps the first maximum.
+      const float4* xv = reinterpret_cast<const float4*>(xr);
+      const int nv = cols >> 2;
+#pragma unroll 4
+      for (int j = threadIdx.x; j < nv; j += blockDim.x) {
+        const float4 v = xv[j];
+        if (v.x > best || (v.x == best && 4 * j < bi)) { best = v.x; bi = 4 * j; }
+        if (v.y > best) { best = v.y; bi = 4 * j + 1; }
+        if (v.z > best) { best = v.z; bi = 4 * j + 2; }
+        if (v.w > best) { best = v.w; bi = 4 * j + 3; }
+      }
+    } else {
+      for (int j = threadIdx.x; j < cols; j += blockDim.x) {
+        float v = xr[j];
+        if (v > best || (v == best && j < bi)) { best = v; bi = j; }
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -176,7 +222,7 @@ int launch_layernorm(cudaStream_t s, int64_t* cnt, const float* x, const float* 
 int launch_rmsnorm(cudaStream_t s, int64_t* cnt, const float* x, const float* gamma, float* y,
                    int rows, int cols, float eps) {
   if (rows <= 0 || cols <= 0) return fail(SPX_ERR_INVALID_ARGUMENT, "rmsnorm: bad shape");
-  rmsnorm_kernel<<<grid_for((int64_t)rows * 32, 256), 256, 0, s>>>(x, gamma, y, rows, cols, eps);
+  rmsnorm_kernel<<<grid_for(rows, 1, 8), 256, 0, s>>>(x, gamma, y, rows, cols, eps);
   return after_launch(cnt, "rmsnorm");
 }
 
@@ -192,7 +238,7 @@ int launch_rope(cudaStream_t s, int64_t* cnt, float* x, const int32_t* pos, int 
 int launch_argmax_rows(cudaStream_t s, int64_t* cnt, const float* x, int32_t* idx, float* val,
                        int rows, int cols) {
   if (rows <= 0 || cols <= 0) return fail(SPX_ERR_INVALID_ARGUMENT, "argmax: bad shape");
-  argmax_rows_kernel<<<grid_for(rows, 1, 8), 512, 0, s>>>(x, idx, val, rows, cols);
+  argmax_rows_kernel<<<grid_for(rows, 1, 8), 1024, 0, s>>>(x, idx, val, rows, cols);
   return after_launch(cnt, "argmax_rows");
 }
 

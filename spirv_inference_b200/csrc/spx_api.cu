@@ -88,6 +88,11 @@ int launch_gemm(cudaStream_t s, int64_t* cnt, const float* a, const float* b, co
       p->c_ms >= p->n && gemm_rows_eligible(a, p->a_ms, b, p->b_ns, p->m, p->k))
     return launch_gemm_rows(s, cnt, a, p->a_ms, b, p->b_ns, p->m, p->n, p->k, bias, res, c,
                             p->c_ms, p->alpha, p->activation, 0);
+  // Up to 128 rows: weights as the UMMA M side, split-k over a cluster.
+  if (g_gemm_path != 1 && single && b && p->a_ks == 1 && p->b_ks == 1 && c &&
+      p->c_ms >= p->n && gemm_tc_skinny_eligible(a, p->a_ms, b, p->b_ns, p->m, p->n, p->k))
+    return launch_gemm_tc_skinny(s, cnt, a, p->a_ms, b, p->b_ns, p->m, p->n, p->k, bias, res, c,
+                                 p->c_ms, p->alpha, p->activation);
   if (g_gemm_path != 1 && single && p->a_ks == 1 && p->b_ks == 1 &&
       gemm_tc_eligible(a, p->a_ms, bb, p->b_ns, p->m, p->n, p->k, c, p->c_ms) &&
       (!split || ((uintptr_t)b_lo & 15) == 0))
@@ -793,7 +798,7 @@ int spx_op_layernorm(spx_graph* g, const float* x, const float* residual, float*
 int spx_op_rmsnorm(spx_graph* g, const float* x, const float* gamma, float* y, int32_t rows,
                    int32_t cols, float eps) {
   SPX_G(g);
-  if (!x || !gamma || !y) return fail(SPX_ERR_INVALID_ARGUMENT, "rmsnorm: null");
+  if (!x || !y) return fail(SPX_ERR_INVALID_ARGUMENT, "rmsnorm: null");
   return launch_rmsnorm(g->stream, &g->launches, x, gamma, y, rows, cols, eps);
 }
 
@@ -839,12 +844,23 @@ int spx_op_attention_kv(spx_graph* g, const float* q, const float* k_cache, cons
 }
 
 int spx_op_swiglu_linear(spx_graph* g, const float* a, int64_t lda, const float* w, int64_t ldw,
-                         int32_t m, int32_t f, int32_t k, float* c, int64_t ldc) {
+                         int32_t m, int32_t f, int32_t k, float rms_eps, float* c, int64_t ldc) {
   SPX_G(g);
   if (!a || !w || !c) return fail(SPX_ERR_INVALID_ARGUMENT, "swiglu_linear: null");
   if (f <= 0 || ldc < f) return fail(SPX_ERR_INVALID_ARGUMENT, "swiglu_linear: bad shape");
   return launch_gemm_rows(g->stream, &g->launches, a, lda, w, ldw, m, f, k, nullptr, nullptr, c,
-                          ldc, 1.0f, SPX_ACT_NONE, (int64_t)f);
+                          ldc, 1.0f, SPX_ACT_NONE, (int64_t)f, rms_eps < 0 ? -1.0f : rms_eps);
+}
+
+int spx_op_rms_linear(spx_graph* g, const float* x, int64_t ldx, const float* w, int64_t ldw,
+                      int32_t m, int32_t n, int32_t k, float rms_eps, const float* residual,
+                      float* c, int64_t ldc, uint64_t* argmax_keys) {
+  SPX_G(g);
+  if (!x || !w || !c) return fail(SPX_ERR_INVALID_ARGUMENT, "rms_linear: null");
+  if (n <= 0 || ldc < n) return fail(SPX_ERR_INVALID_ARGUMENT, "rms_linear: bad shape");
+  return launch_gemm_rows(g->stream, &g->launches, x, ldx, w, ldw, m, n, k, nullptr, residual, c,
+                          ldc, 1.0f, SPX_ACT_NONE, 0, rms_eps < 0 ? -1.0f : rms_eps,
+                          reinterpret_cast<unsigned long long*>(argmax_keys));
 }
 
 int spx_op_swiglu_rows(spx_graph* g, const float* gu, int64_t ld, float* y, int64_t ldy,
@@ -854,11 +870,12 @@ int spx_op_swiglu_rows(spx_graph* g, const float* gu, int64_t ld, float* y, int6
   return launch_swiglu_rows(g->stream, &g->launches, gu, ld, y, ldy, rows, f);
 }
 
-int spx_op_token_commit(spx_graph* g, const int32_t* ids, int32_t* hist, int32_t* state,
-                        int32_t batch, int32_t advance, int32_t hist_cap) {
+int spx_op_token_commit(spx_graph* g, int32_t* ids, int32_t* hist, int32_t* state,
+                        int32_t batch, int32_t advance, int32_t hist_cap, uint64_t* argmax_keys) {
   SPX_G(g);
   if (!ids || !hist || !state) return fail(SPX_ERR_INVALID_ARGUMENT, "token_commit: null");
-  return launch_token_commit(g->stream, &g->launches, ids, hist, state, batch, advance, hist_cap);
+  return launch_token_commit(g->stream, &g->launches, ids, hist, state, batch, advance, hist_cap,
+                             reinterpret_cast<unsigned long long*>(argmax_keys));
 }
 
 int spx_op_argmax_partial(spx_graph* g, const float* x, int64_t ldx, int32_t rows, int32_t cols,

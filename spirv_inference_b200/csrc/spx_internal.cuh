@@ -148,7 +148,8 @@ int launch_swiglu(cudaStream_t s, int64_t* cnt, const float* gate, const float* 
 bool gemm_rows_eligible(const float* a, int64_t lda, const float* w, int64_t ldw, int M, int K);
 int launch_gemm_rows(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, const float* w,
                      int64_t ldw, int M, int N, int K, const float* bias, const float* res,
-                     float* c, int64_t ldc, float alpha, int act, int64_t pair_off);
+                     float* c, int64_t ldc, float alpha, int act, int64_t pair_off,
+                     float rms_eps = -1.0f, unsigned long long* amax = nullptr);
 int launch_rope_kv_append(cudaStream_t s, int64_t* cnt, const float* qkv, int64_t ld_qkv,
                           const float* cos_t, const float* sin_t, const int32_t* pos,
                           float* q_out, float* kc, float* vc, int B, int T, int Hq, int Hkv,
@@ -156,8 +157,9 @@ int launch_rope_kv_append(cudaStream_t s, int64_t* cnt, const float* qkv, int64_
 int launch_attention_kv(cudaStream_t s, int64_t* cnt, const float* q, const float* kc,
                         const float* vc, float* out, const int32_t* pos, int B, int T, int Hq,
                         int Hkv, int D, int max_seq, float scale);
-int launch_token_commit(cudaStream_t s, int64_t* cnt, const int32_t* ids, int32_t* hist,
-                        int32_t* state, int B, int advance, int hist_cap);
+int launch_token_commit(cudaStream_t s, int64_t* cnt, int32_t* ids, int32_t* hist,
+                        int32_t* state, int B, int advance, int hist_cap,
+                        unsigned long long* keys = nullptr);
 int launch_argmax_partial(cudaStream_t s, int64_t* cnt, const float* x, int64_t ldx, int rows,
                           int cols, int col_offset, float* packed);
 int launch_argmax_merge(cudaStream_t s, int64_t* cnt, const float* packed, int parts, int rows,
@@ -195,6 +197,11 @@ bool gemm_tc_eligible(const float* a, int64_t lda, const float* b, int64_t ldb, 
 int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, const float* b,
                    const float* b_lo, int64_t ldb, int M, int N, int K, const float* bias,
                    const float* res, float* c, int64_t ldc, float alpha, int act);
+bool gemm_tc_skinny_eligible(const float* a, int64_t lda, const float* w, int64_t ldw, int M,
+                             int N, int K);
+int launch_gemm_tc_skinny(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda,
+                          const float* w, int64_t ldw, int M, int N, int K, const float* bias,
+                          const float* res, float* c, int64_t ldc, float alpha, int act);
 int launch_weights_split(cudaStream_t s, int64_t* cnt, const float* w, float* hi, float* lo,
                          int64_t n);
 // Returns and clears the device status of the tensor-core pipeline (0 = ok,

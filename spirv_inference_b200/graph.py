@@ -280,16 +280,22 @@ class Graph:
         check(self._l.spx_op_attention_kv(self.h, self._p(q), self._p(k_cache), self._p(v_cache),
                                           self._p(out), self._p(state), ctypes.byref(p), scale))
 
-    def swiglu_linear(self, a, lda, w, ldw, m, f, k, c, ldc):
+    def swiglu_linear(self, a, lda, w, ldw, m, f, k, c, ldc, rms_eps=-1.0):
         check(self._l.spx_op_swiglu_linear(self.h, self._p(a), lda, self._p(w), ldw, m, f, k,
-                                           self._p(c), ldc))
+                                           rms_eps, self._p(c), ldc))
+
+    def rms_linear(self, x, ldx, w, ldw, m, n, k, c, ldc, *, rms_eps=-1.0, residual=None,
+                   argmax_keys=None):
+        check(self._l.spx_op_rms_linear(self.h, self._p(x), ldx, self._p(w), ldw, m, n, k,
+                                        rms_eps, self._p(residual), self._p(c), ldc,
+                                        self._p(argmax_keys)))
 
     def swiglu_rows(self, gu, ld, y, ldy, rows, f):
         check(self._l.spx_op_swiglu_rows(self.h, self._p(gu), ld, self._p(y), ldy, rows, f))
 
-    def token_commit(self, ids, hist, state, batch, advance, hist_cap):
+    def token_commit(self, ids, hist, state, batch, advance, hist_cap, argmax_keys=None):
         check(self._l.spx_op_token_commit(self.h, self._p(ids), self._p(hist), self._p(state),
-                                          batch, advance, hist_cap))
+                                          batch, advance, hist_cap, self._p(argmax_keys)))
 
     def argmax_partial(self, x, ldx, rows, cols, col_offset, packed):
         check(self._l.spx_op_argmax_partial(self.h, self._p(x), ldx, rows, cols, col_offset,

@@ -62,15 +62,29 @@ TINY_TEST = LlamaConfig(layers=2, hidden=512, heads=8, kv_heads=2, head_dim=64, 
                         vocab=1000)
 
 
-def make_weights(cfg: LlamaConfig, seed: int = 0) -> dict:
-    """Seeded weights in the reference's shapes ([in, out] matrices)."""
-    rng = np.random.Generator(np.random.PCG64(seed))
-    H, KV, F = cfg.hidden, cfg.kv_heads * cfg.head_dim, cfg.ffn
+def make_weights(cfg: LlamaConfig, seed: int = 0, generator: str = "numpy") -> dict:
+    """Seeded weights in the reference's shapes ([in, out] matrices).
 
-    def nrm(*shape):
-        a = rng.standard_normal(shape, dtype=np.float32)
-        a *= np.float32(0.02)
-        return a
+    generator "numpy": PCG64 standard normals (parity tests); "torch": the
+    multi-threaded torch CPU generator seeded with `seed` (the 1.1B-parameter
+    benchmark model, where single-threaded numpy would take most of a
+    minute)."""
+    H, KV, F = cfg.hidden, cfg.kv_heads * cfg.head_dim, cfg.ffn
+    if generator == "torch":
+        import torch
+        tg = torch.Generator().manual_seed(seed)
+
+        def nrm(*shape):
+            a = torch.randn(shape, generator=tg, dtype=torch.float32).numpy()
+            a *= np.float32(0.02)
+            return a
+    else:
+        rng = np.random.Generator(np.random.PCG64(seed))
+
+        def nrm(*shape):
+            a = rng.standard_normal(shape, dtype=np.float32)
+            a *= np.float32(0.02)
+            return a
 
     def gain(n):
         return (np.float32(1.0) + nrm(n)).astype(np.float32)
@@ -134,19 +148,28 @@ def tp_shard(cfg: LlamaConfig, rank: int, world: int) -> TpShard:
 
 
 def pack_layer(cfg: LlamaConfig, lw: dict, sh: TpShard) -> dict:
-    """Per-rank device layouts: [out][in] matrices, Q|K|V and gate|up fused."""
+    """Per-rank device layouts: [out][in] matrices, Q|K|V and gate|up fused.
+
+    The RMSNorm gains are folded into the projections they feed
+    (rms_norm(x, g) @ W = (x / rms(x)) @ (g[:, None] * W)), so the device
+    normalises without a gain, inside the projection for few rows."""
     D = cfg.head_dim
     qs = slice(sh.q0 * D, (sh.q0 + sh.nq) * D)
     ks = slice(sh.kv0 * D, (sh.kv0 + sh.nkv) * D)
     fs = slice(sh.f0, sh.f0 + sh.nf)
     wqkv = np.concatenate([lw["q"][:, qs].T, lw["k"][:, ks].T, lw["v"][:, ks].T], axis=0)
+    wgu = np.concatenate([lw["gate"][:, fs].T, lw["up"][:, fs].T], 0)
     return {
-        "ln": lw["ln"], "post_ln": lw["post_ln"],
-        "wqkv": np.ascontiguousarray(wqkv),                     # [(nq + 2 nkv) D][H]
-        "wo": np.ascontiguousarray(lw["o"][qs, :].T),           # [H][nq D]
-        "wgu": np.ascontiguousarray(np.concatenate([lw["gate"][:, fs].T, lw["up"][:, fs].T], 0)),
-        "wdown": np.ascontiguousarray(lw["down"][fs, :].T),     # [H][nf]
+        "wqkv": np.ascontiguousarray(wqkv * lw["ln"][None, :]),      # [(nq + 2 nkv) D][H]
+        "wo": np.ascontiguousarray(lw["o"][qs, :].T),                # [H][nq D]
+        "wgu": np.ascontiguousarray(wgu * lw["post_ln"][None, :]),   # [2 nf][H]
+        "wdown": np.ascontiguousarray(lw["down"][fs, :].T),          # [H][nf]
     }
+
+
+def pack_lm_head(cfg: LlamaConfig, W: dict, sh: TpShard) -> np.ndarray:
+    """This rank's vocabulary rows of the lm_head, [nv][H], final gain folded."""
+    return np.ascontiguousarray(W["lm_head"][:, sh.v0:sh.v0 + sh.nv].T * W["final_ln"][None, :])
 
 
 class _CudaArray:
@@ -179,9 +202,7 @@ class LlamaDecoder:
         self.nqkv = (sh.nq + 2 * sh.nkv) * D
         # Weights.
         self.embed = g.tensor(weights["embed"])
-        self.final_ln = g.tensor(weights["final_ln"])
-        self.lm_head = g.tensor(np.ascontiguousarray(
-            weights["lm_head"][:, sh.v0:sh.v0 + sh.nv].T))     # [nv][H]
+        self.lm_head = g.tensor(pack_lm_head(cfg, weights, sh))
         self.layers = []
         for lw in weights["layers"]:
             pk = pack_layer(cfg, lw, sh)
@@ -199,6 +220,8 @@ class LlamaDecoder:
         self.logits = g.alloc((batch, sh.nv))
         self.kc = [g.alloc((batch, sh.nkv, cfg.max_seq, D)) for _ in range(cfg.layers)]
         self.vc = [g.alloc((batch, sh.nkv, cfg.max_seq, D)) for _ in range(cfg.layers)]
+        self.keys = g.alloc((batch,), np.uint64)
+        g.zero(self.keys)
         self.prompt_ids = g.alloc((M,), np.int32)
         self.ids = g.alloc((batch,), np.int32)
         self.hist = g.alloc((n_new, batch), np.int32)
@@ -215,6 +238,8 @@ class LlamaDecoder:
             self.x_a, self.x_b = g.alloc((M, H)), g.alloc((M, H))
         self.capture = capture
         self._captured = False
+        self._mark = None      # optional callback(label, bytes, flops) after each op
+        self._host_pos = 0
 
     # -- helpers -----------------------------------------------------------
     def _torch_buf(self, t) -> DeviceTensor:
@@ -230,11 +255,17 @@ class LlamaDecoder:
         import torch.distributed as dist
         dist.all_reduce(self._torch_view(t, rows, self.cfg.hidden), group=self.group)
 
+    def _note(self, label: str, nbytes: float, flops: float = 0.0) -> None:
+        if self._mark is not None:
+            self._mark(label, nbytes, flops)
+
     def _linear(self, a: DeviceTensor, lda: int, w: DeviceTensor, m: int, c: DeviceTensor,
-                residual: DeviceTensor | None = None):
+                residual: DeviceTensor | None = None, label: str = "linear"):
         n, k = w.shape
         self.g.gemm(a, w, c, m=m, n=n, k=k, a_strides=(0, lda, 1), b_strides=(0, 1, k),
                     c_strides=(0, n), residual=residual)
+        self._note(label, 4.0 * (n * k + m * k + m * n * (2 if residual is not None else 1)),
+                   2.0 * m * n * k)
 
     # -- one pass over T tokens per sequence -------------------------------
     def _forward(self, ids: DeviceTensor, T: int) -> None:
@@ -245,41 +276,75 @@ class LlamaDecoder:
                   max_seq=cfg.max_seq)
         lead = self.rank == 0
         g.embedding(self.embed, ids, self.x_a, M, H)
+        self._note("small", 8.0 * M * H)
+        # Keys read by attention: positions 0 .. state[0] + T - 1 (state[0] is
+        # on the device; the host tracks it only for the cost model).
+        n_keys = self._host_pos + T
+        few = M <= 8          # weight-streaming projections with the norm folded in
+        eps = cfg.eps
         for li, L in enumerate(self.layers):
-            g.rmsnorm(self.x_a, L["ln"], self.h, M, H, cfg.eps)
-            self._linear(self.h, H, L["wqkv"], M, self.qkv)
+            if few:
+                g.rms_linear(self.x_a, H, L["wqkv"], H, M, self.nqkv, H, self.qkv, self.nqkv,
+                             rms_eps=eps)
+                self._note("linear", 4.0 * (self.nqkv * H + M * H + M * self.nqkv),
+                           2.0 * M * self.nqkv * H)
+            else:
+                g.rmsnorm(self.x_a, None, self.h, M, H, eps)
+                self._note("small", 8.0 * M * H)
+                self._linear(self.h, H, L["wqkv"], M, self.qkv)
             g.rope_kv_append(self.qkv, self.nqkv, self.cos, self.sin, self.state, self.q,
                              self.kc[li], self.vc[li], **kv)
+            self._note("small", 8.0 * M * self.nqkv)
             g.attention_kv(self.q, self.kc[li], self.vc[li], self.att, self.state,
                            scale=float(1.0 / np.sqrt(np.float32(D))), **kv)
+            self._note("attention", 4.0 * (2 * B * sh.nkv * n_keys * D + 2 * M * sh.nq * D),
+                       4.0 * B * sh.nq * T * n_keys * D)
             self._linear(self.att, sh.nq * D, L["wo"], M, self.x_b,
                          residual=self.x_a if lead else None)
             if self.world > 1:
                 self._all_reduce(self.x_b, M)
-            g.rmsnorm(self.x_b, L["post_ln"], self.h, M, H, cfg.eps)
-            if M <= 8:
-                g.swiglu_linear(self.h, H, L["wgu"], H, M, sh.nf, H, self.mlp, sh.nf)
+                self._note("all_reduce", 4.0 * M * H)
+            if few:
+                g.swiglu_linear(self.x_b, H, L["wgu"], H, M, sh.nf, H, self.mlp, sh.nf,
+                                rms_eps=eps)
+                self._note("linear", 4.0 * (2 * sh.nf * H + M * H + M * sh.nf),
+                           4.0 * M * sh.nf * H)
             else:
+                g.rmsnorm(self.x_b, None, self.h, M, H, eps)
+                self._note("small", 8.0 * M * H)
                 self._linear(self.h, H, L["wgu"], M, self.gu)
                 g.swiglu_rows(self.gu, 2 * sh.nf, self.mlp, sh.nf, M, sh.nf)
+                self._note("small", 12.0 * M * sh.nf)
             self._linear(self.mlp, sh.nf, L["wdown"], M, self.x_a,
                          residual=self.x_b if lead else None)
             if self.world > 1:
                 self._all_reduce(self.x_a, M)
+                self._note("all_reduce", 4.0 * M * H)
         # Final norm + lm_head on the last position of every sequence.
-        g.rmsnorm(self.x_a, self.final_ln, self.h, M, H, cfg.eps)
-        last = self.h.view((B, H), offset_elems=(T - 1) * H)
-        self._linear(last, T * H, self.lm_head, B, self.logits)
-        if self.world == 1:
-            g.argmax_rows(self.logits, self.ids, B, sh.nv)
+        keys = None
+        last_x = self.x_a.view((B, H), offset_elems=(T - 1) * H)
+        if B <= 8:
+            keys = self.keys if self.world == 1 else None
+            g.rms_linear(last_x, T * H, self.lm_head, H, B, sh.nv, H, self.logits, sh.nv,
+                         rms_eps=eps, argmax_keys=keys)
+            self._note("linear", 4.0 * (sh.nv * H + B * H + B * sh.nv), 2.0 * B * sh.nv * H)
         else:
+            g.rmsnorm(self.x_a, None, self.h, M, H, eps)
+            self._note("small", 8.0 * M * H)
+            last = self.h.view((B, H), offset_elems=(T - 1) * H)
+            self._linear(last, T * H, self.lm_head, B, self.logits)
+            if self.world == 1:
+                g.argmax_rows(self.logits, self.ids, B, sh.nv)
+        if self.world > 1:
             import torch.distributed as dist
             g.argmax_partial(self.logits, sh.nv, B, sh.nv, sh.v0, self.packed)
             dist.all_gather_into_tensor(self._torch_view(self.packed_all, self.world, B * 2),
                                         self._torch_view(self.packed, 1, B * 2),
                                         group=self.group)
             g.argmax_merge(self.packed_all, self.world, B, self.ids)
-        g.token_commit(self.ids, self.hist, self.state, B, T, self.n_new)
+        g.token_commit(self.ids, self.hist, self.state, B, T, self.n_new, argmax_keys=keys)
+        self._note("small", 4.0 * B * sh.nv)
+        self._host_pos += T
 
     # -- public ------------------------------------------------------------
     def upload_prompt(self, prompt: np.ndarray) -> None:
@@ -289,6 +354,7 @@ class LlamaDecoder:
     def prefill(self) -> None:
         """Resets the position state and runs the prompt block."""
         self.g.zero(self.state)
+        self._host_pos = 0
         self._forward(self.prompt_ids, self.P)
 
     def decode_step(self) -> None:
@@ -297,8 +363,10 @@ class LlamaDecoder:
                 self.g.capture_begin()
                 self._forward(self.ids, 1)
                 self.g.capture_end()
+                self._host_pos -= 1          # recorded, not run
                 self._captured = True
             self.g.replay()
+            self._host_pos += 1
         else:
             self._forward(self.ids, 1)
 

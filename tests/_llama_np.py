@@ -28,7 +28,7 @@ def tp_generate(cfg, W, prompt, n_new, world, reduce=None):
             parts = {}
             for r in ranks:
                 P, s = packed[r][li], sh[r]
-                h = R.rms_norm(x, P["ln"], cfg.eps)
+                h = R.rms_norm(x, np.float32(1.0), cfg.eps)    # gain folded into wqkv
                 qkv = h @ P["wqkv"].T
                 q = qkv[:, :s.nq * D].reshape(T, s.nq, D).transpose(1, 0, 2)
                 k = qkv[:, s.nq * D:(s.nq + s.nkv) * D].reshape(T, s.nkv, D).transpose(1, 0, 2)
@@ -49,15 +49,15 @@ def tp_generate(cfg, W, prompt, n_new, world, reduce=None):
             parts = {}
             for r in ranks:
                 P, s = packed[r][li], sh[r]
-                h = R.rms_norm(x, P["post_ln"], cfg.eps)
+                h = R.rms_norm(x, np.float32(1.0), cfg.eps)    # gain folded into wgu
                 gu = h @ P["wgu"].T
                 parts[r] = (R.silu(gu[:, :s.nf]) * gu[:, s.nf:]) @ P["wdown"].T
             x = x + allreduce(parts)
-        h = R.rms_norm(x[-1:], W["final_ln"], cfg.eps)
+        h = R.rms_norm(x[-1:], np.float32(1.0), cfg.eps)
         best = None
         for r in (range(world) if reduce is None else [reduce.rank]):
             s = llama.tp_shard(cfg, r, world)
-            lg = (h @ W["lm_head"][:, s.v0:s.v0 + s.nv])[0]
+            lg = (h @ llama.pack_lm_head(cfg, W, s).T)[0]
             cand = (float(lg.max()), s.v0 + int(np.argmax(lg)))
             if reduce is not None:
                 return reduce.argmax(cand)

@@ -48,6 +48,27 @@ def test_gemm_rows(g, m, act):
     assert np.max(np.abs(got - ref)) <= 2e-7 * K
 
 
+@pytest.mark.parametrize("m,N,K", [(9, 300, 2048), (16, 2560, 2048), (33, 1000, 100),
+                                   (64, 2048, 5632), (100, 129, 516), (128, 4000, 2048)])
+def test_gemm_tc_skinny(g, m, N, K):
+    """9..128 rows: tensor-core tiles over the weight rows, split-k reduced
+    across a cluster; 3xTF32 accuracy (normwise, grows with K)."""
+    a, w = _u(m, K), _u(N, K) * np.float32(1 / np.sqrt(K))
+    bias, res = _u(N), _u(m, N)
+    da, dw, db, dr, dc = g.tensor(a), g.tensor(w), g.tensor(bias), g.tensor(res), g.alloc((m, N))
+    g.gemm(da, dw, dc, m=m, n=N, k=K, a_strides=(0, K, 1), b_strides=(0, 1, K), c_strides=(0, N),
+           bias=db, residual=dr, activation=_lib.ACT_RELU)
+    ref = np.maximum(a.astype(np.float64) @ w.T.astype(np.float64) + bias + res, 0)
+    got = dc.download()
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    assert err <= 2.5e-8 * K + 1e-6, err
+    # deterministic: the cluster reduction sums partials in a fixed order
+    dc2 = g.alloc((m, N))
+    g.gemm(da, dw, dc2, m=m, n=N, k=K, a_strides=(0, K, 1), b_strides=(0, 1, K),
+           c_strides=(0, N), bias=db, residual=dr, activation=_lib.ACT_RELU)
+    assert np.array_equal(got, dc2.download())
+
+
 def test_swiglu_linear_and_rows(g):
     m, K, F = 4, 1024, 352
     a, w = _u(m, K), _u(2 * F, K) * 0.05
@@ -56,6 +77,13 @@ def test_swiglu_linear_and_rows(g):
     gu = a.astype(np.float64) @ w.T.astype(np.float64)
     ref = gu[:, :F] / (1 + np.exp(-gu[:, :F])) * gu[:, F:]
     assert np.max(np.abs(dc.download() - ref)) <= 1e-5
+    # with the RMSNorm folded in
+    g.swiglu_linear(da, K, dw, K, m, F, K, dc, F, rms_eps=1e-5)
+    a64 = a.astype(np.float64)
+    an = a64 / np.sqrt(np.mean(a64 ** 2, axis=1, keepdims=True) + 1e-5)
+    gn = an @ w.T.astype(np.float64)
+    refn = gn[:, :F] / (1 + np.exp(-gn[:, :F])) * gn[:, F:]
+    assert np.max(np.abs(dc.download() - refn)) <= 1e-5
     dgu, dy = g.tensor(gu.astype(np.float32)), g.alloc((m, F))
     g.swiglu_rows(dgu, 2 * F, dy, F, m, F)
     assert np.max(np.abs(dy.download() - ref)) <= 1e-5
@@ -106,6 +134,27 @@ def test_rope_append_and_attention(g, B, T, Hq, Hkv, pos0):
     assert np.array_equal(d_vc.download(), vc)
     ref = _attn_ref(qr.reshape(B * T, Hq, D), kc, vc, pos0, T, Hq, Hkv)
     assert np.max(np.abs(d_out.download() - ref)) <= 2e-6
+
+
+@pytest.mark.parametrize("m", [1, 3, 8])
+def test_rms_linear_with_fused_argmax(g, m):
+    K, N = 2048, 5000
+    x, w, res = _u(m, K) * 3, _u(N, K) * np.float32(0.02), _u(m, N)
+    w[:, :] = w
+    dx, dw, dr, dc = g.tensor(x), g.tensor(w), g.tensor(res), g.alloc((m, N))
+    keys = g.alloc((m,), np.uint64)
+    g.zero(keys)
+    g.rms_linear(dx, K, dw, K, m, N, K, dc, N, rms_eps=1e-5, residual=dr, argmax_keys=keys)
+    x64 = x.astype(np.float64)
+    xn = x64 / np.sqrt(np.mean(x64 ** 2, axis=1, keepdims=True) + 1e-5)
+    ref = xn @ w.T.astype(np.float64) + res
+    got = dc.download()
+    assert np.max(np.abs(got - ref)) <= 1e-5
+    ids, hist = g.alloc((m,), np.int32), g.alloc((1, m), np.int32)
+    state = g.tensor(np.zeros(2, np.int32), np.int32)
+    g.token_commit(ids, hist, state, m, 1, 1, argmax_keys=keys)
+    assert np.array_equal(ids.download(), np.argmax(got, axis=1))   # first maximum on ties
+    assert np.all(keys.download() == 0)                               # reset for the next step
 
 
 def test_argmax_partial_merge_and_commit(g):
