@@ -586,6 +586,7 @@ constexpr int kSkMma = 5;
 
 struct SkArgs {
   int M, N, K, Mp, k_blocks, kb_per_split, splits, stages;
+  int presplit;  // W arrives as hi and lo tiles (pre-split weights): converters split X only
   uint32_t idesc, tmem_cols, stage_bytes, x_bytes;
   const float* bias;
   const float* res;
@@ -620,6 +621,7 @@ __device__ __forceinline__ float ld_cluster(uint32_t addr) {
 
 __global__ void __launch_bounds__(kSkThreads)
     gemm_tc_skinny_kernel(const __grid_constant__ CUtensorMap tmW,
+                          const __grid_constant__ CUtensorMap tmWlo,
                           const __grid_constant__ CUtensorMap tmX, const SkArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -670,8 +672,9 @@ __global__ void __launch_bounds__(kSkThreads)
       for (int i = 0; i < nkb; ++i) {
         if (!bar_wait(&empty[s], ph ^ 1, abort_flag, kTimeoutNs, 64)) break;
         uint8_t* st = smem + (size_t)s * p.stage_bytes;
-        bar_expect_tx(&full[s], w_bytes + p.x_bytes);
+        bar_expect_tx(&full[s], (p.presplit ? 2 * w_bytes : w_bytes) + p.x_bytes);
         tma_load_2d(st, &tmW, &full[s], (kb0 + i) * kBK, nt * kBM);
+        if (p.presplit) tma_load_2d(st + w_bytes, &tmWlo, &full[s], (kb0 + i) * kBK, nt * kBM);
         tma_load_2d(st + 2 * w_bytes, &tmX, &full[s], (kb0 + i) * kBK, 0);
         armed |= 1u << s;
         armed_par = (armed_par & ~(1u << s)) | (ph << s);
@@ -733,7 +736,8 @@ __global__ void __launch_bounds__(kSkThreads)
       ok = bar_wait(&full[s], ph, abort_flag, kTimeoutNs, 256);
       if (!ok) break;
       uint8_t* st = smem + (size_t)s * p.stage_bytes;
-      split_buffer((float4*)st, (float4*)(st + w_bytes), w_bytes / 16, ct, 128);
+      if (!p.presplit)
+        split_buffer((float4*)st, (float4*)(st + w_bytes), w_bytes / 16, ct, 128);
       split_buffer((float4*)(st + 2 * w_bytes), (float4*)(st + 2 * w_bytes + p.x_bytes),
                    p.x_bytes / 16, ct, 128);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -949,8 +953,9 @@ bool gemm_tc_skinny_eligible(const float* a, int64_t lda, const float* w, int64_
 }
 
 int launch_gemm_tc_skinny(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda,
-                          const float* w, int64_t ldw, int M, int N, int K, const float* bias,
-                          const float* res, float* c, int64_t ldc, float alpha, int act) {
+                          const float* w, const float* w_lo, int64_t ldw, int M, int N, int K,
+                          const float* bias, const float* res, float* c, int64_t ldc,
+                          float alpha, int act) {
   if (!gemm_tc_skinny_eligible(a, lda, w, ldw, M, N, K) || ldc < N || !c)
     return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_tc_skinny: operands not eligible");
   SkArgs p = {};
@@ -958,6 +963,8 @@ int launch_gemm_tc_skinny(cudaStream_t s, int64_t* cnt, const float* a, int64_t 
   p.N = N;
   p.K = K;
   p.Mp = (M + 15) / 16 * 16;
+  p.presplit = w_lo != nullptr;
+  if (w_lo && ((uintptr_t)w_lo & 15)) return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_tc_skinny: w_lo");
   p.k_blocks = (K + kBK - 1) / kBK;
   const int tiles = (N + kBM - 1) / kBM;
   // Two CTAs per SM; split k over a cluster until the grid fills them.
@@ -981,9 +988,11 @@ int launch_gemm_tc_skinny(cudaStream_t s, int64_t* cnt, const float* a, int64_t 
   p.ldc = ldc;
   p.alpha = alpha;
   p.act = act;
-  CUtensorMap mw, mx;
+  CUtensorMap mw, mwlo, mx;
   int rc;
   if ((rc = make_map(&mw, w, N, K, ldw, kBM))) return rc;
+  mwlo = mw;
+  if (w_lo && (rc = make_map(&mwlo, w_lo, N, K, ldw, kBM))) return rc;
   if ((rc = make_map(&mx, a, M, K, lda, p.Mp))) return rc;
   size_t smem = 1024 + (size_t)p.stages * p.stage_bytes + 256;
   const size_t red_bytes = (size_t)p.Mp * kBM * 4;
@@ -1008,7 +1017,7 @@ int launch_gemm_tc_skinny(cudaStream_t s, int64_t* cnt, const float* a, int64_t 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_skinny_kernel, mw, mx, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_skinny_kernel, mw, mwlo, mx, p);
   if (e != cudaSuccess) return check_cuda(e, "gemm_tc_skinny launch");
   return after_launch(cnt, "gemm_tc_skinny");
 }

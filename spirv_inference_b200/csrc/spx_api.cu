@@ -82,17 +82,18 @@ int launch_gemm(cudaStream_t s, int64_t* cnt, const float* a, const float* b, co
   const bool single = p->batch == 1 && (p->batch_inner <= 1);
   const bool split = b_hi && b_lo;
   const float* bb = split ? b_hi : b;
-  // A handful of rows (decode, small-batch FC): stream the weights once on
-  // CUDA cores; a 128-row tensor-core tile would be almost all padding.
-  if (g_gemm_path == 0 && single && !split && p->a_ks == 1 && p->b_ks == 1 && c &&
+  // A handful of rows (decode, small-batch FC): stream the fp32 weights once
+  // on CUDA cores; a 128-row tensor-core tile would be almost all padding.
+  if (g_gemm_path == 0 && single && b && p->a_ks == 1 && p->b_ks == 1 && c &&
       p->c_ms >= p->n && gemm_rows_eligible(a, p->a_ms, b, p->b_ns, p->m, p->k))
     return launch_gemm_rows(s, cnt, a, p->a_ms, b, p->b_ns, p->m, p->n, p->k, bias, res, c,
                             p->c_ms, p->alpha, p->activation, 0);
-  // Up to 128 rows: weights as the UMMA M side, split-k over a cluster.
-  if (g_gemm_path != 1 && single && b && p->a_ks == 1 && p->b_ks == 1 && c &&
-      p->c_ms >= p->n && gemm_tc_skinny_eligible(a, p->a_ms, b, p->b_ns, p->m, p->n, p->k))
-    return launch_gemm_tc_skinny(s, cnt, a, p->a_ms, b, p->b_ns, p->m, p->n, p->k, bias, res, c,
-                                 p->c_ms, p->alpha, p->activation);
+  // Up to 128 rows: weights as the UMMA M side, split-k over a cluster; with
+  // pre-split weights the tiles arrive as hi / lo and only the rows are split.
+  if (g_gemm_path != 1 && single && bb && p->a_ks == 1 && p->b_ks == 1 && c &&
+      p->c_ms >= p->n && gemm_tc_skinny_eligible(a, p->a_ms, bb, p->b_ns, p->m, p->n, p->k))
+    return launch_gemm_tc_skinny(s, cnt, a, p->a_ms, bb, split ? b_lo : nullptr, p->b_ns, p->m,
+                                 p->n, p->k, bias, res, c, p->c_ms, p->alpha, p->activation);
   if (g_gemm_path != 1 && single && p->a_ks == 1 && p->b_ks == 1 &&
       gemm_tc_eligible(a, p->a_ms, bb, p->b_ns, p->m, p->n, p->k, c, p->c_ms) &&
       (!split || ((uintptr_t)b_lo & 15) == 0))

@@ -199,9 +199,11 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
                    const float* res, float* c, int64_t ldc, float alpha, int act);
 bool gemm_tc_skinny_eligible(const float* a, int64_t lda, const float* w, int64_t ldw, int M,
                              int N, int K);
+// w_lo non-null: w is the pre-split hi part (spx_weights_split) and w_lo the lo part.
 int launch_gemm_tc_skinny(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda,
-                          const float* w, int64_t ldw, int M, int N, int K, const float* bias,
-                          const float* res, float* c, int64_t ldc, float alpha, int act);
+                          const float* w, const float* w_lo, int64_t ldw, int M, int N, int K,
+                          const float* bias, const float* res, float* c, int64_t ldc,
+                          float alpha, int act);
 int launch_weights_split(cudaStream_t s, int64_t* cnt, const float* w, float* hi, float* lo,
                          int64_t n);
 // Returns and clears the device status of the tensor-core pipeline (0 = ok,

@@ -207,6 +207,12 @@ class LlamaDecoder:
         for lw in weights["layers"]:
             pk = pack_layer(cfg, lw, sh)
             self.layers.append({k: g.tensor(v) for k, v in pk.items()})
+        # Tensor-core copies (hi / lo tf32 parts) of every projection: blocks of
+        # more than 8 rows (prefill, batch > 8) stream these instead of
+        # splitting the fp32 weights on chip; single rows keep the fp32 copy.
+        self._split = {}
+        for t in [self.lm_head] + [w for L in self.layers for w in L.values()]:
+            self._split[t.ptr] = g.weights_split(t)
         cos, sin = rope_tables(cfg, cfg.max_seq)
         self.cos, self.sin = g.tensor(cos), g.tensor(sin)
         # Activations (sized for the prefill block).
@@ -262,9 +268,11 @@ class LlamaDecoder:
     def _linear(self, a: DeviceTensor, lda: int, w: DeviceTensor, m: int, c: DeviceTensor,
                 residual: DeviceTensor | None = None, label: str = "linear"):
         n, k = w.shape
+        split = self._split.get(w.ptr) if m > 8 else None
         self.g.gemm(a, w, c, m=m, n=n, k=k, a_strides=(0, lda, 1), b_strides=(0, 1, k),
-                    c_strides=(0, n), residual=residual)
-        self._note(label, 4.0 * (n * k + m * k + m * n * (2 if residual is not None else 1)),
+                    c_strides=(0, n), residual=residual, b_split=split)
+        wb = 8.0 if split else 4.0
+        self._note(label, wb * n * k + 4.0 * (m * k + m * n * (2 if residual is not None else 1)),
                    2.0 * m * n * k)
 
     # -- one pass over T tokens per sequence -------------------------------

@@ -62,6 +62,13 @@ def test_gemm_tc_skinny(g, m, N, K):
     got = dc.download()
     err = np.abs(got - ref).max() / np.abs(ref).max()
     assert err <= 2.5e-8 * K + 1e-6, err
+    # pre-split weights (hi / lo tiles by TMA, only the rows split on chip):
+    # the same tf32 terms, so the same result
+    dcs = g.alloc((m, N))
+    g.gemm(da, dw, dcs, m=m, n=N, k=K, a_strides=(0, K, 1), b_strides=(0, 1, K),
+           c_strides=(0, N), bias=db, residual=dr, activation=_lib.ACT_RELU,
+           b_split=g.weights_split(dw))
+    assert np.array_equal(got, dcs.download())
     # deterministic: the cluster reduction sums partials in a fixed order
     dc2 = g.alloc((m, N))
     g.gemm(da, dw, dc2, m=m, n=N, k=K, a_strides=(0, K, 1), b_strides=(0, 1, K),
