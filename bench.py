@@ -597,10 +597,13 @@ def run_llama_spx(args) -> None:
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = llama_cpu_baseline(W, args.cpu_seconds)
         print(json.dumps(line), flush=True)
+    # Free the decoder (and its captured CUDA graph, which holds NCCL work on
+    # the communicator) before the process group goes away.
+    torch.cuda.synchronize()
+    dec.close()
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
-    dec.close()
 
 
 def main():

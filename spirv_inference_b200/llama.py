@@ -366,13 +366,21 @@ class LlamaDecoder:
         self._forward(self.prompt_ids, self.P)
 
     def decode_step(self) -> None:
-        if self.capture and self.world == 1:
-            if not self._captured:
+        """One cached decode step.  With `capture` the step (kernels and, at
+        world > 1, its NCCL collectives) is recorded once as a CUDA graph and
+        replayed; if recording fails the step runs eagerly from then on."""
+        if self.capture and not self._captured:
+            try:
                 self.g.capture_begin()
-                self._forward(self.ids, 1)
-                self.g.capture_end()
+                try:
+                    self._forward(self.ids, 1)
+                finally:
+                    self.g.capture_end()
                 self._host_pos -= 1          # recorded, not run
                 self._captured = True
+            except Exception:
+                self.capture = False
+        if self._captured:
             self.g.replay()
             self._host_pos += 1
         else:
