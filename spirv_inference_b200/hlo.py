@@ -264,6 +264,15 @@ def run_hlo(g: HloGraph, feeds: dict[str, np.ndarray], rk: RunKernel,
             out = rk("hlo_dot_batched.spv", at, bt, total, [B, M, K, N, total])
             vals[op.name] = out.reshape(op.shape)
             log.append("hlo_dot_batched.spv")
+        elif oc == "slice":
+            # host side, as compiler.rs does for slice / concatenate
+            sl = tuple(slice(a, b, st) for a, b, st in op.attrs["slice"])
+            vals[op.name] = np.ascontiguousarray(ins[0][sl])
+        elif oc == "concatenate":
+            vals[op.name] = np.concatenate(ins, axis=op.attrs["dimensions"][0])
+        elif oc in ("tuple", "get-tuple-element"):
+            # single-element tuples (the exported graphs' return wrappers)
+            vals[op.name] = ins[op.attrs.get("index", 0)] if oc == "get-tuple-element" else ins[0]
         elif oc == "compare":
             a, b = ins
             b = broadcast_host(b, op.shape, infer_broadcast_dims(b.shape, op.shape))

@@ -154,6 +154,20 @@ def eval_hlo_f64(g, feeds):
             Bs = [x.shape[d] for d in lb]
             M, K, N = int(np.prod([x.shape[d] for d in lf])), x.shape[lc[0]], int(np.prod([y.shape[d] for d in rf]))
             r = (xt.reshape(-1, M, K) @ yt.reshape(-1, K, N)).reshape(op.shape)
+        elif oc == "slice":
+            r = ins[0][tuple(slice(s0, e0, st) for s0, e0, st in a["slice"])]
+        elif oc == "concatenate":
+            r = np.concatenate(ins, axis=a["dimensions"][0])
+        elif oc in ("tuple", "convert"):
+            r = ins[0]
+        elif oc == "get-tuple-element":
+            r = ins[0]
+        elif oc == "compare":
+            fn = {"LT": np.less, "LE": np.less_equal, "EQ": np.equal, "NE": np.not_equal,
+                  "GE": np.greater_equal}.get(a.get("direction"), np.greater)
+            r = fn(ins[0], ins[1]).astype(np.float64)
+        elif oc == "select":
+            r = np.where(ins[0] != 0, ins[1], ins[2])
         else:
             fns = {"add": np.add, "subtract": np.subtract, "multiply": np.multiply, "divide": np.divide,
                    "maximum": np.maximum, "minimum": np.minimum, "power": np.power}
