@@ -4,9 +4,11 @@
 //  * conv_smallk: dense conv whose reduction K = kh*kw*ic is small (the
 //    3x3x3 stem of MobileNetV2 / EfficientNet-Lite0, conv2d.comp:26-50 as an
 //    NHWC kernel).  Weights [K][oc] sit in shared memory and are read as
-//    warp broadcasts; one thread computes all oc outputs of one pixel and
-//    writes them as contiguous 16-byte stores.  Input bytes are read once
-//    from HBM (tap overlap is served by L1), outputs written once.
+//    16-byte warp broadcasts; one thread computes all oc outputs of one
+//    pixel.  A warp's 32 pixels are consecutive, so their outputs are one
+//    contiguous run: it is staged in shared memory and written as whole
+//    rows of 16-byte vectors.  Input bytes are read once from HBM (tap
+//    overlap is served by L1), outputs written once.
 //
 //  * dw_rows: depthwise conv (depthwise_conv2d.comp:27-49) with a vertical
 //    sliding window: a thread owns 4 channels of one output column and R
@@ -19,14 +21,19 @@
 namespace spx {
 namespace {
 
-template <int OC>
+// KH / KW / IC > 0 fix the window at compile time (the 3x3x3 stems: the 27
+// input loads of a pixel are then issued before its FMAs); 0 = runtime.
+template <int OC, int KH = 0, int KW = 0, int IC = 0>
 __global__ void __launch_bounds__(128) conv_smallk_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ bias,
-    const float* __restrict__ res, float* __restrict__ y, int n, int ih, int iw, int ic, int oh,
-    int ow, int kh, int kw, int sh, int sw, int pt, int pl, int dh, int dw, int act,
+    const float* __restrict__ res, float* __restrict__ y, int n, int ih, int iw, int ic_rt,
+    int oh, int ow, int kh_rt, int kw_rt, int sh, int sw, int pt, int pl, int dh, int dw, int act,
     int w_layout) {
-  extern __shared__ float ws[];  // [K][OC] then bias[OC]
+  const int kh = KH > 0 ? KH : kh_rt, kw = KW > 0 ? KW : kw_rt, ic = IC > 0 ? IC : ic_rt;
+  extern __shared__ float ws[];  // [K][OC], bias[OC], then per-warp output staging
+  constexpr int kStride = OC + 4;  // staging row pitch (floats): conflict-free float4 rows
   const int K = kh * kw * ic;
+  float* stage = ws + K * OC + OC + (threadIdx.x >> 5) * 32 * kStride;
   for (int i = threadIdx.x; i < K * OC; i += blockDim.x) {
     const int k = i / OC, o = i % OC;
     // OHWI: w[o][k]; HWIO: w[k][o]  (k = (ky*kw + kx)*ic + ci in both)
@@ -34,45 +41,97 @@ __global__ void __launch_bounds__(128) conv_smallk_kernel(
   }
   for (int o = threadIdx.x; o < OC; o += blockDim.x) ws[K * OC + o] = bias ? bias[o] : 0.0f;
   __syncthreads();
+  const int lane = threadIdx.x & 31;
   const int total = n * oh * ow;
-  for (int pix = blockIdx.x * blockDim.x + threadIdx.x; pix < total; pix += gridDim.x * blockDim.x) {
-    const int ox = pix % ow;
-    const int t = pix / ow;
-    const int oy = t % oh;
-    const int img = t / oh;
+  // Warp-uniform loop: each warp takes 32 consecutive output pixels, whose
+  // NHWC outputs are one contiguous 32 * OC run.
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int base = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; base < total;
+       base += warps * 32) {
+    const int pix = base + lane;
     float acc[OC];
 #pragma unroll
     for (int o = 0; o < OC; ++o) acc[o] = ws[K * OC + o];
-    const float* xi = x + (size_t)img * ih * iw * ic;
-    for (int ky = 0; ky < kh; ++ky) {
-      const int iy = oy * sh + ky * dh - pt;
-      if (iy < 0 || iy >= ih) continue;
-      for (int kx = 0; kx < kw; ++kx) {
-        const int ix = ox * sw + kx * dw - pl;
-        if (ix < 0 || ix >= iw) continue;
-        const float* xp = xi + ((size_t)iy * iw + ix) * ic;
-        const float* wp = ws + ((ky * kw + kx) * ic) * OC;
-        for (int ci = 0; ci < ic; ++ci) {
-          const float v = __ldg(xp + ci);
+    if (pix < total) {
+      const int ox = pix % ow;
+      const int t = pix / ow;
+      const int oy = t % oh;
+      const int img = t / oh;
+      const float* xi = x + (size_t)img * ih * iw * ic;
+      if constexpr (KH > 0 && KW > 0 && IC > 0) {
+        float xv[KH * KW * IC];
 #pragma unroll
-          for (int o = 0; o < OC; ++o) acc[o] = fmaf(v, wp[ci * OC + o], acc[o]);
+        for (int ky = 0; ky < KH; ++ky)
+#pragma unroll
+          for (int kx = 0; kx < KW; ++kx) {
+            const int iy = oy * sh + ky * dh - pt, ix = ox * sw + kx * dw - pl;
+            const bool in = iy >= 0 && iy < ih && ix >= 0 && ix < iw;
+            const float* xp = xi + ((size_t)(in ? iy : 0) * iw + (in ? ix : 0)) * IC;
+#pragma unroll
+            for (int ci = 0; ci < IC; ++ci) xv[(ky * KW + kx) * IC + ci] = in ? __ldg(xp + ci) : 0.0f;
+          }
+#pragma unroll
+        for (int k = 0; k < KH * KW * IC; ++k) {
+          const float4* wp = reinterpret_cast<const float4*>(ws + k * OC);
+#pragma unroll
+          for (int o = 0; o < OC / 4; ++o) {
+            const float4 wv = wp[o];
+            acc[4 * o + 0] = fmaf(xv[k], wv.x, acc[4 * o + 0]);
+            acc[4 * o + 1] = fmaf(xv[k], wv.y, acc[4 * o + 1]);
+            acc[4 * o + 2] = fmaf(xv[k], wv.z, acc[4 * o + 2]);
+            acc[4 * o + 3] = fmaf(xv[k], wv.w, acc[4 * o + 3]);
+          }
+        }
+      } else
+      for (int ky = 0; ky < kh; ++ky) {
+        const int iy = oy * sh + ky * dh - pt;
+        if (iy < 0 || iy >= ih) continue;
+        for (int kx = 0; kx < kw; ++kx) {
+          const int ix = ox * sw + kx * dw - pl;
+          if (ix < 0 || ix >= iw) continue;
+          const float* xp = xi + ((size_t)iy * iw + ix) * ic;
+          const float4* wp = reinterpret_cast<const float4*>(ws + ((ky * kw + kx) * ic) * OC);
+          for (int ci = 0; ci < ic; ++ci) {
+            const float v = __ldg(xp + ci);
+#pragma unroll
+            for (int o = 0; o < OC / 4; ++o) {
+              const float4 wv = wp[ci * (OC / 4) + o];
+              acc[4 * o + 0] = fmaf(v, wv.x, acc[4 * o + 0]);
+              acc[4 * o + 1] = fmaf(v, wv.y, acc[4 * o + 1]);
+              acc[4 * o + 2] = fmaf(v, wv.z, acc[4 * o + 2]);
+              acc[4 * o + 3] = fmaf(v, wv.w, acc[4 * o + 3]);
+            }
+          }
         }
       }
     }
-    float* yp = y + (size_t)pix * OC;
-    const float* rp = res ? res + (size_t)pix * OC : nullptr;
+    // Stage the warp's 32 x OC outputs, then write them out as whole rows of
+    // 16-byte vectors (coalesced), adding the residual and the activation.
+    __syncwarp();
+#pragma unroll
+    for (int o = 0; o < OC; o += 4)
+      *reinterpret_cast<float4*>(stage + lane * kStride + o) =
+          make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
+    __syncwarp();
+    const int valid = min(32, total - base) * OC / 4;  // float4s of this warp's run
+    float* yb = y + (size_t)base * OC;
+    const float* rb = res ? res + (size_t)base * OC : nullptr;
     with_act(act, [&](auto tag) {
       constexpr int A = decltype(tag)::value;
 #pragma unroll
-      for (int o = 0; o < OC; o += 4) {
-        float4 v = make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
-        if (rp) {
-          const float4 r = *reinterpret_cast<const float4*>(rp + o);
-          v.x += r.x; v.y += r.y; v.z += r.z; v.w += r.w;
+      for (int i = 0; i < OC / 4; ++i) {
+        const int e4 = i * 32 + lane;  // float4 index within the run
+        if (e4 < valid) {
+          const int px = (e4 * 4) / OC, ch = (e4 * 4) % OC;
+          float4 v = *reinterpret_cast<const float4*>(stage + px * kStride + ch);
+          if (rb) {
+            const float4 r = *reinterpret_cast<const float4*>(rb + (size_t)e4 * 4);
+            v.x += r.x; v.y += r.y; v.z += r.z; v.w += r.w;
+          }
+          v.x = act_c<A>(v.x); v.y = act_c<A>(v.y);
+          v.z = act_c<A>(v.z); v.w = act_c<A>(v.w);
+          *reinterpret_cast<float4*>(yb + (size_t)e4 * 4) = v;
         }
-        v.x = act_c<A>(v.x); v.y = act_c<A>(v.y);
-        v.z = act_c<A>(v.z); v.w = act_c<A>(v.w);
-        *reinterpret_cast<float4*>(yp + o) = v;
       }
     });
   }
@@ -192,19 +251,26 @@ int try_conv_smallk(cudaStream_t s, int64_t* cnt, const float* x, const float* w
       (int64_t)p->n * p->ih * p->iw * p->ic >= INT32_MAX)
     return -1;
   const int total = p->n * p->oh * p->ow;
-  const size_t smem = ((size_t)K * p->oc + p->oc) * sizeof(float);
+  // weights + bias, then 4 warps x 32 rows x (oc + 4) floats of output staging
+  const size_t smem = ((size_t)K * p->oc + p->oc + 4 * 32 * (p->oc + 4)) * sizeof(float);
   const int grid = grid_for(total, 128, 16);
   const int dh = p->dilation_h > 0 ? p->dilation_h : 1, dw = p->dilation_w > 0 ? p->dilation_w : 1;
-#define SPX_SMALLK(OCV)                                                                        \
-  conv_smallk_kernel<OCV><<<grid, 128, smem, s>>>(x, w, bias, res, y, p->n, p->ih, p->iw,      \
+#define SPX_SMALLK(...)                                                                        \
+  if (smem > 48 * 1024)                                                                        \
+    cudaFuncSetAttribute(conv_smallk_kernel<__VA_ARGS__>,                                      \
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);              \
+  conv_smallk_kernel<__VA_ARGS__><<<grid, 128, smem, s>>>(x, w, bias, res, y, p->n, p->ih, p->iw,      \
                                                   p->ic, p->oh, p->ow, p->kh, p->kw,           \
                                                   p->stride_h, p->stride_w, p->pad_top,        \
                                                   p->pad_left, dh, dw, p->activation,          \
                                                   p->weight_layout)
+  const bool k333 = p->kh == 3 && p->kw == 3 && p->ic == 3;
   switch (p->oc) {
     case 8: SPX_SMALLK(8); break;
     case 16: SPX_SMALLK(16); break;
-    case 32: SPX_SMALLK(32); break;
+    case 32:
+      if (k333) { SPX_SMALLK(32, 3, 3, 3); } else { SPX_SMALLK(32); }
+      break;
     default: SPX_SMALLK(64); break;
   }
 #undef SPX_SMALLK
