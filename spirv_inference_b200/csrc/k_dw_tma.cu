@@ -125,13 +125,15 @@ __global__ void __launch_bounds__(256, KH == 3 ? 2 : 1)
     int img, ty, tx, cc;
     tile_coords(t, img, ty, tx, cc);
     const int ch = cc * CB + cg * 4;
+    const bool live = ch < c;  // the last chunk may run past c (TMA fills zeros there)
     if (cc != cc_prev) {  // weights of this channel chunk, kept in registers
 #pragma unroll
       for (int ky = 0; ky < KH; ++ky)
 #pragma unroll
         for (int kx = 0; kx < KW; ++kx)
-          wr[ky][kx] = __ldg(reinterpret_cast<const float4*>(w + (ky * KW + kx) * c + ch));
-      if (bias) bv = __ldg(reinterpret_cast<const float4*>(bias + ch));
+          wr[ky][kx] = live ? __ldg(reinterpret_cast<const float4*>(w + (ky * KW + kx) * c + ch))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (bias && live) bv = __ldg(reinterpret_cast<const float4*>(bias + ch));
       cc_prev = cc;
     }
     if (!mb_wait(&full[b], (phase >> b) & 1)) s_abort = 1;
@@ -170,7 +172,7 @@ __global__ void __launch_bounds__(256, KH == 3 ? 2 : 1)
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const int oy = ty * TH + rb * R + r;
-        if (oy < oh && ox < ow) {
+        if (oy < oh && ox < ow && live) {
           float4 v = acc[r];
           v.x = act_c<A>(v.x);
           v.y = act_c<A>(v.y);
@@ -240,7 +242,7 @@ int launch_cfg(cudaStream_t s, const float* x, const float* w, const float* b, f
                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(SPX_ERR_CUDA, "dw tensor map encode failed (%d)", (int)r);
   const int tiles_h = (p->oh + TH - 1) / TH, tiles_w = (p->ow + TW - 1) / TW;
-  const int c_chunks = p->c / CB;
+  const int c_chunks = (p->c + CB - 1) / CB;
   const int64_t total = (int64_t)p->n * tiles_h * tiles_w * c_chunks;
   const size_t smem = 2 * kBufBytes + 128 + 64;
   auto kern = dw_tma_kernel<KH, KW, S, TH, TW, R, CB>;
@@ -266,15 +268,22 @@ bool a16(const void* q) { return ((uintptr_t)q & 15) == 0; }
 int try_dw_tma(cudaStream_t s, int64_t* cnt, const float* x, const float* w, const float* b,
                float* y, const spx_dw_params* p) {
   if (p->dilation_h > 1 || p->dilation_w > 1 || p->stride_h != p->stride_w) return -1;
-  // Output tiles are 8 x 16 (stride 1) or 4 x 16 pixels: on maps smaller than
+  // Output tiles are 8 x 16 (stride 1) or 4 x 16 pixels, 14 x 16 on 14 x 14
+  // stride-1 maps and 7 x 8 (128 channels) on 7 x 7 ones: elsewhere below
   // 14 x 14 most of a tile would be padding; the register kernel serves those.
-  if (p->oh < 14 || p->ow < 14) return -1;
+  const bool m14 = p->oh == 14 && p->ow == 14 && p->stride_h == 1;
+  const bool m7 = p->oh == 7 && p->ow == 7 && p->stride_h == 1 && p->c % 32 == 0;
+  if ((p->oh < 14 || p->ow < 14) && !m7) return -1;
   if (!a16(x) || !a16(w) || !a16(y) || (b && !a16(b))) return -1;
   if ((int64_t)p->n * p->oh * p->ow * p->c >= INT32_MAX) return -1;
   if ((int64_t)p->n * (p->oh / 8 + 1) * (p->ow / 8 + 1) * (p->c / 8) >= INT32_MAX) return -1;
   const int k = p->kh == p->kw ? p->kh : 0, st = p->stride_h;
   int rc = -1;
-  if (p->c % 32 == 0) {
+  if (m7 && k == 3) {
+    rc = launch_cfg<3, 3, 1, 7, 8, 7, 128>(s, x, w, b, y, p);
+  } else if (m14 && k == 3 && p->c % 32 == 0) {
+    rc = launch_cfg<3, 3, 1, 14, 16, 7, 32>(s, x, w, b, y, p);
+  } else if (p->c % 32 == 0) {
     if (k == 3 && st == 1) rc = launch_cfg<3, 3, 1, 8, 16, 4, 32>(s, x, w, b, y, p);
     else if (k == 3 && st == 2) rc = launch_cfg<3, 3, 2, 4, 16, 2, 32>(s, x, w, b, y, p);
     else if (k == 5 && st == 1) rc = launch_cfg<5, 5, 1, 8, 16, 4, 32>(s, x, w, b, y, p);

@@ -247,3 +247,26 @@ def test_cuda_graph_capture_and_launch_count(g):
     ref = np.clip(np.maximum(np.einsum("nhwc,oc->nhwo", (x * 2).astype(np.float64),
                                        w.download()[:, 0, 0, :].astype(np.float64)), 0), 0, 6)
     np.testing.assert_allclose(second, ref, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("n,ih,c,k,s", [(3, 7, 96, 3, 1), (2, 14, 64, 3, 1), (2, 14, 32, 3, 2),
+                                        (2, 16, 32, 3, 1), (2, 14, 64, 5, 1), (3, 7, 32, 5, 2),
+                                        (1, 15, 32, 3, 2)])
+@pytest.mark.parametrize("path", [0, 1])
+def test_depthwise_small_maps_all_paths(g, n, ih, c, k, s, path):
+    """Maps up to 16 x 16 through the automatic choice (TMA tiles where they
+    apply, path 0) and the register sliding window (path 1), against the
+    float64 reference."""
+    oh = -(-ih // s)
+    tot = max((oh - 1) * s + k - ih, 0)
+    pt = tot // 2
+    x, w, b = _r(n, ih, ih, c), _r(k, k, c), _r(c)
+    dy = g.alloc((n, oh, oh, c))
+    _lib.set_option("dw_path", path)
+    try:
+        g.depthwise_nhwc(g.tensor(x), g.tensor(w), g.tensor(b), dy, stride=(s, s), pad=(pt, pt),
+                         activation=_lib.ACT_RELU6)
+    finally:
+        _lib.set_option("dw_path", 0)
+    ref = _act(R.depthwise_nhwc(x, w, b, (s, s), (pt, pt), (oh, oh), (1, 1)), _lib.ACT_RELU6)
+    np.testing.assert_allclose(dy.download(), ref, rtol=1e-5, atol=1e-5)
