@@ -268,27 +268,27 @@ bool a16(const void* q) { return ((uintptr_t)q & 15) == 0; }
 int try_dw_tma(cudaStream_t s, int64_t* cnt, const float* x, const float* w, const float* b,
                float* y, const spx_dw_params* p) {
   if (p->dilation_h > 1 || p->dilation_w > 1 || p->stride_h != p->stride_w) return -1;
-  // Output tiles are 8 x 16 (stride 1) or 4 x 16 pixels, 14 x 16 on 14 x 14
-  // stride-1 maps and 7 x 8 (128 channels) on 7 x 7 ones: elsewhere below
-  // 14 x 14 most of a tile would be padding; the register kernel serves those.
-  const bool m14 = p->oh == 14 && p->ow == 14 && p->stride_h == 1;
-  const bool m7 = p->oh == 7 && p->ow == 7 && p->stride_h == 1 && p->c % 32 == 0;
+  // Tiles: 3x3 stride 1 as 14 x 16 outputs (7 rows per thread), 7 x 8 x 128
+  // channels on 7x7 maps; stride 2 and 5x5 as 4 x 16 / 8 x 16.  Channel
+  // chunks are 32 wide for c >= 32 (a partial last chunk reads the tensor
+  // map's zero fill and stores nothing), 16 wide below.  Under 14 x 14
+  // (except 7x7 stride 1) most of a tile would be padding: the register
+  // kernel serves those.
+  const bool m7 = p->oh == 7 && p->ow == 7 && p->stride_h == 1;
   if ((p->oh < 14 || p->ow < 14) && !m7) return -1;
-  if (!a16(x) || !a16(w) || !a16(y) || (b && !a16(b))) return -1;
+  if (p->c % 4 || !a16(x) || !a16(w) || !a16(y) || (b && !a16(b))) return -1;
   if ((int64_t)p->n * p->oh * p->ow * p->c >= INT32_MAX) return -1;
-  if ((int64_t)p->n * (p->oh / 8 + 1) * (p->ow / 8 + 1) * (p->c / 8) >= INT32_MAX) return -1;
+  if ((int64_t)p->n * (p->oh / 4 + 1) * (p->ow / 8 + 1) * (p->c / 4 + 1) >= INT32_MAX) return -1;
   const int k = p->kh == p->kw ? p->kh : 0, st = p->stride_h;
   int rc = -1;
-  if (m7 && k == 3) {
-    rc = launch_cfg<3, 3, 1, 7, 8, 7, 128>(s, x, w, b, y, p);
-  } else if (m14 && k == 3 && p->c % 32 == 0) {
-    rc = launch_cfg<3, 3, 1, 14, 16, 7, 32>(s, x, w, b, y, p);
-  } else if (p->c % 32 == 0) {
-    if (k == 3 && st == 1) rc = launch_cfg<3, 3, 1, 8, 16, 4, 32>(s, x, w, b, y, p);
+  if (p->c >= 32) {
+    if (m7) {
+      if (k == 3) rc = launch_cfg<3, 3, 1, 7, 8, 7, 128>(s, x, w, b, y, p);
+    } else if (k == 3 && st == 1) rc = launch_cfg<3, 3, 1, 14, 16, 7, 32>(s, x, w, b, y, p);
     else if (k == 3 && st == 2) rc = launch_cfg<3, 3, 2, 4, 16, 2, 32>(s, x, w, b, y, p);
     else if (k == 5 && st == 1) rc = launch_cfg<5, 5, 1, 8, 16, 4, 32>(s, x, w, b, y, p);
     else if (k == 5 && st == 2) rc = launch_cfg<5, 5, 2, 4, 16, 2, 32>(s, x, w, b, y, p);
-  } else if (p->c % 16 == 0) {
+  } else if (p->c % 16 == 0 && !m7) {
     if (k == 3 && st == 1) rc = launch_cfg<3, 3, 1, 8, 32, 4, 16>(s, x, w, b, y, p);
     else if (k == 3 && st == 2) rc = launch_cfg<3, 3, 2, 4, 32, 2, 16>(s, x, w, b, y, p);
     else if (k == 5 && st == 1) rc = launch_cfg<5, 5, 1, 8, 32, 4, 16>(s, x, w, b, y, p);
