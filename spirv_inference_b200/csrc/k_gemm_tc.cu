@@ -93,6 +93,13 @@ struct TcArgs {
   float alpha;
   int act;
   int vec4;
+  // Implicit-GEMM convolution (conv != 0): A is gathered per k-block by a
+  // 4-D TMA box over the NHWC input; an M tile is a patch of tn images x th
+  // rows x tw columns of output pixels (tn * th * tw <= 128 rows).
+  int conv;
+  int oh, ow, ic_blocks, kw, sh, pt, pl;
+  int th, tw, tn, tiles_h, tiles_w;
+  uint32_t a_tx;  // bytes one A load delivers
 };
 
 __device__ __forceinline__ uint32_t su32(const void* p) {
@@ -158,6 +165,32 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(su32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(su32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(su32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// Output pixel index (n * oh + oy) * ow + ox of row r of conv M tile mt, or
+// -1 for rows outside the patch or the map.
+__device__ __forceinline__ int64_t conv_row(const TcArgs& p, int mt, int r) {
+  const int per = p.th * p.tw;
+  if (r >= p.tn * per) return -1;
+  const int ni = r / per, rem = r % per;
+  const int tx = mt % p.tiles_w;
+  const int t2 = mt / p.tiles_w;
+  const int ty = t2 % p.tiles_h;
+  const int nb = t2 / p.tiles_h;
+  const int img = nb * p.tn + ni;
+  const int oy = ty * p.th + rem / p.tw, ox = tx * p.tw + rem % p.tw;
+  if (oy >= p.oh || ox >= p.ow) return -1;
+  const int64_t pix = ((int64_t)img * p.oh + oy) * p.ow + ox;
+  return pix < p.M ? pix : -1;
 }
 
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
@@ -306,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0, armed = 0, armed_par = 0;
-      const uint32_t tx = kATileBytes + p.b_bytes * (p.presplit ? 2u : 1u);
+      const uint32_t tx = p.a_tx + p.b_bytes * (p.presplit ? 2u : 1u);
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         const int mt = t / p.n_tiles, nt = t % p.n_tiles;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
@@ -314,7 +347,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* st = smem + (size_t)s * p.stage_bytes;
           bar_expect_tx(&full[s], tx);
           if (kb == 0) TC_TRACE(0, (t - blockIdx.x) / gridDim.x);
-          tma_load_2d(st, &tmA, &full[s], kb * kBK, mt * kBM);
+          if (p.conv) {
+            // k-block -> (tap, 32-channel block); the box starts at the
+            // patch origin shifted by the tap, padding comes from the zero fill.
+            const int tap = kb / p.ic_blocks, cb = kb % p.ic_blocks;
+            const int ky = tap / p.kw, kx = tap % p.kw;
+            const int tx0 = mt % p.tiles_w, t2 = mt / p.tiles_w;
+            const int ty0 = t2 % p.tiles_h, nb = t2 / p.tiles_h;
+            tma_load_4d(st, &tmA, &full[s], cb * kBK, tx0 * p.tw * p.sh + kx - p.pl,
+                        ty0 * p.th * p.sh + ky - p.pt, nb * p.tn);
+          } else {
+            tma_load_2d(st, &tmA, &full[s], kb * kBK, mt * kBM);
+          }
           tma_load_2d(st + 2 * kATileBytes, &tmB, &full[s], kb * kBK, nt * p.BN);
           if (p.presplit)
             tma_load_2d(st + 2 * kATileBytes + p.b_bytes, &tmBlo, &full[s], kb * kBK, nt * p.BN);
@@ -523,8 +567,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int rr = i * 4 + sub_r;
-          const int64_t m = row0 + rr;
-          if (m >= p.M || n >= p.N) continue;
+          const int64_t m = p.conv ? conv_row(p, mt, quarter * 32 + rr) : row0 + rr;
+          if (m < 0 || m >= p.M || n >= p.N) continue;
           float4 o = *reinterpret_cast<const float4*>(tile + rr * kEpiStride + sub_c);
           float* op = &o.x;
           const float* bp = &b4.x;
@@ -872,9 +916,69 @@ bool gemm_tc_eligible(const float* a, int64_t lda, const float* b, int64_t ldb, 
          ldb >= K && al16(a) && al16(b) && ldc >= N && c != nullptr;
 }
 
+namespace {
+// 4-D fp32 tensor map over an NHWC activation (dims C, W, H, N) whose box is
+// one conv M tile's worth of one k-block: 32 channels x tw x th x tn pixels,
+// traversed with the conv stride in W and H, 128-byte swizzle, zero fill.
+int make_conv_map(CUtensorMap* map, const float* x, const spx_conv_params* q, int tw, int th,
+                  int tn) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(SPX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[4] = {(cuuint64_t)q->ic, (cuuint64_t)q->iw, (cuuint64_t)q->ih,
+                        (cuuint64_t)q->n};
+  cuuint64_t strides[3] = {(cuuint64_t)q->ic * 4, (cuuint64_t)q->iw * q->ic * 4,
+                           (cuuint64_t)q->ih * q->iw * q->ic * 4};
+  cuuint32_t box[4] = {(cuuint32_t)kBK, (cuuint32_t)(tw * q->stride_w),
+                       (cuuint32_t)(th * q->stride_h), (cuuint32_t)tn};
+  cuuint32_t estr[4] = {1, (cuuint32_t)q->stride_w, (cuuint32_t)q->stride_h, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)x, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SPX_ERR_CUDA, "conv tensor map encode failed (%d)", (int)r);
+  return SPX_OK;
+}
+}  // namespace
+
+bool conv_tc_eligible(const float* x, const float* w, const float* y,
+                      const spx_conv_params* q) {
+  auto al16 = [](const void* v) { return ((uintptr_t)v & 15) == 0; };
+  const int dh = q->dilation_h > 0 ? q->dilation_h : 1, dw = q->dilation_w > 0 ? q->dilation_w : 1;
+  return q->weight_layout == SPX_WEIGHT_OHWI && dh == 1 && dw == 1 && q->ic % kBK == 0 &&
+         q->stride_h == q->stride_w && q->stride_h <= 8 && q->ow * q->stride_w <= 256 &&
+         q->oc > 0 && al16(x) && al16(w) && y != nullptr &&
+         (int64_t)q->n * q->oh * q->ow < INT32_MAX;
+}
+
+int launch_conv_tc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
+                   const float* w_lo, const float* bias, const float* res, float* y,
+                   const spx_conv_params* q) {
+  // Output patch per 128-row tile: whole rows (tw = ow when it fits), as
+  // many rows as fit, and several images when a whole map fits.
+  const int tw = q->ow <= kBM ? q->ow : kBM;
+  int th = kBM / tw;
+  if (th > q->oh) th = q->oh;
+  // Fewer, fuller row bands: the smallest th with the same number of bands.
+  const int bands = (q->oh + th - 1) / th;
+  th = (q->oh + bands - 1) / bands;
+  int tn = th == q->oh ? kBM / (th * tw) : 1;
+  if (tn > q->n) tn = q->n;
+  if (tn < 1) tn = 1;
+  if (tw * q->stride_w > 256 || th * q->stride_h > 256)
+    return fail(SPX_ERR_UNSUPPORTED, "conv_tc: patch exceeds a TMA box");
+  CUtensorMap mx;
+  int rc = make_conv_map(&mx, x, q, tw, th, tn);
+  if (rc) return rc;
+  ConvGeom g = {q->oh, q->ow, q->ic / kBK, q->kw, q->stride_h, q->pad_top, q->pad_left,
+                th, tw, tn, (q->oh + th - 1) / th, (q->ow + tw - 1) / tw};
+  const int K = q->kh * q->kw * q->ic;
+  return launch_gemm_tc(s, cnt, x, K, w, w_lo, K, q->n * q->oh * q->ow, q->oc, K, bias, res, y,
+                        q->oc, 1.0f, q->activation, &g, &mx, (q->n + tn - 1) / tn);
+}
+
 int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, const float* b,
                    const float* b_lo, int64_t ldb, int M, int N, int K, const float* bias,
-                   const float* res, float* c, int64_t ldc, float alpha, int act) {
+                   const float* res, float* c, int64_t ldc, float alpha, int act,
+                   const ConvGeom* conv, const void* conv_map, int conv_img_groups) {
   TcArgs p = {};
   p.M = M;
   p.N = N;
@@ -884,7 +988,7 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   // halved while there are fewer than two tiles per SM.
   const int nt0 = (N + 255) / 256;
   p.BN = ((N + nt0 - 1) / nt0 + 31) / 32 * 32;
-  p.m_tiles = (M + kBM - 1) / kBM;
+  p.m_tiles = conv ? conv_img_groups * conv->tiles_h * conv->tiles_w : (M + kBM - 1) / kBM;
   // More, narrower tiles only pay while the k-loop is short: every n-tile
   // re-splits the same A tiles and narrow UMMAs cost nearly as much to issue
   // as wide ones.
@@ -919,10 +1023,29 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   p.act = act;
   auto al16 = [](const void* q) { return ((uintptr_t)q & 15) == 0; };
   p.vec4 = (ldc % 4 == 0) && al16(c) && (!res || al16(res)) && (!bias || al16(bias));
-  p.tma_store = p.vec4;
+  p.tma_store = p.vec4 && !conv;
+  p.a_tx = kATileBytes;
   CUtensorMap ma, mb, mblo;
   int rc;
-  if ((rc = make_map(&ma, a, M, K, lda, kBM))) return rc;
+  if (conv) {
+    p.conv = 1;
+    p.oh = conv->oh;
+    p.ow = conv->ow;
+    p.ic_blocks = conv->ic_blocks;
+    p.kw = conv->kw;
+    p.sh = conv->sh;
+    p.pt = conv->pt;
+    p.pl = conv->pl;
+    p.th = conv->th;
+    p.tw = conv->tw;
+    p.tn = conv->tn;
+    p.tiles_h = conv->tiles_h;
+    p.tiles_w = conv->tiles_w;
+    p.a_tx = (uint32_t)(conv->tn * conv->th * conv->tw) * kBK * 4;
+    ma = *reinterpret_cast<const CUtensorMap*>(conv_map);
+  } else if ((rc = make_map(&ma, a, M, K, lda, kBM))) {
+    return rc;
+  }
   if ((rc = make_map(&mb, b, N, K, ldb, p.BN))) return rc;
   mblo = mb;
   if (p.presplit && (rc = make_map(&mblo, b_lo, N, K, ldb, p.BN))) return rc;

@@ -65,6 +65,12 @@ int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* 
       return launch_gemm_tc(s, cnt, x, p->ic, wb, split ? w_lo : nullptr, p->ic, M, p->oc, p->ic,
                             bias, res, y, p->oc, 1.0f, p->activation);
   }
+  if (g_gemm_path != 1 && !pointwise) {
+    const bool split = w_hi && w_lo;
+    const float* wb = split ? w_hi : w;
+    if (conv_tc_eligible(x, wb, y, p) && (!split || ((uintptr_t)w_lo & 15) == 0))
+      return launch_conv_tc(s, cnt, x, wb, split ? w_lo : nullptr, bias, res, y, p);
+  }
   if (g_gemm_path == 2)
     return fail(SPX_ERR_UNSUPPORTED, "conv2d_nhwc: shape not eligible for the tensor-core path");
   if (!pointwise) {

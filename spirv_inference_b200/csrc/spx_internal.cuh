@@ -194,9 +194,21 @@ bool gemm_tc_eligible(const float* a, int64_t lda, const float* b, int64_t ldb, 
                       int K, const float* c, int64_t ldc);
 // b_lo != nullptr: B is given pre-split (b = tf32 hi terms, b_lo = lo terms,
 // from launch_weights_split); otherwise B is split on chip.
+// Implicit-GEMM convolution geometry for launch_gemm_tc (k_gemm_tc.cu).
+struct ConvGeom {
+  int oh, ow, ic_blocks, kw, sh, pt, pl, th, tw, tn, tiles_h, tiles_w;
+};
 int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, const float* b,
                    const float* b_lo, int64_t ldb, int M, int N, int K, const float* bias,
-                   const float* res, float* c, int64_t ldc, float alpha, int act);
+                   const float* res, float* c, int64_t ldc, float alpha, int act,
+                   const ConvGeom* conv = nullptr, const void* conv_map = nullptr,
+                   int conv_img_groups = 0);
+// KxK / strided convolutions on tensor cores: NHWC input, OHWI weights
+// (w_lo non-null: w is the pre-split hi part), ic a multiple of 32.
+bool conv_tc_eligible(const float* x, const float* w, const float* y, const spx_conv_params* q);
+int launch_conv_tc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
+                   const float* w_lo, const float* bias, const float* res, float* y,
+                   const spx_conv_params* q);
 bool gemm_tc_skinny_eligible(const float* a, int64_t lda, const float* w, int64_t ldw, int M,
                              int N, int K);
 // w_lo non-null: w is the pre-split hi part (spx_weights_split) and w_lo the lo part.

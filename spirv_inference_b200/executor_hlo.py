@@ -369,7 +369,9 @@ class HloExecutor:
             self.done.update(consumed)
         out = self._new(op.shape)
         pointwise = kh == 1 and kw == 1 and tuple(st) == (1, 1)
-        if pointwise:  # OHWI copy (the tensor-core B operand), pre-split once
+        # Tensor-core convs (pointwise GEMM, or the implicit GEMM of KxK /
+        # strided convs over 32-channel blocks) take an OHWI copy, pre-split once.
+        if pointwise or w.shape[2] % 32 == 0:
             wt = self._weight_buf(wname, np.ascontiguousarray(w.transpose(3, 0, 1, 2)), "ohwi")
             split = self.g.weights_split(wt) if self.presplit else None
             layout = _lib.WEIGHT_OHWI

@@ -3,6 +3,7 @@ gemm_path = 2) against float64 numpy and the exact-fp32 SIMT path."""
 import numpy as np
 import pytest
 
+import _np_ref as R
 from spirv_inference_b200 import _lib
 from spirv_inference_b200.graph import Graph
 
@@ -105,4 +106,34 @@ def test_tc_presplit_weights_match_on_chip_split(g, M, N, K):
     np.testing.assert_array_equal(outs[0], outs[1])
     ref = np.maximum(a.astype(np.float64) @ w.T.astype(np.float64) + res, 0)
     err = np.abs(outs[1] - ref).max() / np.abs(ref).max()
+    assert err <= 2.5e-8 * K + 1e-6, err
+
+
+@pytest.mark.parametrize("n,ih,ic,oc,k,s,pad", [(2, 56, 64, 64, 3, 1, 1), (2, 56, 64, 128, 3, 2, 1),
+                                               (3, 7, 64, 96, 3, 1, 1), (2, 14, 32, 64, 3, 1, 1),
+                                               (2, 28, 128, 64, 1, 2, 0), (1, 15, 32, 48, 5, 1, 2),
+                                               (5, 7, 128, 32, 3, 2, 1), (2, 9, 32, 40, 3, 1, 0)])
+def test_conv_tc_implicit_gemm(g, n, ih, ic, oc, k, s, pad):
+    """KxK / strided convs as implicit GEMM on tensor cores (4-D TMA boxes of
+    the NHWC input per tap, zero fill as padding) against float64."""
+    oh = (ih + 2 * pad - k) // s + 1
+    x = _r(n, ih, ih, ic)
+    w = _r(oc, k, k, ic, scale=1.0 / np.sqrt(k * k * ic))   # OHWI
+    b, res = _r(oc), _r(n, oh, oh, oc)
+    dx, dw, db, dr = g.tensor(x), g.tensor(w), g.tensor(b), g.tensor(res)
+    ref = R.conv_nhwc(x, np.transpose(w, (1, 2, 3, 0)), (s, s), (pad, pad), (oh, oh)) + b + res
+    ref = np.maximum(ref, 0)
+    outs = []
+    for split in (None, g.weights_split(dw)):
+        dy = g.alloc((n, oh, oh, oc))
+        _lib.set_option("gemm_path", 2)
+        try:
+            g.conv2d_nhwc(dx, dw, db, dy, stride=(s, s), pad=(pad, pad), residual=dr,
+                          activation=_lib.ACT_RELU, w_split=split)
+        finally:
+            _lib.set_option("gemm_path", 0)
+        outs.append(dy.download())
+    np.testing.assert_array_equal(outs[0], outs[1])
+    K = k * k * ic
+    err = np.abs(outs[0] - ref).max() / np.abs(ref).max()
     assert err <= 2.5e-8 * K + 1e-6, err
