@@ -47,8 +47,11 @@ def test_hlo_executor_matches_oracle(gpu, oracle_runs, name, fuse):
     finally:
         ex.close()
     assert got.shape == ref.shape
-    # logits / activations: <= 1e-3 relative (north-star gate), fp32 here gives ~1e-5
-    assert _normerr(got, ref) <= 1e-4, _normerr(got, ref)
+    # logits / activations: <= 1e-3 relative (north-star gate).  ResNet runs
+    # every conv on 3xTF32 tensor cores whose accumulate rounds toward zero:
+    # ~1e-4 after 53 convs; the BERT graphs stay near 1e-5.
+    tol = 1e-3 if name.startswith("resnet") else 1e-4
+    assert _normerr(got, ref) <= tol, _normerr(got, ref)
     if name.startswith("resnet"):
         np.testing.assert_array_equal(np.argmax(got, 1), np.argmax(ref, 1))
 
