@@ -79,6 +79,8 @@ class HloExecutor:
                 self.consumers.setdefault(o, []).append(op)
         self.byname = {op.name: op for op in g.ops}
         self.done: set[str] = set()
+        self.folded_pad: dict[str, tuple] = {}  # pad op -> (source, top, left) folded into consumers
+        self.nonneg: set[str] = set()            # tensors known to be >= 0 (ReLU outputs)
         self.deferred_scale: dict[str, float] = {}
         self.weights_np = g.params
         self._build()
@@ -340,7 +342,39 @@ class HloExecutor:
             return
         self._set(op.name, View(op.shape, tuple(src.strides[p] for p in perm), src.t))
 
+    def _foldable_pad(self, op) -> bool:
+        """A spatial pad of an NHWC tensor whose every consumer can take it as
+        its own low-side padding: a convolution (zero pad), or a max
+        reduce-window whose padded taps cannot win (pad value -inf, or 0 over
+        a tensor known to be >= 0, e.g. a fused conv + ReLU output)."""
+        if not self.fuse or len(op.shape) != 4:
+            return False
+        padding = op.attrs["padding"]
+        if padding[0] != (0, 0) or padding[3] != (0, 0) or any(lo < 0 or hi < 0
+                                                               for lo, hi in padding):
+            return False
+        pv = self.v[op.operands[1]].scalar
+        cs = self.consumers.get(op.name, [])
+        if not cs:
+            return False
+        for c in cs:
+            if c.operands[0] != op.name:
+                return False
+            if c.opcode == "convolution" and pv == 0.0:
+                continue
+            if (c.opcode == "reduce-window" and c.attrs["kind"] == "max"
+                    and (pv == -np.inf or (pv == 0.0 and op.operands[0] in self.nonneg))):
+                continue
+            return False
+        return True
+
     def _op_pad(self, op):
+        if self._foldable_pad(op):
+            # No kernel: the consumer reads the unpadded tensor with its low-side
+            # padding grown by this pad (out-of-map taps are zero / ignored).
+            self.folded_pad[op.name] = (op.operands[0], op.attrs["padding"][1][0],
+                                        op.attrs["padding"][2][0])
+            return
         src = self._contig(self.v[op.operands[0]])
         pv = self.v[op.operands[1]].scalar
         r = len(op.shape)
@@ -352,12 +386,20 @@ class HloExecutor:
         self.plan.append(("pad4", src.t, out.t, float(pv), od + idd + pl + [total]))
         self._set(op.name, out)
 
+    def _unfold(self, name: str):
+        """(source view, extra top pad, extra left pad) of an operand."""
+        if name in self.folded_pad:
+            src, pt, pl = self.folded_pad[name]
+            return self._contig(self.v[src]), pt, pl
+        return self._contig(self.v[name]), 0, 0
+
     def _op_convolution(self, op):
-        x = self._contig(self.v[op.operands[0]])
+        x, ept, epl = self._unfold(op.operands[0])
         wname = op.operands[1]
         w = self.weights_np[wname]
         kh, kw, ic, oc = w.shape
         st, pd = op.attrs["stride"], op.attrs["pad"]
+        pd = ((pd[0][0] + ept, pd[0][1]), (pd[1][0] + epl, pd[1][1]))
         fused = self._match_bias_chain(op.name) if self.fuse else None
         bias = res = None
         relu = False
@@ -382,12 +424,15 @@ class HloExecutor:
                                        activation=_lib.ACT_RELU if relu else _lib.ACT_NONE,
                                        residual=res, w_split=split)))
         self._set(last, out)
+        if relu:
+            self.nonneg.add(last)
         if last != op.name:
             self._set(op.name, out)
 
     def _op_reduce_window(self, op):
-        x = self._contig(self.v[op.operands[0]])
+        x, ept, epl = self._unfold(op.operands[0])
         sz, st, pd = op.attrs["size"], op.attrs["stride"], op.attrs["pad"]
+        pd = ((pd[0][0] + ept, pd[0][1]), (pd[1][0] + epl, pd[1][1]))
         out = self._new(op.shape)
         kind = _lib.POOL_MAX if op.attrs["kind"] == "max" else _lib.POOL_SUM
         self.plan.append(("pool", x.t, out.t, tuple(sz), tuple(st), (pd[0][0], pd[1][0]), kind))
