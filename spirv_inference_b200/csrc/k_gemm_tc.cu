@@ -76,7 +76,6 @@ constexpr int kEpiStride = 36;   // floats per row of a warp's transpose tile
 // 128-byte-swizzled layout (4 KB), or the padded transpose tile of the
 // fallback path (32 x kEpiStride floats).
 constexpr uint32_t kEpiSlot = 5120;
-constexpr uint32_t kEpiBytes = kEpiWarps * kEpiSlot;
 constexpr uint32_t kATileBytes = kBM * kBK * 4;       // 16 KB
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 constexpr unsigned long long kDrainNs = 200000000ull;     // 0.2 s drain on abort
@@ -100,6 +99,7 @@ struct TcArgs {
   int oh, ow, ic_blocks, kw, sh, pt, pl;
   int th, tw, tn, tiles_h, tiles_w;
   uint32_t a_tx;  // bytes one A load delivers
+  int epi_warps;  // epilogue warps in use (4 or 8): long k-loops trade them for stages
 };
 
 __device__ __forceinline__ uint32_t su32(const void* p) {
@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int S = p.stages;
   uint8_t* epi = smem + (size_t)S * p.stage_bytes;  // kEpiWarps slots of kEpiSlot bytes
-  uint64_t* full = (uint64_t*)(epi + kEpiBytes);
+  uint64_t* full = (uint64_t*)(epi + p.epi_warps * kEpiSlot);
   uint64_t* conv = full + kMaxStages;
   uint64_t* empty = conv + kMaxStages;
   uint64_t* tfull = empty + kMaxStages;
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       bar_init(&tfull[a], 1);
-      bar_init(&tempty[a], kEpiWarps * 32);
+      bar_init(&tempty[a], p.epi_warps * 32);
     }
     for (int w = 0; w < kEpiWarps; ++w) bar_init(&rfull[w], 1);
     bar_init(drain, 1);
@@ -452,6 +452,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   conv_done:;
+  } else if (warp >= p.epi_warps) {
+    // epilogue warp not in use for this launch
   } else if (p.tma_store) {
     // ---------------- epilogue via TMA (warps 0 .. kEpiWarps-1) ----------------
     // Warp w reads TMEM lane quarter w % 4 (lane = tile row) and takes every
@@ -476,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int quarter = warp & 3;
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.BN);
       const int row0 = mt * kBM + quarter * 32;
-      for (int c0 = (warp >> 2) * 32; c0 < p.BN; c0 += 32 * (kEpiWarps / 4)) {
+      for (int c0 = (warp >> 2) * 32; c0 < p.BN; c0 += 32 * (p.epi_warps / 4)) {
         const int n0 = nt * p.BN + c0;
         if (n0 >= p.N) break;  // uniform across the warp
         // The lane that issued the previous store waits until it has read the
@@ -547,7 +549,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int quarter = warp & 3;
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.BN);
       const int64_t row0 = (int64_t)mt * kBM + quarter * 32;
-      for (int c0 = (warp >> 2) * 32; c0 < p.BN; c0 += 32 * (kEpiWarps / 4)) {
+      for (int c0 = (warp >> 2) * 32; c0 < p.BN; c0 += 32 * (p.epi_warps / 4)) {
         float v[32];
         tmem_ld32(tbase + (uint32_t)c0, v);  // lane = row, 32 consecutive columns
         float4* trow = reinterpret_cast<float4*>(tile + lane * kEpiStride);
@@ -997,9 +999,15 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   while (p.BN > 32 && (int64_t)p.m_tiles * ((N + p.BN - 1) / p.BN) <
                           (kb_total <= 4 ? 2 * sm_count() : sm_count() / 2))
     p.BN = (p.BN / 2 + 31) / 32 * 32;
-  // At least two pipeline stages must fit next to the epilogue tiles.
-  const int budget = 227 * 1024 - 1024 - (int)kEpiBytes - 512;
-  while (p.BN > 32 && budget / (int)(2 * kATileBytes + 2 * (uint32_t)p.BN * kBK * 4) < 2)
+  // Long k-loops keep the tensor pipe busy only with several stages in
+  // flight; their epilogue is rare, so they give up half the epilogue warps
+  // (and staging) for stages.  At least two stages must fit (three for long
+  // k-loops) next to the epilogue tiles.
+  p.epi_warps = kb_total >= 8 ? 4 : kEpiWarps;
+  const int budget = 227 * 1024 - 1024 - p.epi_warps * (int)kEpiSlot - 512;
+  const int min_stages = kb_total >= 8 ? 3 : 2;
+  while (p.BN > 32 &&
+         budget / (int)(2 * kATileBytes + 2 * (uint32_t)p.BN * kBK * 4) < min_stages)
     p.BN = (p.BN / 2 + 31) / 32 * 32;
   p.n_tiles = (N + p.BN - 1) / p.BN;
   p.k_blocks = (K + kBK - 1) / kBK;
@@ -1054,7 +1062,8 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
     if ((rc = make_map(&mc, c, M, N, ldc, 32))) return rc;
     if (res && (rc = make_map(&mr, res, M, N, ldc, 32))) return rc;
   }
-  const size_t smem = 1024 + (size_t)p.stages * p.stage_bytes + kEpiBytes + 512;
+  const size_t smem =
+      1024 + (size_t)p.stages * p.stage_bytes + p.epi_warps * (size_t)kEpiSlot + 512;
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
