@@ -999,16 +999,21 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   while (p.BN > 32 && (int64_t)p.m_tiles * ((N + p.BN - 1) / p.BN) <
                           (kb_total <= 4 ? 2 * sm_count() : sm_count() / 2))
     p.BN = (p.BN / 2 + 31) / 32 * 32;
-  // Long k-loops keep the tensor pipe busy only with several stages in
-  // flight; their epilogue is rare, so they give up half the epilogue warps
-  // (and staging) for stages.  At least two stages must fit (three for long
-  // k-loops) next to the epilogue tiles.
-  p.epi_warps = kb_total >= 8 ? 4 : kEpiWarps;
-  const int budget = 227 * 1024 - 1024 - p.epi_warps * (int)kEpiSlot - 512;
-  const int min_stages = kb_total >= 8 ? 3 : 2;
-  while (p.BN > 32 &&
-         budget / (int)(2 * kATileBytes + 2 * (uint32_t)p.BN * kBK * 4) < min_stages)
+  // At least two pipeline stages must fit next to the epilogue tiles.
+  const int full_budget = 227 * 1024 - 1024 - kEpiWarps * (int)kEpiSlot - 512;
+  while (p.BN > 32 && full_budget / (int)(2 * kATileBytes + 2 * (uint32_t)p.BN * kBK * 4) < 2)
     p.BN = (p.BN / 2 + 31) / 32 * 32;
+  // Long k-loops keep the tensor pipe busy only with several stages in
+  // flight; their epilogue is rare, so when that buys a third stage they
+  // give up half the epilogue warps (and their staging tiles).
+  p.epi_warps = kEpiWarps;
+  {
+    const int bn_stage = (int)(2 * kATileBytes + 2 * (uint32_t)p.BN * kBK * 4);
+    const int half_budget = 227 * 1024 - 1024 - 4 * (int)kEpiSlot - 512;
+    if (kb_total >= 8 && full_budget / bn_stage < 3 && half_budget / bn_stage >= 3)
+      p.epi_warps = 4;
+  }
+  const int budget = 227 * 1024 - 1024 - p.epi_warps * (int)kEpiSlot - 512;
   p.n_tiles = (N + p.BN - 1) / p.BN;
   p.k_blocks = (K + kBK - 1) / kBK;
   p.b_bytes = (uint32_t)p.BN * kBK * 4;
