@@ -385,6 +385,26 @@ int spx_op_argmax_partial(spx_graph* g, const float* x, int64_t ldx, int32_t row
 int spx_op_argmax_merge(spx_graph* g, const float* packed, int32_t parts, int32_t rows,
                         int32_t* ids);
 
+/* ---- one-shot all-reduce over peer memory (tensor-parallel decode) ------
+ * No counterpart in the reference (its TP plan names an NCCL all-reduce,
+ * which this replaces for small messages).  Each rank creates a
+ * communicator with two data slots of max_bytes, exports its handle
+ * (spx_ar_handle, spx_ar_handle_size() bytes), gathers every rank's handle
+ * (rank order) and opens them (spx_ar_open).  A producer writes this rank's
+ * partial sum into spx_ar_slot(a, s); spx_op_allreduce sums slot s of all
+ * ranks into out (out must not alias a slot).  Consecutive all-reduces must
+ * alternate slots 0 / 1 and be issued in the same order on every rank.
+ * Waits for peers are bounded (2 s); a timeout is reported as SPX_ERR_CUDA
+ * at the next graph sync. */
+typedef struct spx_ar spx_ar;
+int spx_ar_create(int32_t device, int32_t rank, int32_t world, size_t max_bytes, spx_ar** out);
+size_t spx_ar_handle_size(void);
+int spx_ar_handle(spx_ar* a, void* handle, size_t handle_bytes);
+int spx_ar_open(spx_ar* a, const void* handles);
+float* spx_ar_slot(spx_ar* a, int32_t slot);
+int spx_op_allreduce(spx_graph* g, spx_ar* a, int32_t slot, float* out, int64_t n);
+int spx_ar_destroy(spx_ar* a);
+
 /* Rank-4 constant pad (pad.comp with the reference's 13 push constants
  * od0..3, id0..3, pl0..3, total) and rank-4 permutation (transpose.comp's
  * 13 push constants in0..3, out0..3, p0..3, total). */

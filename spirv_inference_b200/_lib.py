@@ -151,6 +151,13 @@ _SIGS = {
     "spx_op_argmax_partial": ([c_void_p, c_void_p, c_int64, c_int32, c_int32, c_int32,
                                c_void_p], c_int),
     "spx_op_argmax_merge": ([c_void_p, c_void_p, c_int32, c_int32, c_void_p], c_int),
+    "spx_ar_create": ([c_int32, c_int32, c_int32, ctypes.c_size_t, POINTER(c_void_p)], c_int),
+    "spx_ar_handle_size": ([], ctypes.c_size_t),
+    "spx_ar_handle": ([c_void_p, c_void_p, ctypes.c_size_t], c_int),
+    "spx_ar_open": ([c_void_p, c_void_p], c_int),
+    "spx_ar_slot": ([c_void_p, c_int32], c_void_p),
+    "spx_op_allreduce": ([c_void_p, c_void_p, c_int32, c_void_p, c_int64], c_int),
+    "spx_ar_destroy": ([c_void_p], c_int),
     "spx_op_pad4": ([c_void_p, c_void_p, c_void_p, c_float, _IP], c_int),
     "spx_op_transpose4": ([c_void_p, c_void_p, c_void_p, _IP], c_int),
 }

@@ -473,6 +473,8 @@ static int device_status(const char* what) {
   if (tc_take_status())
     return fail(SPX_ERR_CUDA, "%s: a tensor-core pipeline wait timed out; tiles were abandoned",
                 what);
+  if (ar_take_status())
+    return fail(SPX_ERR_CUDA, "%s: an all-reduce waited 2 s for a peer rank and gave up", what);
   return SPX_OK;
 }
 

@@ -221,6 +221,7 @@ int launch_weights_split(cudaStream_t s, int64_t* cnt, const float* w, float* hi
 // Returns and clears the device status of the tensor-core pipeline (0 = ok,
 // 1 = a pipeline wait timed out and the kernel aborted its tiles).
 int tc_take_status();
+int ar_take_status();
 
 // Process-wide dense-contraction path: 0 auto, 1 SIMT only, 2 tensor cores
 // required (ineligible shapes fail with SPX_ERR_UNSUPPORTED).

@@ -189,7 +189,8 @@ class LlamaDecoder:
 
     def __init__(self, cfg: LlamaConfig, weights: dict, batch: int, prompt_len: int,
                  n_new: int, *, device: int = 0, stream: int | None = None,
-                 rank: int = 0, world: int = 1, group=None, capture: bool = True):
+                 rank: int = 0, world: int = 1, group=None, capture: bool = True,
+                 peer_allreduce: bool = False):
         self.cfg, self.B, self.P, self.n_new = cfg, batch, prompt_len, n_new
         if prompt_len + n_new - 1 > cfg.max_seq:
             raise ValueError(f"prompt {prompt_len} + {n_new} new tokens exceed max_seq "
@@ -242,6 +243,17 @@ class LlamaDecoder:
             self.packed_all = self._torch_buf(torch.empty((world, batch, 2), device=dev))
         else:
             self.x_a, self.x_b = g.alloc((M, H)), g.alloc((M, H))
+        # Optionally, small all-reduces (decode steps; prefill when it is small
+        # too) go over peer memory: one kernel per all-reduce instead of an
+        # NCCL call.  Measured on 2 B200s it matches NCCL inside a captured
+        # step (b1 678 vs 708 tok/s, b64 15.6k vs 15.8k), so NCCL stays the
+        # default.
+        self.peer_ar = None
+        self._ar_slot = 0
+        if world > 1 and peer_allreduce:
+            from .comm import PeerAllReduce
+            self.peer_ar = PeerAllReduce(device, rank, world,
+                                         min(M, 256) * H * 4, group=group)
         self.capture = capture
         self._captured = False
         self._mark = None      # optional callback(label, bytes, flops) after each op
@@ -275,6 +287,27 @@ class LlamaDecoder:
         self._note(label, wb * n * k + 4.0 * (m * k + m * n * (2 if residual is not None else 1)),
                    2.0 * m * n * k)
 
+    def _row_parallel(self, a: DeviceTensor, lda: int, w: DeviceTensor, M: int,
+                      x_in: DeviceTensor, x_out: DeviceTensor) -> None:
+        """x_out = x_in + sum over ranks of a @ w^T (rank 0 adds the residual)."""
+        lead = self.rank == 0
+        H = self.cfg.hidden
+        if self.world == 1:
+            self._linear(a, lda, w, M, x_out, residual=x_in)
+            return
+        ar = self.peer_ar
+        if ar is not None and M * H * 4 <= ar.max_bytes:
+            s = self._ar_slot
+            self._ar_slot ^= 1
+            part = ar.slot(s, (M, H), self.g)
+            self._linear(a, lda, w, M, part, residual=x_in if lead else None)
+            ar.allreduce(self.g, s, x_out, M * H)
+            self._note("all_reduce", 4.0 * M * H * self.world)
+            return
+        self._linear(a, lda, w, M, x_out, residual=x_in if lead else None)
+        self._all_reduce(x_out, M)
+        self._note("all_reduce", 4.0 * M * H)
+
     # -- one pass over T tokens per sequence -------------------------------
     def _forward(self, ids: DeviceTensor, T: int) -> None:
         cfg, g, sh = self.cfg, self.g, self.sh
@@ -307,11 +340,7 @@ class LlamaDecoder:
                            scale=float(1.0 / np.sqrt(np.float32(D))), **kv)
             self._note("attention", 4.0 * (2 * B * sh.nkv * n_keys * D + 2 * M * sh.nq * D),
                        4.0 * B * sh.nq * T * n_keys * D)
-            self._linear(self.att, sh.nq * D, L["wo"], M, self.x_b,
-                         residual=self.x_a if lead else None)
-            if self.world > 1:
-                self._all_reduce(self.x_b, M)
-                self._note("all_reduce", 4.0 * M * H)
+            self._row_parallel(self.att, sh.nq * D, L["wo"], M, self.x_a, self.x_b)
             if few:
                 g.swiglu_linear(self.x_b, H, L["wgu"], H, M, sh.nf, H, self.mlp, sh.nf,
                                 rms_eps=eps)
@@ -323,11 +352,7 @@ class LlamaDecoder:
                 self._linear(self.h, H, L["wgu"], M, self.gu)
                 g.swiglu_rows(self.gu, 2 * sh.nf, self.mlp, sh.nf, M, sh.nf)
                 self._note("small", 12.0 * M * sh.nf)
-            self._linear(self.mlp, sh.nf, L["wdown"], M, self.x_a,
-                         residual=self.x_b if lead else None)
-            if self.world > 1:
-                self._all_reduce(self.x_a, M)
-                self._note("all_reduce", 4.0 * M * H)
+            self._row_parallel(self.mlp, sh.nf, L["wdown"], M, self.x_b, self.x_a)
         # Final norm + lm_head on the last position of every sequence.
         keys = None
         last_x = self.x_a.view((B, H), offset_elems=(T - 1) * H)
@@ -406,4 +431,8 @@ class LlamaDecoder:
         return self.logits.download()
 
     def close(self) -> None:
+        self.g.sync()
+        if self.peer_ar is not None:
+            self.peer_ar.close()
+            self.peer_ar = None
         self.g.close()

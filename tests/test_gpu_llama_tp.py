@@ -23,7 +23,61 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, batch, q, capture=True):
+def _ar_worker(rank, world, port, q):
+    """Peer-memory all-reduce kernel on its own: alternating slots, sizes
+    from one float4 to 256 KB, repeated so epochs advance."""
+    import torch.distributed as dist
+    from spirv_inference_b200.comm import PeerAllReduce
+    from spirv_inference_b200.graph import Graph
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    try:
+        g = Graph(rank)
+        ar = PeerAllReduce(rank, rank, world, 1 << 20)
+        errs = []
+        for it, n in enumerate([4, 1000, 65536, 4, 262144 // 4 * 4]):
+            slot = it % 2
+            data = [np.random.default_rng(100 * r + it).standard_normal(n).astype(np.float32)
+                    for r in range(world)]
+            part = ar.slot(slot, (n,), g)
+            g.upload(part, data[rank])
+            out = g.alloc((n,))
+            # every rank's slot is written before anyone reduces
+            g.sync()
+            dist.barrier()
+            ar.allreduce(g, slot, out, n)
+            got = out.download()
+            ref = data[0].astype(np.float64)
+            for r in range(1, world):
+                ref = ref + data[r]
+            errs.append(float(np.abs(got - ref).max()))
+        g.sync()
+        ar.close()
+        g.close()
+        q.put((rank, errs))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_allreduce_two_gpus(gpu):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ar_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert max(res[0] + res[1]) <= 1e-5
+
+
+def _worker(rank, world, port, batch, q, capture=True, peer=False):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -36,7 +90,8 @@ def _worker(rank, world, port, batch, q, capture=True):
         s = torch.cuda.Stream()
         torch.cuda.set_stream(s)
         dec = llama.LlamaDecoder(cfg, W, batch, 32, 12, device=rank, stream=s.cuda_stream,
-                                 rank=rank, world=world, capture=capture)
+                                 rank=rank, world=world, capture=capture,
+                                 peer_allreduce=peer)
         toks = dec.generate(prompt)
         toks2 = dec.generate(prompt)          # replay of the captured step
         assert np.array_equal(toks, toks2)
@@ -47,8 +102,8 @@ def _worker(rank, world, port, batch, q, capture=True):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("batch", [1, 12])
-def test_tp2_matches_single_gpu(gpu, batch):
+@pytest.mark.parametrize("batch,peer", [(1, False), (12, False), (1, True), (12, True)])
+def test_tp2_matches_single_gpu(gpu, batch, peer):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     cfg = llama.TINY_TEST
@@ -60,7 +115,8 @@ def test_tp2_matches_single_gpu(gpu, batch):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, batch, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, batch, q, True, peer))
+             for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in procs)
