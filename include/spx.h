@@ -206,6 +206,24 @@ typedef struct spx_dw_params {
 int spx_op_depthwise_conv2d_nhwc(spx_graph* g, const float* x, const float* w,
                                  const float* bias, float* y, const spx_dw_params* p);
 
+/* Fused MobileNet block front half (no counterpart op in the reference,
+ * which dispatches conv2d.comp then depthwise_conv2d.comp with the expanded
+ * tensor in memory between them, scheduler.rs:321-548):
+ *   e = act_expand(x . W_e^T + b_e)   (1x1 conv, x [n][ih][iw][cin],
+ *                                      W_e OHWI [ce][1][1][cin])
+ *   y = act_dw(depthwise3x3(e, W_d, stride, SAME) + b_d)
+ *                                     (W_d [3][3][ce], y [n][oh][ow][ce])
+ * The expanded tensor never leaves the chip.  cin must be 16, 24 or 32,
+ * ce a multiple of 4, stride 1 or 2 with oh = ceil(ih / stride); pads are
+ * the SAME offsets (pad_top / pad_left = floor(total / 2)). */
+typedef struct spx_expand_dw_params {
+  int32_t n, ih, iw, cin, ce, oh, ow, stride, pad_top, pad_left;
+  int32_t act_expand, act_dw;
+} spx_expand_dw_params;
+int spx_op_expand_dw_nhwc(spx_graph* g, const float* x, const float* w_expand,
+                          const float* b_expand, const float* w_dw, const float* b_dw, float* y,
+                          const spx_expand_dw_params* p);
+
 /* Batched strided GEMM: C[b][m][n] = act(alpha * sum_k A[b,m,k] B[b,k,n]
  * + bias[n] + R[b][m][n]).  Element strides let one entry cover
  * fully_connected (B = W^T), hlo_dot_rank2, hlo_dot_batched with any

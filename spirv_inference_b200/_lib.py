@@ -62,6 +62,11 @@ class GemmParams(Structure):
                 + [("alpha", c_float), ("activation", c_int32)])
 
 
+class ExpandDwParams(Structure):
+    _fields_ = [(n, c_int32) for n in ("n", "ih", "iw", "cin", "ce", "oh", "ow", "stride",
+                                       "pad_top", "pad_left", "act_expand", "act_dw")]
+
+
 class KvParams(Structure):
     _fields_ = [(n, c_int32) for n in ("batch", "q_len", "q_heads", "kv_heads", "head_dim",
                                        "max_seq")]
@@ -158,6 +163,7 @@ _SIGS = {
     "spx_ar_slot": ([c_void_p, c_int32], c_void_p),
     "spx_op_allreduce": ([c_void_p, c_void_p, c_int32, c_void_p, c_int64], c_int),
     "spx_ar_destroy": ([c_void_p], c_int),
+    "spx_op_expand_dw_nhwc": ([c_void_p] + [c_void_p] * 6 + [POINTER(ExpandDwParams)], c_int),
     "spx_op_pad4": ([c_void_p, c_void_p, c_void_p, c_float, _IP], c_int),
     "spx_op_transpose4": ([c_void_p, c_void_p, c_void_p, _IP], c_int),
 }

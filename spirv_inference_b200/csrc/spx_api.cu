@@ -901,6 +901,13 @@ int spx_op_argmax_merge(spx_graph* g, const float* packed, int32_t parts, int32_
   return launch_argmax_merge(g->stream, &g->launches, packed, parts, rows, ids);
 }
 
+int spx_op_expand_dw_nhwc(spx_graph* g, const float* x, const float* w_expand,
+                          const float* b_expand, const float* w_dw, const float* b_dw, float* y,
+                          const spx_expand_dw_params* p) {
+  SPX_G(g);
+  return launch_expand_dw(g->stream, &g->launches, x, w_expand, b_expand, w_dw, b_dw, y, p);
+}
+
 int spx_op_swiglu(spx_graph* g, const float* gate, const float* up, float* y, int64_t n) {
   SPX_G(g);
   if (!gate || !up || !y) return fail(SPX_ERR_INVALID_ARGUMENT, "swiglu: null");

@@ -188,6 +188,9 @@ int try_dw_tma(cudaStream_t s, int64_t* cnt, const float* x, const float* w, con
                float* y, const spx_dw_params* p);
 // Returns and clears the depthwise kernel's device status (1 = a wait timed out).
 int dw_take_status();
+int launch_expand_dw(cudaStream_t s, int64_t* cnt, const float* x, const float* we,
+                     const float* be, const float* wd, const float* bd, float* y,
+                     const spx_expand_dw_params* p);
 
 // tcgen05 3xTF32 GEMM (k_gemm_tc.cu): both operands K-contiguous.
 bool gemm_tc_eligible(const float* a, int64_t lda, const float* b, int64_t ldb, int M, int N,

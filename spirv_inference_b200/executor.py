@@ -10,6 +10,11 @@ issues activations and residual adds as extra dispatches
 * keeps every activation in HBM in NHWC,
 * fuses bias + activation into every conv / depthwise / FC epilogue and the
   residual ADD of an inverted-residual block into the projecting 1x1 conv,
+* optionally (fuse_expand_dw) runs a block's 1x1 expand conv and the 3x3
+  depthwise after it as one kernel, the expanded tensor staying on chip;
+  off by default: its CUDA-core expand (exact fp32, ~14 TFLOP/s) is slower
+  than the tensor-core expand plus TMA depthwise it replaces on every
+  MobileNetV2 block but one,
 * treats RESHAPE as an alias, and
 * records the whole graph on one stream, optionally captured once into a
   CUDA graph and replayed.
@@ -21,16 +26,18 @@ import numpy as np
 from . import _lib
 from .graph import DeviceTensor, Graph
 from .lowering import same_padding_offsets
-from .nets import Model
+from .nets import Model, Op
 
 
 class CnnExecutor:
     def __init__(self, model: Model, batch: int, device: int = 0, graph: Graph | None = None,
-                 fuse_residual: bool = True, presplit: bool = True):
+                 fuse_residual: bool = True, presplit: bool = True,
+                 fuse_expand_dw: bool = False):
         self.model = model
         self.batch = batch
         self.g = graph or Graph(device)
         self.fuse_residual = fuse_residual
+        self.fuse_expand_dw = fuse_expand_dw
         self.presplit = presplit
         self._splits: dict = {}
         self.w: dict[str, DeviceTensor] = {}
@@ -76,9 +83,52 @@ class CnnExecutor:
                         fused_into[p.output] = (op.output, op.inputs[si])
                         break
         skip_adds = {v[0] for v in fused_into.values()}
+        # Expand -> depthwise fusion: a 1x1 stride-1 conv with 16 / 24 / 32
+        # input channels whose only consumer is a 3x3 depthwise (SAME, no
+        # dilation, depth multiplier 1) with 4-aligned channels.
+        expand_of: dict[str, Op] = {}  # depthwise output -> expand op
+        expanded: set[str] = set()     # expand outputs that never materialise
+        if self.fuse_expand_dw:
+            producers = {op.output: op for op in m.ops}
+            for op in m.ops:
+                if op.type != "DEPTHWISE_CONV_2D":
+                    continue
+                a = op.attrs
+                p = producers.get(op.inputs[0])
+                wd = m.weights[op.inputs[1]]
+                if (p is None or p.type != "CONV_2D" or uses[p.output] != 1
+                        or p.output in fused_into):
+                    continue
+                we = m.weights[p.inputs[1]]
+                if (we.shape[1:3] != (1, 1) or tuple(p.attrs["stride"]) != (1, 1)
+                        or we.shape[3] not in (16, 24, 32) or wd.shape[1:3] != (3, 3)
+                        or tuple(a.get("dilation", (1, 1))) != (1, 1)
+                        or a.get("depth_multiplier", 1) != 1 or a.get("padding") != "SAME"
+                        or a["stride"][0] != a["stride"][1] or a["stride"][0] not in (1, 2)
+                        or wd.shape[3] % 4):
+                    continue
+                expand_of[op.output] = p
+                expanded.add(p.output)
         self._buf(m.input)
         for op in m.ops:
             a = op.attrs
+            if op.type == "CONV_2D" and op.output in expanded:
+                continue  # runs inside the depthwise that consumes it
+            if op.type == "DEPTHWISE_CONV_2D" and op.output in expand_of:
+                p = expand_of[op.output]
+                x, y = self._buf(p.inputs[0]), self._buf(op.output)
+                wd = self.w[op.inputs[1]]
+                ce = wd.shape[3]
+                s_ = a["stride"][0]
+                ih = x.shape[1]
+                pt, pl = same_padding_offsets("SAME", ih, x.shape[2], y.shape[1], y.shape[2],
+                                              3, 3, s_, s_)
+                self._plan.append(("expand_dw", dict(
+                    x=x, we=self.w[p.inputs[1]], be=self.w[p.inputs[2]],
+                    wd=wd.view((3, 3, ce)), bd=self.w[op.inputs[2]], y=y, stride=s_,
+                    pad=(pt, pl), act_e=p.attrs.get("activation", 0),
+                    act_d=a.get("activation", 0))))
+                continue
             if op.type == "CONV_2D":
                 x = self._buf(op.inputs[0])
                 res = None
@@ -147,6 +197,10 @@ class CnnExecutor:
                 g.conv2d_nhwc(p["x"], p["w"], p["bias"], p["y"], stride=p["stride"], pad=p["pad"],
                               activation=p["activation"], residual=p["residual"],
                               w_split=p["w_split"])
+            elif kind == "expand_dw":
+                g.expand_dw_nhwc(p["x"], p["we"], p["be"], p["wd"], p["bd"], p["y"],
+                                 stride=p["stride"], pad=p["pad"], act_expand=p["act_e"],
+                                 act_dw=p["act_d"])
             elif kind == "dw":
                 g.depthwise_nhwc(p["x"], p["w"], p["bias"], p["y"], stride=p["stride"],
                                  pad=p["pad"], dilation=p["dilation"], activation=p["activation"])
@@ -177,6 +231,13 @@ class CnnExecutor:
                 f = 2 * y.size * k
                 b = x.size + w.size + y.shape[-1] + y.size + (y.size if p["residual"] else 0)
                 label = f"conv{w.shape[1]}x{w.shape[2]}"
+            elif kind == "expand_dw":
+                x, y, we = p["x"], p["y"], p["we"]
+                ce, cin = we.shape[0], we.shape[3]
+                e_px = x.size // cin                       # expanded pixels (input resolution)
+                f = 2 * e_px * ce * cin + 2 * y.size * 9
+                b = x.size + we.size + ce + p["wd"].size + ce + y.size
+                label = "expand_dw"
             elif kind == "dw":
                 x, w, y = p["x"], p["w"], p["y"]
                 f = 2 * y.size * w.shape[0] * w.shape[1]

@@ -270,3 +270,25 @@ def test_depthwise_small_maps_all_paths(g, n, ih, c, k, s, path):
         _lib.set_option("dw_path", 0)
     ref = _act(R.depthwise_nhwc(x, w, b, (s, s), (pt, pt), (oh, oh), (1, 1)), _lib.ACT_RELU6)
     np.testing.assert_allclose(dy.download(), ref, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("n,ih,cin,ce,s", [(2, 112, 16, 96, 2), (2, 56, 24, 144, 1),
+                                           (2, 56, 24, 144, 2), (3, 28, 32, 192, 1),
+                                           (2, 28, 32, 192, 2), (1, 15, 16, 40, 1),
+                                           (2, 13, 24, 100, 2)])
+def test_expand_dw_fused(g, n, ih, cin, ce, s):
+    """1x1 expand + ReLU6 then 3x3 depthwise + ReLU6 in one kernel, against
+    the float64 composition of the two ops (SAME padding of the depthwise
+    applies to the expanded tensor)."""
+    oh = -(-ih // s)
+    tot = max((oh - 1) * s + 3 - ih, 0)
+    pt = tot // 2
+    x = _r(n, ih, ih, cin)
+    we, be = _r(ce, 1, 1, cin, scale=0.5), _r(ce)
+    wd, bd = _r(3, 3, ce), _r(ce)
+    dy = g.alloc((n, oh, oh, ce))
+    g.expand_dw_nhwc(g.tensor(x), g.tensor(we), g.tensor(be), g.tensor(wd), g.tensor(bd), dy,
+                     stride=s, pad=(pt, pt))
+    e = np.clip(x.astype(np.float64) @ we.reshape(ce, cin).T.astype(np.float64) + be, 0, 6)
+    ref = np.clip(R.depthwise_nhwc(e, wd, bd, (s, s), (pt, pt), (oh, oh), (1, 1)), 0, 6)
+    np.testing.assert_allclose(dy.download(), ref, rtol=1e-5, atol=1e-5)

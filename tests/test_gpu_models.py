@@ -76,3 +76,24 @@ def test_executor_batch_shards_are_independent(gpu, oracle_outputs):
     finally:
         full.close()
         one.close()
+
+
+def test_mnv2_expand_dw_fusion_matches_unfused(gpu):
+    """The fused expand -> depthwise path (opt-in) against the default
+    executor on the same MobileNetV2 batch."""
+    import numpy as np
+    from spirv_inference_b200 import nets
+    from spirv_inference_b200.executor import CnnExecutor
+    m = nets.mobilenet_v2(seed=0)
+    x = nets.make_input(m, 4, seed=11)
+    outs = []
+    for fuse in (False, True):
+        ex = CnnExecutor(m, batch=4, device=gpu, fuse_expand_dw=fuse)
+        try:
+            outs.append(ex.forward(x))
+            if fuse:
+                assert sum(k == "expand_dw" for k, _ in ex._plan) == 6
+        finally:
+            ex.close()
+    assert np.abs(outs[0] - outs[1]).max() <= 1e-4
+    assert np.array_equal(outs[0].argmax(1), outs[1].argmax(1))
