@@ -363,13 +363,16 @@ def run_spx(args) -> None:
             "kernels_per_step": ex.kernels_per_run,
             "clocks": clk.summary(),
         }
-        if not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(args.model, seconds=args.cpu_seconds)
-        print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
     ex.close()
+    if rank == 0:
+        # Timed after the process group is gone: NCCL's polling threads and
+        # the other ranks no longer compete for the host cores.
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.model, seconds=args.cpu_seconds)
+        print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------
@@ -594,9 +597,6 @@ def run_llama_spx(args) -> None:
             "tokens_first_sequence": toks[0].tolist(),
             "clocks": clk.summary(),
         }
-        if not args.no_cpu_baseline:
-            line["cpu_baseline"] = llama_cpu_baseline(W, args.cpu_seconds)
-        print(json.dumps(line), flush=True)
     # Free the decoder (and its captured CUDA graph, which holds NCCL work on
     # the communicator) before the process group goes away.
     torch.cuda.synchronize()
@@ -604,6 +604,10 @@ def run_llama_spx(args) -> None:
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+    if rank == 0:
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = llama_cpu_baseline(W, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
 
 
 def main():
