@@ -223,6 +223,14 @@ typedef struct spx_expand_dw_params {
 int spx_op_expand_dw_nhwc(spx_graph* g, const float* x, const float* w_expand,
                           const float* b_expand, const float* w_dw, const float* b_dw, float* y,
                           const spx_expand_dw_params* p);
+/* The same with the expand weights also pre-split (spx_weights_split): the
+ * expand runs as 3xTF32 tensor-core MMAs into TMEM (both activations ReLU6
+ * or both none, ce <= 256); other shapes fall back to spx_op_expand_dw_nhwc
+ * (w_expand needed then). */
+int spx_op_expand_dw_nhwc_split(spx_graph* g, const float* x, const float* w_expand,
+                                const float* w_expand_hi, const float* w_expand_lo,
+                                const float* b_expand, const float* w_dw, const float* b_dw,
+                                float* y, const spx_expand_dw_params* p);
 
 /* Batched strided GEMM: C[b][m][n] = act(alpha * sum_k A[b,m,k] B[b,k,n]
  * + bias[n] + R[b][m][n]).  Element strides let one entry cover

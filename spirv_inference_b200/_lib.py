@@ -164,6 +164,8 @@ _SIGS = {
     "spx_op_allreduce": ([c_void_p, c_void_p, c_int32, c_void_p, c_int64], c_int),
     "spx_ar_destroy": ([c_void_p], c_int),
     "spx_op_expand_dw_nhwc": ([c_void_p] + [c_void_p] * 6 + [POINTER(ExpandDwParams)], c_int),
+    "spx_op_expand_dw_nhwc_split": ([c_void_p] + [c_void_p] * 8 + [POINTER(ExpandDwParams)],
+                                    c_int),
     "spx_op_pad4": ([c_void_p, c_void_p, c_void_p, c_float, _IP], c_int),
     "spx_op_transpose4": ([c_void_p, c_void_p, c_void_p, _IP], c_int),
 }

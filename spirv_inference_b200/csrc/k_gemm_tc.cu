@@ -909,6 +909,369 @@ int sm_count() {
   return n;
 }
 
+
+// ===========================================================================
+// Fused inverted-residual front half on tensor cores: 1x1 expand conv
+// (3xTF32 UMMAs, accumulators in TMEM) + bias + activation + 3x3 depthwise +
+// bias + activation, the expanded tensor never leaving the chip.
+//
+// Persistent CTA, one per SM, walking spatial tiles (TH x TW outputs of one
+// image).  Per spatial tile the TMA producer loads the block input's halo
+// box (IH x IW pixels x 32 channels, zero fill past cin and past the map)
+// once; the converters split it into tf32 hi / lo tiles; then for every
+// 32-channel chunk of the expanded width the MMA warp computes the expanded
+// halo [pixels x 32] into one of two TMEM accumulators (3 M tiles of 128
+// pixel rows), and the eight epilogue warps move it through bias,
+// activation and the out-of-map zeroing (the depthwise padding applies to
+// the expanded tensor) into a shared-memory tile, then run the depthwise
+// rows on it and store the output.  The expand weights (all chunks, hi and
+// lo) stay resident in shared memory.
+//   warp 0      TMA producer        warp 1   TMEM owner, MMA issuer
+//   warps 2-5   converters          warps 6-13  epilogue + depthwise
+constexpr int kXdwThreads = 14 * 32;
+constexpr int kXdwEpi0 = 6;  // first epilogue warp
+
+struct XdwArgs {
+  int n, ih, iw, cin, ce, oh, ow, pt, pl;
+  int tiles_h, tiles_w, nch, ksteps;
+  uint32_t xbytes, row_bytes, idesc;
+  const float* be;
+  const float* wd;
+  const float* bd;
+  float* y;
+};
+
+__device__ __forceinline__ void epi_bar() {  // the 256 epilogue threads
+  asm volatile("bar.sync 1, 256;" ::: "memory");
+}
+
+template <int S, int TH, int TW, int R, int ACT>
+__global__ void __launch_bounds__(kXdwThreads, 1)
+    xdw_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmWh,
+                  const __grid_constant__ CUtensorMap tmWl, const XdwArgs p) {
+  constexpr int IH = (TH - 1) * S + 3, IW = (TW - 1) * S + 3;
+  constexpr int NPIX = IH * IW;
+  constexpr int NROW = (NPIX + 7) / 8 * 8;
+  constexpr int MT = (NPIX + kBM - 1) / kBM;
+  constexpr uint32_t kXB = NROW * 128;
+  constexpr int CG = 8;  // 4-channel groups of a 32-channel chunk
+  static_assert((TH / R) * TW * CG == 256, "one epilogue thread per (rows, column, group)");
+  static_assert(MT * 32 * 2 <= 256, "two accumulators of MT x 32 columns");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* xraw = smem;
+  uint8_t* xhi = xraw + kXB;
+  uint8_t* xlo = xhi + kXB;
+  uint8_t* wres = xlo + kXB;                              // [nch][hi 4 KB | lo 4 KB]
+  float* es = (float*)(wres + (size_t)p.nch * 8192);      // [NPIX][32], 16-byte chunks swizzled
+  uint64_t* bars = (uint64_t*)(es + NPIX * 32);
+  uint64_t* bfull = bars + 0;
+  uint64_t* xraw_full = bars + 1;
+  uint64_t* xraw_empty = bars + 2;
+  uint64_t* xsplit_full = bars + 3;
+  uint64_t* xsplit_empty = bars + 4;
+  uint64_t* tfull = bars + 5;   // [2]
+  uint64_t* tempty = bars + 7;  // [2]
+  uint64_t* drain = bars + 9;
+  uint32_t* tmem_slot = (uint32_t*)(bars + 10);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = p.n * p.tiles_h * p.tiles_w;
+  if (threadIdx.x == 0) {
+    bar_init(bfull, 1);
+    bar_init(xraw_full, 1);
+    bar_init(xraw_empty, 128);
+    bar_init(xsplit_full, 128);
+    bar_init(xsplit_empty, 1);
+    for (int a = 0; a < 2; ++a) {
+      bar_init(&tfull[a], 1);
+      bar_init(&tempty[a], 256);
+    }
+    bar_init(drain, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     su32(tmem_slot)),
+                 "r"(256));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto coords = [&](int st, int& img, int& ty, int& tx) {
+    tx = st % p.tiles_w;
+    const int r = st / p.tiles_w;
+    ty = r % p.tiles_h;
+    img = r / p.tiles_h;
+  };
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      bool armed = false;
+      uint32_t armed_par = 0;
+      bar_expect_tx(bfull, (uint32_t)p.nch * 8192);
+      for (int c = 0; c < p.nch; ++c) {
+        tma_load_2d(wres + (size_t)c * 8192, &tmWh, bfull, 0, c * 32);
+        tma_load_2d(wres + (size_t)c * 8192 + 4096, &tmWl, bfull, 0, c * 32);
+      }
+      uint32_t ph = 0;
+      for (int st = blockIdx.x; st < total; st += gridDim.x) {
+        if (!bar_wait(xraw_empty, ph ^ 1, abort_flag, kTimeoutNs, 64)) break;
+        int img, ty, tx;
+        coords(st, img, ty, tx);
+        bar_expect_tx(xraw_full, p.xbytes);
+        tma_load_4d(xraw, &tmX, xraw_full, 0, tx * TW * S - p.pl, ty * TH * S - p.pt, img);
+        armed = true;
+        armed_par = ph;
+        ph ^= 1;
+      }
+      if (*abort_flag) {
+        volatile int never = 0;
+        bar_wait(bfull, 0, &never, kDrainNs);
+        if (armed) bar_wait(xraw_full, armed_par, &never, kDrainNs);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      bool issued = false;
+      uint32_t xph = 0;
+      int it = 0;  // chunk counter over the whole launch
+      if (!bar_wait(bfull, 0, abort_flag, kTimeoutNs, 64)) goto mma_done;
+      for (int st = blockIdx.x; st < total; st += gridDim.x) {
+        if (!bar_wait(xsplit_full, xph, abort_flag, kTimeoutNs, 64)) goto mma_done;
+        xph ^= 1;
+        tc_fence_after();
+        for (int c = 0; c < p.nch; ++c, ++it) {
+          const int a = it & 1;
+          const uint32_t aph = (uint32_t)(it >> 1) & 1u;
+          if (!bar_wait(&tempty[a], aph ^ 1, abort_flag, kTimeoutNs, 64)) goto mma_done;
+          tc_fence_after();
+          const uint32_t wh = su32(wres + (size_t)c * 8192), wl = wh + 4096;
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            const uint32_t d = tmem + (uint32_t)(a * MT * 32 + m * 32);
+            const uint32_t xh = su32(xhi + m * kBM * 128), xl = su32(xlo + m * kBM * 128);
+            for (int k = 0; k < p.ksteps; ++k) {
+              const uint32_t off = k * 32;
+              umma_tf32(d, sdesc(xl + off), sdesc(wh + off), p.idesc, k ? 1u : 0u);
+              umma_tf32(d, sdesc(xh + off), sdesc(wl + off), p.idesc, 1u);
+              umma_tf32(d, sdesc(xh + off), sdesc(wh + off), p.idesc, 1u);
+            }
+          }
+          issued = true;
+          umma_commit(&tfull[a]);
+        }
+        umma_commit(xsplit_empty);  // the split x tile is free once these MMAs finish
+      }
+    mma_done:
+      if (*abort_flag && issued) {
+        umma_commit(drain);
+        volatile int never = 0;
+        bar_wait(drain, 0, &never, kDrainNs);
+      }
+    }
+  } else if (warp < kXdwEpi0) {
+    // ---------------- converters: raw halo -> hi / lo ----------------
+    const int ct = threadIdx.x - 64;
+    uint32_t rph = 0, sph = 0;
+    for (int st = blockIdx.x; st < total; st += gridDim.x) {
+      if (!bar_wait(xraw_full, rph, abort_flag, kTimeoutNs, 256)) break;
+      rph ^= 1;
+      if (!bar_wait(xsplit_empty, sph ^ 1, abort_flag, kTimeoutNs, 256)) break;
+      sph ^= 1;
+      const float4* src = reinterpret_cast<const float4*>(xraw);
+      float4* hi = reinterpret_cast<float4*>(xhi);
+      float4* lo = reinterpret_cast<float4*>(xlo);
+      const int chunks = 2 * p.ksteps;  // 16-byte chunks of K that the MMAs read
+#pragma unroll 4
+      for (int i = ct; i < NPIX * 8; i += 128) {
+        if (((i & 7) ^ ((i >> 3) & 7)) >= chunks) continue;
+        const float4 v = src[i];
+        const float4 h = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+        lo[i] = make_float4(split_lo(v.x, h.x), split_lo(v.y, h.y), split_lo(v.z, h.z),
+                            split_lo(v.w, h.w));
+        hi[i] = h;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      bar_arrive(xraw_empty);
+      bar_arrive(xsplit_full);
+    }
+  } else {
+    // ---------------- epilogue + depthwise (256 threads) ----------------
+    const int et = threadIdx.x - kXdwEpi0 * 32;
+    const int quarter = warp & 3;
+    const int group = (warp - kXdwEpi0) >> 2;  // 0 or 1: which M tiles this warp drains
+    const int cg = et % CG;
+    const int ox_l = (et / CG) % TW;
+    const int rb = et / (CG * TW);
+    int it = 0;
+    for (int st = blockIdx.x; st < total; st += gridDim.x) {
+      int img, ty, tx;
+      coords(st, img, ty, tx);
+      const int y0 = ty * TH * S - p.pt, x0 = tx * TW * S - p.pl;
+      for (int c = 0; c < p.nch; ++c, ++it) {
+        const int a = it & 1;
+        const uint32_t aph = (uint32_t)(it >> 1) & 1u;
+        const bool ok = bar_wait(&tfull[a], aph, abort_flag, kTimeoutNs, 128);
+        (void)ok;
+        epi_bar();  // previous chunk's depthwise reads of es are done; abort is uniform
+        if (*abort_flag) break;
+        tc_fence_after();
+        // TMEM -> es: this warp drains M tiles group, group + 2, ...
+        const int c0 = c * 32;
+        for (int m = group; m < MT; m += 2) {
+          float v[32];
+          tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * MT * 32 + m * 32), v);
+          const int r = m * kBM + quarter * 32 + lane;  // halo pixel
+          if (r < NPIX) {
+            const int py = y0 + r / IW, px = x0 + r % IW;
+            const bool in = py >= 0 && py < p.ih && px >= 0 && px < p.iw;
+            float4* row = reinterpret_cast<float4*>(es + r * 32);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const int ch = c0 + 4 * q;
+              float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (p.be && ch < p.ce) b4 = __ldg(reinterpret_cast<const float4*>(p.be + ch));
+              float4 e;
+              e.x = in ? act_c<ACT>(v[4 * q + 0] + b4.x) : 0.0f;
+              e.y = in ? act_c<ACT>(v[4 * q + 1] + b4.y) : 0.0f;
+              e.z = in ? act_c<ACT>(v[4 * q + 2] + b4.z) : 0.0f;
+              e.w = in ? act_c<ACT>(v[4 * q + 3] + b4.w) : 0.0f;
+              row[q ^ (r & 7)] = e;  // swizzled: conflict-free across a warp's rows
+            }
+          }
+        }
+        tc_fence_before();
+        bar_arrive(&tempty[a]);
+        epi_bar();  // es complete
+        // Depthwise rows (dw_tma_kernel's walk) on the expanded halo.
+        const int ch = c0 + cg * 4;
+        const bool live = ch < p.ce;
+        float4 wr[9];
+#pragma unroll
+        for (int k = 0; k < 9; ++k)
+          wr[k] = live ? __ldg(reinterpret_cast<const float4*>(p.wd + (size_t)k * p.ce + ch))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 bv = (p.bd && live) ? __ldg(reinterpret_cast<const float4*>(p.bd + ch))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 acc[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = bv;
+#pragma unroll
+        for (int j = 0; j < (R - 1) * S + 3; ++j) {
+          const int iy = rb * R * S + j;
+          float4 rowv[3];
+#pragma unroll
+          for (int kx = 0; kx < 3; ++kx) {
+            const int pix = iy * IW + ox_l * S + kx;
+            rowv[kx] = reinterpret_cast<const float4*>(es + pix * 32)[cg ^ (pix & 7)];
+          }
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const int ky = j - r * S;
+            if (ky < 0 || ky >= 3) continue;
+#pragma unroll
+            for (int kx = 0; kx < 3; ++kx) {
+              const float4 w4 = wr[ky * 3 + kx];
+              acc[r].x = fmaf(rowv[kx].x, w4.x, acc[r].x);
+              acc[r].y = fmaf(rowv[kx].y, w4.y, acc[r].y);
+              acc[r].z = fmaf(rowv[kx].z, w4.z, acc[r].z);
+              acc[r].w = fmaf(rowv[kx].w, w4.w, acc[r].w);
+            }
+          }
+        }
+        const int ox = tx * TW + ox_l;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int oy = ty * TH + rb * R + r;
+          if (oy < p.oh && ox < p.ow && live) {
+            float4 v = acc[r];
+            v.x = act_c<ACT>(v.x);
+            v.y = act_c<ACT>(v.y);
+            v.z = act_c<ACT>(v.z);
+            v.w = act_c<ACT>(v.w);
+            *reinterpret_cast<float4*>(p.y + (((size_t)img * p.oh + oy) * p.ow + ox) * p.ce + ch) =
+                v;
+          }
+        }
+      }
+      if (*abort_flag) break;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
+  }
+}
+
+template <int S, int TH, int TW, int R, int ACT>
+int launch_xdw(cudaStream_t s, const float* x, const float* we_hi, const float* we_lo,
+               const float* be, const float* wd, const float* bd, float* y,
+               const spx_expand_dw_params* q) {
+  constexpr int IH = (TH - 1) * S + 3, IW = (TW - 1) * S + 3;
+  constexpr int NPIX = IH * IW;
+  constexpr int NROW = (NPIX + 7) / 8 * 8;
+  XdwArgs p = {};
+  p.n = q->n;
+  p.ih = q->ih;
+  p.iw = q->iw;
+  p.cin = q->cin;
+  p.ce = q->ce;
+  p.oh = q->oh;
+  p.ow = q->ow;
+  p.pt = q->pad_top;
+  p.pl = q->pad_left;
+  p.tiles_h = (q->oh + TH - 1) / TH;
+  p.tiles_w = (q->ow + TW - 1) / TW;
+  p.nch = (q->ce + 31) / 32;
+  p.ksteps = (q->cin + 7) / 8;
+  p.xbytes = NPIX * 128;
+  p.idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(32 >> 3) << 17) |
+            ((uint32_t)(kBM >> 4) << 24);
+  p.be = be;
+  p.wd = wd;
+  p.bd = bd;
+  p.y = y;
+  const size_t smem = 1024 + 3 * (size_t)NROW * 128 + (size_t)p.nch * 8192 +
+                      (size_t)NPIX * 32 * 4 + 128;
+  if (smem > 227 * 1024) return -1;
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(SPX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  CUtensorMap mx, mwh, mwl;
+  cuuint64_t dims[4] = {(cuuint64_t)q->cin, (cuuint64_t)q->iw, (cuuint64_t)q->ih,
+                        (cuuint64_t)q->n};
+  cuuint64_t strides[3] = {(cuuint64_t)q->cin * 4, (cuuint64_t)q->iw * q->cin * 4,
+                           (cuuint64_t)q->ih * q->iw * q->cin * 4};
+  cuuint32_t box[4] = {(cuuint32_t)kBK, (cuuint32_t)IW, (cuuint32_t)IH, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)x, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SPX_ERR_CUDA, "expand_dw x map encode failed (%d)", (int)r);
+  int rc;
+  if ((rc = make_map(&mwh, we_hi, q->ce, q->cin, q->cin, 32))) return rc;
+  if ((rc = make_map(&mwl, we_lo, q->ce, q->cin, q->cin, 32))) return rc;
+  auto kern = xdw_tc_kernel<S, TH, TW, R, ACT>;
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [&] {
+    attr = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  });
+  if (attr != cudaSuccess) return check_cuda(attr, "expand_dw_tc: smem attribute");
+  const int total = p.n * p.tiles_h * p.tiles_w;
+  const int grid = total < sm_count() ? total : sm_count();
+  kern<<<grid, kXdwThreads, smem, s>>>(mx, mwh, mwl, p);
+  return SPX_OK;
+}
 }  // namespace
 
 bool gemm_tc_eligible(const float* a, int64_t lda, const float* b, int64_t ldb, int M, int N,
@@ -1171,6 +1534,33 @@ extern "C" int spx_tc_trace_fetch(unsigned long long* out) {
   return cudaMemcpyFromSymbol(out, g_tc_trace, sizeof(g_tc_trace)) == cudaSuccess ? 0 : 3;
 }
 #endif
+
+int launch_expand_dw_tc(cudaStream_t s, int64_t* cnt, const float* x, const float* we_hi,
+                        const float* we_lo, const float* be, const float* wd, const float* bd,
+                        float* y, const spx_expand_dw_params* q) {
+  auto al16 = [](const void* v) { return ((uintptr_t)v & 15) == 0; };
+  if (!x || !we_hi || !we_lo || !wd || !y || !q) return -1;
+  if ((q->cin != 16 && q->cin != 24 && q->cin != 32) || q->ce % 4 || q->ce > 256 ||
+      (q->stride != 1 && q->stride != 2) || q->act_expand != q->act_dw ||
+      (q->act_expand != SPX_ACT_RELU6 && q->act_expand != SPX_ACT_NONE))
+    return -1;
+  if (q->oh != (q->ih + q->stride - 1) / q->stride || q->ow != (q->iw + q->stride - 1) / q->stride)
+    return -1;
+  if (!al16(x) || !al16(we_hi) || !al16(we_lo) || !al16(wd) || !al16(y) || (be && !al16(be)) ||
+      (bd && !al16(bd)))
+    return -1;
+  if ((int64_t)q->n * q->oh * q->ow * q->ce >= INT32_MAX) return -1;
+  const bool r6 = q->act_expand == SPX_ACT_RELU6;
+  int rc;
+  if (q->stride == 1)
+    rc = r6 ? launch_xdw<1, 14, 16, 7, SPX_ACT_RELU6>(s, x, we_hi, we_lo, be, wd, bd, y, q)
+            : launch_xdw<1, 14, 16, 7, SPX_ACT_NONE>(s, x, we_hi, we_lo, be, wd, bd, y, q);
+  else
+    rc = r6 ? launch_xdw<2, 4, 16, 2, SPX_ACT_RELU6>(s, x, we_hi, we_lo, be, wd, bd, y, q)
+            : launch_xdw<2, 4, 16, 2, SPX_ACT_NONE>(s, x, we_hi, we_lo, be, wd, bd, y, q);
+  if (rc != SPX_OK) return rc;
+  return after_launch(cnt, "expand_dw_tc");
+}
 
 int tc_take_status() {
   int v = 0;

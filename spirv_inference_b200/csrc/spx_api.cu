@@ -908,6 +908,20 @@ int spx_op_expand_dw_nhwc(spx_graph* g, const float* x, const float* w_expand,
   return launch_expand_dw(g->stream, &g->launches, x, w_expand, b_expand, w_dw, b_dw, y, p);
 }
 
+int spx_op_expand_dw_nhwc_split(spx_graph* g, const float* x, const float* w_expand,
+                                const float* w_expand_hi, const float* w_expand_lo,
+                                const float* b_expand, const float* w_dw, const float* b_dw,
+                                float* y, const spx_expand_dw_params* p) {
+  SPX_G(g);
+  if (g_gemm_path != 1) {
+    const int rc = launch_expand_dw_tc(g->stream, &g->launches, x, w_expand_hi, w_expand_lo,
+                                       b_expand, w_dw, b_dw, y, p);
+    if (rc != -1) return rc;
+  }
+  if (!w_expand) return fail(SPX_ERR_UNSUPPORTED, "expand_dw: shape not covered by the tensor-core path");
+  return launch_expand_dw(g->stream, &g->launches, x, w_expand, b_expand, w_dw, b_dw, y, p);
+}
+
 int spx_op_swiglu(spx_graph* g, const float* gate, const float* up, float* y, int64_t n) {
   SPX_G(g);
   if (!gate || !up || !y) return fail(SPX_ERR_INVALID_ARGUMENT, "swiglu: null");

@@ -188,6 +188,10 @@ int try_dw_tma(cudaStream_t s, int64_t* cnt, const float* x, const float* w, con
                float* y, const spx_dw_params* p);
 // Returns and clears the depthwise kernel's device status (1 = a wait timed out).
 int dw_take_status();
+// Tensor-core variant (k_gemm_tc.cu): -1 when the shape is not covered.
+int launch_expand_dw_tc(cudaStream_t s, int64_t* cnt, const float* x, const float* we_hi,
+                        const float* we_lo, const float* be, const float* wd, const float* bd,
+                        float* y, const spx_expand_dw_params* q);
 int launch_expand_dw(cudaStream_t s, int64_t* cnt, const float* x, const float* we,
                      const float* be, const float* wd, const float* bd, float* y,
                      const spx_expand_dw_params* p);

@@ -124,7 +124,8 @@ class CnnExecutor:
                 pt, pl = same_padding_offsets("SAME", ih, x.shape[2], y.shape[1], y.shape[2],
                                               3, 3, s_, s_)
                 self._plan.append(("expand_dw", dict(
-                    x=x, we=self.w[p.inputs[1]], be=self.w[p.inputs[2]],
+                    x=x, we=self.w[p.inputs[1]], we_split=self._split(p.inputs[1]),
+                    be=self.w[p.inputs[2]],
                     wd=wd.view((3, 3, ce)), bd=self.w[op.inputs[2]], y=y, stride=s_,
                     pad=(pt, pl), act_e=p.attrs.get("activation", 0),
                     act_d=a.get("activation", 0))))
@@ -200,7 +201,7 @@ class CnnExecutor:
             elif kind == "expand_dw":
                 g.expand_dw_nhwc(p["x"], p["we"], p["be"], p["wd"], p["bd"], p["y"],
                                  stride=p["stride"], pad=p["pad"], act_expand=p["act_e"],
-                                 act_dw=p["act_d"])
+                                 act_dw=p["act_d"], w_split=p["we_split"])
             elif kind == "dw":
                 g.depthwise_nhwc(p["x"], p["w"], p["bias"], p["y"], stride=p["stride"],
                                  pad=p["pad"], dilation=p["dilation"], activation=p["activation"])

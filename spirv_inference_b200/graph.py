@@ -267,13 +267,18 @@ class Graph:
         check(self._l.spx_op_swiglu(self.h, self._p(gate), self._p(up), self._p(y), n))
 
     def expand_dw_nhwc(self, x, w_expand, b_expand, w_dw, b_dw, y, *, stride, pad,
-                       act_expand=_lib.ACT_RELU6, act_dw=_lib.ACT_RELU6):
+                       act_expand=_lib.ACT_RELU6, act_dw=_lib.ACT_RELU6, w_split=None):
         """Fused 1x1 expand conv + 3x3 depthwise (x NHWC [n][ih][iw][cin],
         w_expand OHWI [ce][1][1][cin], w_dw [3][3][ce] (or [1][3][3][ce]))."""
         n, ih, iw, cin = x.shape
         _, oh, ow, ce = y.shape
         p = _lib.ExpandDwParams(n, ih, iw, cin, ce, oh, ow, stride, pad[0], pad[1], act_expand,
                                 act_dw)
+        if w_split is not None:
+            check(self._l.spx_op_expand_dw_nhwc_split(
+                self.h, self._p(x), self._p(w_expand), self._p(w_split[0]), self._p(w_split[1]),
+                self._p(b_expand), self._p(w_dw), self._p(b_dw), self._p(y), ctypes.byref(p)))
+            return
         check(self._l.spx_op_expand_dw_nhwc(self.h, self._p(x), self._p(w_expand),
                                             self._p(b_expand), self._p(w_dw), self._p(b_dw),
                                             self._p(y), ctypes.byref(p)))

@@ -286,9 +286,11 @@ def test_expand_dw_fused(g, n, ih, cin, ce, s):
     x = _r(n, ih, ih, cin)
     we, be = _r(ce, 1, 1, cin, scale=0.5), _r(ce)
     wd, bd = _r(3, 3, ce), _r(ce)
-    dy = g.alloc((n, oh, oh, ce))
-    g.expand_dw_nhwc(g.tensor(x), g.tensor(we), g.tensor(be), g.tensor(wd), g.tensor(bd), dy,
-                     stride=s, pad=(pt, pt))
     e = np.clip(x.astype(np.float64) @ we.reshape(ce, cin).T.astype(np.float64) + be, 0, 6)
     ref = np.clip(R.depthwise_nhwc(e, wd, bd, (s, s), (pt, pt), (oh, oh), (1, 1)), 0, 6)
-    np.testing.assert_allclose(dy.download(), ref, rtol=1e-5, atol=1e-5)
+    dx, dwe, dbe, dwd, dbd = g.tensor(x), g.tensor(we), g.tensor(be), g.tensor(wd), g.tensor(bd)
+    # CUDA-core expand, then the tensor-core expand (pre-split weights)
+    for split in (None, g.weights_split(dwe)):
+        dy = g.alloc((n, oh, oh, ce))
+        g.expand_dw_nhwc(dx, dwe, dbe, dwd, dbd, dy, stride=s, pad=(pt, pt), w_split=split)
+        np.testing.assert_allclose(dy.download(), ref, rtol=1e-5, atol=2e-5)
