@@ -1362,6 +1362,27 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   while (p.BN > 32 && (int64_t)p.m_tiles * ((N + p.BN - 1) / p.BN) <
                           (kb_total <= 4 ? 2 * sm_count() : sm_count() / 2))
     p.BN = (p.BN / 2 + 31) / 32 * 32;
+  // Few waves of tiles (small M, e.g. 7x7 maps): pick the N tile that
+  // minimises waves x per-tile cost, so the last wave is not mostly idle.
+  // A tile's cost is modelled as its width plus a fixed 64 columns' worth
+  // for the A side (load and split, the same for every width).
+  {
+    const int sms = sm_count();
+    const int64_t tiles = (int64_t)p.m_tiles * ((N + p.BN - 1) / p.BN);
+    if (tiles < 6 * sms) {
+      int best_bn = p.BN;
+      int64_t best = ((tiles + sms - 1) / sms) * (p.BN + 64);
+      for (int bn = p.BN - 32; bn >= 64; bn -= 32) {
+        const int64_t t = (int64_t)p.m_tiles * ((N + bn - 1) / bn);
+        const int64_t cost = ((t + sms - 1) / sms) * (bn + 64);
+        if (cost < best) {
+          best = cost;
+          best_bn = bn;
+        }
+      }
+      p.BN = best_bn;
+    }
+  }
   // At least two pipeline stages must fit next to the epilogue tiles.
   const int full_budget = 227 * 1024 - 1024 - kEpiWarps * (int)kEpiSlot - 512;
   while (p.BN > 32 && full_budget / (int)(2 * kATileBytes + 2 * (uint32_t)p.BN * kBK * 4) < 2)
