@@ -614,10 +614,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ===========================================================================
-// Few-row GEMM on tensor cores, operands swapped: C[m][n] for M <= 128 rows
+// Few-row GEMM on tensor cores, operands swapped: C[m][n] for M <= 256 rows
 // (decode / small-batch linear layers) computed as D[n][m] = W[n][:] . X[m][:]
 // so the 128-row UMMA M dimension runs over the weight rows and the batch is
-// the UMMA N dimension (16..128).  Weights stream through the CTA exactly
+// the UMMA N dimension (16..256).  Weights stream through the CTA exactly
 // once; the k range is split over a thread-block cluster along grid.y and the
 // partial tiles are summed through distributed shared memory (fixed order,
 // deterministic), each CTA of the cluster reducing and storing its share of
@@ -1469,7 +1469,7 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
 bool gemm_tc_skinny_eligible(const float* a, int64_t lda, const float* w, int64_t ldw, int M,
                              int N, int K) {
   auto al16 = [](const void* q) { return ((uintptr_t)q & 15) == 0; };
-  return M >= 1 && M <= 128 && N > 0 && K > 0 && K % 4 == 0 && lda % 4 == 0 && ldw % 4 == 0 &&
+  return M >= 1 && M <= 256 && N > 0 && K > 0 && K % 4 == 0 && lda % 4 == 0 && ldw % 4 == 0 &&
          lda >= K && ldw >= K && al16(a) && al16(w);
 }
 
@@ -1497,7 +1497,7 @@ int launch_gemm_tc_skinny(cudaStream_t s, int64_t* cnt, const float* a, int64_t 
   p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
   p.x_bytes = (uint32_t)p.Mp * kBK * 4;
   p.stage_bytes = 2 * kATileBytes + 2 * p.x_bytes;
-  p.stages = p.Mp <= 64 ? 2 : 3;
+  p.stages = p.Mp <= 64 ? 2 : (p.Mp <= 128 ? 3 : 2);
   uint32_t cols = 32;
   while (cols < (uint32_t)p.Mp) cols <<= 1;
   p.tmem_cols = cols;

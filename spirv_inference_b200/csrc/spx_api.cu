@@ -60,6 +60,14 @@ int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* 
     const int M = p->n * p->oh * p->ow;
     const bool split = w_hi && w_lo;
     const float* wb = split ? w_hi : w;
+    // A 1x1-conv classifier over pooled features (1 x 1 maps, few images):
+    // weights as the UMMA M side, split-k over a cluster.  Larger maps keep
+    // the row-tiled GEMM whatever the batch, so an image's result does not
+    // depend on how many images share the launch.
+    if (p->oh == 1 && p->ow == 1 && M <= 256 && y && gemm_tc_skinny_eligible(x, p->ic, wb, p->ic, M, p->oc, p->ic) &&
+        (!split || ((uintptr_t)w_lo & 15) == 0))
+      return launch_gemm_tc_skinny(s, cnt, x, p->ic, wb, split ? w_lo : nullptr, p->ic, M, p->oc,
+                                   p->ic, bias, res, y, p->oc, 1.0f, p->activation);
     if (gemm_tc_eligible(x, p->ic, wb, p->ic, M, p->oc, p->ic, y, p->oc) &&
         (!split || ((uintptr_t)w_lo & 15) == 0))
       return launch_gemm_tc(s, cnt, x, p->ic, wb, split ? w_lo : nullptr, p->ic, M, p->oc, p->ic,
@@ -94,7 +102,7 @@ int launch_gemm(cudaStream_t s, int64_t* cnt, const float* a, const float* b, co
       p->c_ms >= p->n && gemm_rows_eligible(a, p->a_ms, b, p->b_ns, p->m, p->k))
     return launch_gemm_rows(s, cnt, a, p->a_ms, b, p->b_ns, p->m, p->n, p->k, bias, res, c,
                             p->c_ms, p->alpha, p->activation, 0);
-  // Up to 128 rows: weights as the UMMA M side, split-k over a cluster; with
+  // Up to 256 rows: weights as the UMMA M side, split-k over a cluster; with
   // pre-split weights the tiles arrive as hi / lo and only the rows are split.
   if (g_gemm_path != 1 && single && bb && p->a_ks == 1 && p->b_ks == 1 && c &&
       p->c_ms >= p->n && gemm_tc_skinny_eligible(a, p->a_ms, bb, p->b_ns, p->m, p->n, p->k))

@@ -49,7 +49,8 @@ def test_gemm_rows(g, m, act):
 
 
 @pytest.mark.parametrize("m,N,K", [(9, 300, 2048), (16, 2560, 2048), (33, 1000, 100),
-                                   (64, 2048, 5632), (100, 129, 516), (128, 4000, 2048)])
+                                   (64, 2048, 5632), (100, 129, 516), (128, 4000, 2048),
+                                   (200, 1001, 1280), (256, 1001, 1280)])
 def test_gemm_tc_skinny(g, m, N, K):
     """9..128 rows: tensor-core tiles over the weight rows, split-k reduced
     across a cluster; 3xTF32 accuracy (normwise, grows with K)."""
