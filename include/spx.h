@@ -78,7 +78,13 @@ int spx_select_device(const char* selector, int* ordinal);
  * operands allow, exact-fp32 SIMT otherwise), 1 = SIMT only, 2 = tensor cores
  * required (shapes they cannot take fail with SPX_ERR_UNSUPPORTED).
  * "dw_path": 0 = automatic (TMA-tiled depthwise where the shape allows),
- * 1 = the register sliding-window depthwise kernel only. */
+ * 1 = the register sliding-window depthwise kernel only.
+ * "pw_path": 0 (default) = 1x1 convolutions on the tensor-core GEMM,
+ * 1 = short-reduction 1x1 convolutions (K * N <= 8192) on the CUDA-core
+ * pointwise kernel instead (exact fp32; slower on B200, kept for checking).
+ * "tc_wide_epilogue": 1 (default) = tensor-core GEMMs with one k-block per
+ * tile give four converter warps to the epilogue where that saves a round of
+ * output chunks, 0 = never. */
 int spx_set_option(const char* name, int64_t value);
 int64_t spx_get_option(const char* name);
 

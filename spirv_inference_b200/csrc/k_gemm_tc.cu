@@ -46,10 +46,11 @@
 namespace spx {
 
 __device__ int g_tc_status = 0;
+int g_tc_epi12 = 1;
 
 #ifdef SPX_TC_TRACE
 // Development-only pipeline trace of CTA 0 (not compiled into the library).
-__device__ unsigned long long g_tc_trace[8][64];
+__device__ unsigned long long g_tc_trace[16][64];
 #define TC_TRACE(ev, i)                                                     \
   do {                                                                      \
     if (blockIdx.x == 0 && (i) < 64) g_tc_trace[ev][i] = gtimer();          \
@@ -64,9 +65,10 @@ namespace {
 
 constexpr int kBM = 128;         // UMMA M: output rows per tile
 constexpr int kBK = 32;          // fp32 elements per k-block (one 128-byte row)
-constexpr int kEpiWarps = 8;     // two per TMEM lane quarter
+constexpr int kEpiWarps = 8;     // two per TMEM lane quarter (default)
+constexpr int kMaxAcc = 4;       // TMEM accumulators (2, or 4 with two epilogue groups)
+constexpr int kMaxEpiWarps = 12; // three per quarter: short k-loops with 3+ chunks per quarter
 constexpr int kConvWarps = 8;
-constexpr int kConvThreads = kConvWarps * 32;
 constexpr int kProducerWarp = kEpiWarps + kConvWarps;
 constexpr int kMmaWarp = kProducerWarp + 1;
 constexpr int kThreads = (kMmaWarp + 1) * 32;  // 18 warps
@@ -99,7 +101,10 @@ struct TcArgs {
   int oh, ow, ic_blocks, kw, sh, pt, pl;
   int th, tw, tn, tiles_h, tiles_w;
   uint32_t a_tx;  // bytes one A load delivers
-  int epi_warps;  // epilogue warps in use (4 or 8): long k-loops trade them for stages
+  int groups;     // epilogue groups taking alternate tiles (1, or 2 for N <= 32 with TMA stores)
+  int nacc;       // TMEM accumulators: 2 per group
+  int epi_warps;  // epilogue warps in use (4, 8 or 12): long k-loops trade them for stages,
+                  // 1-block k-loops take 12 (warps 8-11 leave the converters)
 };
 
 __device__ __forceinline__ uint32_t su32(const void* p) {
@@ -250,20 +255,84 @@ __device__ __forceinline__ float tf32_rna(float x) {
   return __uint_as_float(h);
 }
 
-// In-place hi / separate lo split of n16 16-byte vectors.  For finite x,
-// lo = x - hi is exact; for inf / nan the lo term is zeroed so the hi*hi
-// product carries the special value.
+// tf32 round-to-nearest, ties away from zero, on the bit pattern: adding half
+// a tf32 ulp (bit 12) to the magnitude and clearing the 13 dropped bits rounds
+// |x| half-up, which is ties-away for a sign-magnitude format.  Finite inputs
+// only (infinities and NaNs are handled by the callers).
+__device__ __forceinline__ uint32_t rna13(uint32_t b) { return (b + 0x1000u) & 0xFFFFE000u; }
+
+// hi = rna_tf32(x), lo = rna_tf32(x - hi).  For finite x, x - hi is exact; for
+// inf / nan hi keeps the special value (nan made quiet) and lo is zero, so
+// the hi*hi product carries it.
+__device__ __forceinline__ void split1(float x, float& hi, float& lo) {
+  const uint32_t b = __float_as_uint(x);
+  if ((b & 0x7F800000u) == 0x7F800000u) {
+    hi = __uint_as_float((b & 0x007FFFFFu) ? 0x7FFFFFFFu : b);
+    lo = 0.0f;
+    return;
+  }
+  hi = __uint_as_float(rna13(b));
+  lo = __uint_as_float(rna13(__float_as_uint(x - hi)));
+}
 __device__ __forceinline__ float split_lo(float x, float h) {
   const float r = x - h;
   return r == r ? tf32_rna(r) : 0.0f;
 }
+__device__ __forceinline__ void split4(const float4& v, float4& h, float4& l) {
+  split1(v.x, h.x, l.x);
+  split1(v.y, h.y, l.y);
+  split1(v.z, h.z, l.z);
+  split1(v.w, h.w, l.w);
+}
+// lo-only split for an operand the MMA reads raw: kind::tf32 uses the upper
+// 19 bits of each 32-bit element (sign, exponent, 10 mantissa bits) and
+// ignores the low 13, so the raw fp32 tile already is hi = trunc_tf32(x) and
+// only lo = rna_tf32(x - trunc_tf32(x)) (exact difference, below one tf32
+// ulp) is written.  inf / nan: lo = 0 and the raw special value carries the
+// product.  The tensor-core GEMM tests at fp32 tolerance check this reading.
+__device__ __forceinline__ float lo_of_raw(float x) {
+  const uint32_t b = __float_as_uint(x);
+  if ((b & 0x7F800000u) == 0x7F800000u) return 0.0f;
+  return __uint_as_float(rna13(__float_as_uint(x - __uint_as_float(b & 0xFFFFE000u))));
+}
+__device__ __forceinline__ void split_lo_buffer(const float4* x, float4* lo, int n16, int tid,
+                                                int nthr) {
+  int i = tid;
+  for (; i + 3 * nthr < n16; i += 4 * nthr) {
+    float4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = x[i + j * nthr];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      lo[i + j * nthr] =
+          make_float4(lo_of_raw(v[j].x), lo_of_raw(v[j].y), lo_of_raw(v[j].z), lo_of_raw(v[j].w));
+  }
+  for (; i < n16; i += nthr) {
+    const float4 v = x[i];
+    lo[i] = make_float4(lo_of_raw(v.x), lo_of_raw(v.y), lo_of_raw(v.z), lo_of_raw(v.w));
+  }
+}
+
+// In-place hi / separate lo split of n16 16-byte vectors, all loads of a
+// thread's batch of four issued before its stores.
 __device__ __forceinline__ void split_buffer(float4* hi, float4* lo, int n16, int tid, int nthr) {
-#pragma unroll 4
-  for (int i = tid; i < n16; i += nthr) {
-    const float4 v = hi[i];
-    const float4 h = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
-    lo[i] = make_float4(split_lo(v.x, h.x), split_lo(v.y, h.y), split_lo(v.z, h.z),
-                        split_lo(v.w, h.w));
+  int i = tid;
+  for (; i + 3 * nthr < n16; i += 4 * nthr) {
+    float4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = hi[i + j * nthr];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float4 h, l;
+      split4(v[j], h, l);
+      lo[i + j * nthr] = l;
+      hi[i + j * nthr] = h;
+    }
+  }
+  for (; i < n16; i += nthr) {
+    float4 h, l;
+    split4(hi[i], h, l);
+    lo[i] = l;
     hi[i] = h;
   }
 }
@@ -300,24 +369,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* conv = full + kMaxStages;
   uint64_t* empty = conv + kMaxStages;
   uint64_t* tfull = empty + kMaxStages;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* rfull = tempty + 2;  // per epilogue warp: residual box landed
-  uint64_t* drain = rfull + kEpiWarps;
+  uint64_t* tempty = tfull + kMaxAcc;
+  uint64_t* rfull = tempty + kMaxAcc;  // per epilogue warp: residual box landed
+  uint64_t* drain = rfull + kMaxEpiWarps;
   uint32_t* tmem_slot = (uint32_t*)(drain + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Converters: warps conv_lo .. kEpiWarps + kConvWarps - 1.
+  const int conv_lo = p.epi_warps > kEpiWarps ? p.epi_warps : kEpiWarps;
+  const int conv_threads = (kEpiWarps + kConvWarps - conv_lo) * 32;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       bar_init(&full[s], 1);
-      bar_init(&conv[s], kConvThreads);
+      bar_init(&conv[s], conv_threads);
       bar_init(&empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < p.nacc; ++a) {
       bar_init(&tfull[a], 1);
-      bar_init(&tempty[a], p.epi_warps * 32);
+      bar_init(&tempty[a], p.epi_warps / p.groups * 32);
     }
-    for (int w = 0; w < kEpiWarps; ++w) bar_init(&rfull[w], 1);
+    for (int w = 0; w < kMaxEpiWarps; ++w) bar_init(&rfull[w], 1);
     bar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -416,8 +488,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(&tfull[acc]);
         TC_TRACE(4, (t - blockIdx.x) / gridDim.x);
-        acc ^= 1;
-        if (!acc) aph ^= 1;
+        if (++acc == p.nacc) {
+          acc = 0;
+          aph ^= 1;
+        }
       }
     mma_done:
       if (*abort_flag && issued) {  // wait for this CTA's MMAs before TMEM is freed
@@ -426,9 +500,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         bar_wait(drain, 0, &never, kDrainNs);
       }
     }
-  } else if (warp >= kEpiWarps) {
+  } else if (warp >= conv_lo) {
     // ---------------- converters (hi/lo split) ----------------
-    const int ct = threadIdx.x - kEpiWarps * 32;
+    const int ct = threadIdx.x - conv_lo * 32;
     int s = 0;
     uint32_t ph = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
@@ -436,12 +510,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!bar_wait(&full[s], ph, abort_flag, kTimeoutNs, 256)) goto conv_done;
         if (kb == 0 && ct == 0) TC_TRACE(7, (t - blockIdx.x) / gridDim.x);
         uint8_t* st = smem + (size_t)s * p.stage_bytes;
-        split_buffer((float4*)st, (float4*)(st + kATileBytes), kATileBytes / 16, ct,
-                     kConvThreads);
+        split_lo_buffer((const float4*)st, (float4*)(st + kATileBytes), kATileBytes / 16, ct,
+                     conv_threads);
         if (!p.presplit)
           split_buffer((float4*)(st + 2 * kATileBytes),
                        (float4*)(st + 2 * kATileBytes + p.b_bytes), p.b_bytes / 16, ct,
-                       kConvThreads);
+                       conv_threads);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         bar_arrive(&conv[s]);
         if (kb == 0 && ct == 0) TC_TRACE(1, (t - blockIdx.x) / gridDim.x);
@@ -462,14 +536,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     // TMA-loads the residual box into it; lanes add bias / residual, apply the
     // activation, write their row back 128-byte swizzled; lane 0 TMA-stores
     // the 32 x 32 box.  No block-wide barrier; stores run asynchronously.
-    int acc = 0;
+    // With two groups (one 32-column chunk per quarter: N <= 32), warps 0-3
+    // take the CTA's even tiles and warps 4-7 the odd ones, each group
+    // cycling over its own two of the four accumulators.
+    const int wpg = p.epi_warps / p.groups;       // warps per group
+    const int grp = warp / wpg;
+    int acc = grp;
     int issuer = 31;  // lane that issued the last store from this warp's staging
     uint32_t aph = 0, rph = 0;
     uint8_t* stg = epi + warp * kEpiSlot;
     float4* srow = reinterpret_cast<float4*>(stg + lane * 128);
     const int sw = lane & 7;
     bool ok = true;
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+    for (int t = blockIdx.x + grp * gridDim.x; t < total; t += p.groups * gridDim.x) {
       const int mt = t / p.n_tiles, nt = t % p.n_tiles;
       ok = bar_wait(&tfull[acc], aph, abort_flag, kTimeoutNs, 128) && ok;
       if (threadIdx.x == 0) TC_TRACE(5, (t - blockIdx.x) / gridDim.x);
@@ -478,12 +557,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int quarter = warp & 3;
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.BN);
       const int row0 = mt * kBM + quarter * 32;
-      for (int c0 = (warp >> 2) * 32; c0 < p.BN; c0 += 32 * (p.epi_warps / 4)) {
+      for (int c0 = ((warp % wpg) >> 2) * 32; c0 < p.BN; c0 += 32 * (wpg / 4)) {
         const int n0 = nt * p.BN + c0;
         if (n0 >= p.N) break;  // uniform across the warp
         // The lane that issued the previous store waits until it has read the
         // staging tile; the next store is issued by the following lane, so no
         // lane's proxy fence has to wait behind its own in-flight store.
+        const bool trc = warp == 0 && lane == 0 && c0 == 0;
+        if (trc) TC_TRACE(8, (t - blockIdx.x) / gridDim.x);
         if (lane == issuer) bulk_wait_read0();
         const int next = (issuer + 1) & 31;
         if (lane == next) {
@@ -493,8 +574,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         __syncwarp();
+        if (trc) TC_TRACE(9, (t - blockIdx.x) / gridDim.x);
         float v[32];
         tmem_ld32(tbase + (uint32_t)c0, v);
+        if (trc) TC_TRACE(10, (t - blockIdx.x) / gridDim.x);
         if (p.res) {
           ok = bar_wait(&rfull[warp], rph, abort_flag) && ok;
           rph ^= 1;
@@ -515,19 +598,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             srow[q ^ sw] = o;
           }
         });
+        if (trc) TC_TRACE(11, (t - blockIdx.x) / gridDim.x);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
+        if (trc) TC_TRACE(12, (t - blockIdx.x) / gridDim.x);
         if (lane == next) {
           tma_store_2d(&tmC, stg, n0, row0);
           bulk_commit();
         }
+#ifdef SPX_TC_TRACE
+        __syncwarp();
+        if (trc) TC_TRACE(13, (t - blockIdx.x) / gridDim.x);
+#endif
         issuer = next;
       }
       tc_fence_before();
       bar_arrive(&tempty[acc]);
       if (threadIdx.x == 0) TC_TRACE(6, (t - blockIdx.x) / gridDim.x);
-      acc ^= 1;
-      if (!acc) aph ^= 1;
+      acc += p.groups;
+      if (acc >= p.nacc) {
+        acc -= p.nacc;
+        aph ^= 1;
+      }
     }
     bulk_wait_all();  // every lane that issued stores waits for them
   } else {
@@ -1396,6 +1488,15 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
     const int half_budget = 227 * 1024 - 1024 - 4 * (int)kEpiSlot - 512;
     if (kb_total >= 8 && full_budget / bn_stage < 3 && half_budget / bn_stage >= 3)
       p.epi_warps = 4;
+    // One k-block per tile (K <= 32, the expand layers): the converters are
+    // mostly idle and the epilogue's per-chunk latency sets the tile period,
+    // so four converter warps become a third epilogue warp per lane quarter
+    // when that saves a round of chunks.
+    const int chunks = (p.BN + 31) / 32;
+    const int wide_budget = 227 * 1024 - 1024 - kMaxEpiWarps * (int)kEpiSlot - 512;
+    if (g_tc_epi12 && kb_total == 1 && (chunks + 2) / 3 < (chunks + 1) / 2 &&
+        wide_budget / bn_stage >= 2)
+      p.epi_warps = kMaxEpiWarps;
   }
   const int budget = 227 * 1024 - 1024 - p.epi_warps * (int)kEpiSlot - 512;
   p.n_tiles = (N + p.BN - 1) / p.BN;
@@ -1405,8 +1506,15 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   p.stages = budget / (int)p.stage_bytes;
   if (p.stages > kMaxStages) p.stages = kMaxStages;
   if (p.stages < 2) return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_tc: tile does not fit");
+  auto al16 = [](const void* q) { return ((uintptr_t)q & 15) == 0; };
+  p.vec4 = (ldc % 4 == 0) && al16(c) && (!res || al16(res)) && (!bias || al16(bias));
+  p.tma_store = p.vec4 && !conv;
+  // One 32-column chunk per lane quarter: the two halves of the epilogue take
+  // alternate tiles (four accumulators) so two tiles drain at once.
+  p.groups = (g_tc_epi12 && p.tma_store && p.BN == 32 && p.epi_warps == kEpiWarps) ? 2 : 1;
+  p.nacc = 2 * p.groups;
   uint32_t cols = 32;
-  while (cols < (uint32_t)(2 * p.BN)) cols <<= 1;
+  while (cols < (uint32_t)(p.nacc * p.BN)) cols <<= 1;
   p.tmem_cols = cols;
   p.idesc = (1u << 4)                          // accumulator F32
             | (2u << 7) | (2u << 10)           // A, B: TF32
@@ -1418,9 +1526,6 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   p.ldc = ldc;
   p.alpha = alpha;
   p.act = act;
-  auto al16 = [](const void* q) { return ((uintptr_t)q & 15) == 0; };
-  p.vec4 = (ldc % 4 == 0) && al16(c) && (!res || al16(res)) && (!bias || al16(bias));
-  p.tma_store = p.vec4 && !conv;
   p.a_tx = kATileBytes;
   CUtensorMap ma, mb, mblo;
   int rc;

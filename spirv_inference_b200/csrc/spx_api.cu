@@ -42,6 +42,7 @@ int after_launch(int64_t* counter, const char* what) {
 
 int g_gemm_path = 0;
 int g_dw_path = 0;
+int g_pw_path = 0;
 
 // ---- algorithm selection for dense contractions ---------------------------
 int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
@@ -68,6 +69,11 @@ int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* 
         (!split || ((uintptr_t)w_lo & 15) == 0))
       return launch_gemm_tc_skinny(s, cnt, x, p->ic, wb, split ? w_lo : nullptr, p->ic, M, p->oc,
                                    p->ic, bias, res, y, p->oc, 1.0f, p->activation);
+    // Opt-in: short reductions (inverted-residual expand / project layers)
+    // in exact fp32 on CUDA cores.  Measured slower than the tensor-core
+    // GEMM on every MobileNetV2 layer, so off by default.
+    if (g_gemm_path == 0 && g_pw_path == 1 && pw_simt_eligible(x, y, res, M, p->ic, p->oc))
+      return launch_pw_simt(s, cnt, x, w, bias, res, y, M, p->ic, p->oc, p->activation);
     if (gemm_tc_eligible(x, p->ic, wb, p->ic, M, p->oc, p->ic, y, p->oc) &&
         (!split || ((uintptr_t)w_lo & 15) == 0))
       return launch_gemm_tc(s, cnt, x, p->ic, wb, split ? w_lo : nullptr, p->ic, M, p->oc, p->ic,
@@ -460,6 +466,16 @@ int spx_set_option(const char* name, int64_t value) {
     g_dw_path = (int)value;
     return SPX_OK;
   }
+  if (n == "tc_wide_epilogue") {
+    if (value < 0 || value > 1) return fail(SPX_ERR_INVALID_ARGUMENT, "tc_wide_epilogue must be 0..1");
+    g_tc_epi12 = (int)value;
+    return SPX_OK;
+  }
+  if (n == "pw_path") {
+    if (value < 0 || value > 1) return fail(SPX_ERR_INVALID_ARGUMENT, "pw_path must be 0..1");
+    g_pw_path = (int)value;
+    return SPX_OK;
+  }
   if (n == "gemm_path") {
     if (value < 0 || value > 2) return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_path must be 0..2");
     g_gemm_path = (int)value;
@@ -472,6 +488,8 @@ int64_t spx_get_option(const char* name) {
   std::string n = name ? name : "";
   if (n == "gemm_path") return g_gemm_path;
   if (n == "dw_path") return g_dw_path;
+  if (n == "pw_path") return g_pw_path;
+  if (n == "tc_wide_epilogue") return g_tc_epi12;
   return -1;
 }
 

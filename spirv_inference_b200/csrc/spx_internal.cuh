@@ -174,6 +174,10 @@ int launch_transpose4(cudaStream_t s, int64_t* cnt, const float* x, float* y,
 // Exact-fp32 SIMT implementations (k_gemm_simt.cu).
 int launch_gemm_simt(cudaStream_t s, int64_t* cnt, const float* a, const float* b,
                      const float* bias, const float* res, float* c, const spx_gemm_params* p);
+bool pw_simt_eligible(const float* x, const float* y, const float* res, int64_t M, int K, int N);
+int launch_pw_simt(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
+                   const float* bias, const float* res, float* y, int64_t M, int K, int N,
+                   int act);
 int launch_conv_simt(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
                      const float* bias, const float* res, float* y, const spx_conv_params* p);
 
@@ -233,6 +237,7 @@ int ar_take_status();
 // Process-wide dense-contraction path: 0 auto, 1 SIMT only, 2 tensor cores
 // required (ineligible shapes fail with SPX_ERR_UNSUPPORTED).
 extern int g_gemm_path;
+extern int g_tc_epi12;
 // Depthwise path: 0 automatic (TMA tiles where the shape allows), 1 register
 // sliding-window kernel only.
 extern int g_dw_path;
