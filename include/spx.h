@@ -84,7 +84,10 @@ int spx_select_device(const char* selector, int* ordinal);
  * pointwise kernel instead (exact fp32; slower on B200, kept for checking).
  * "tc_wide_epilogue": 1 (default) = tensor-core GEMMs with one k-block per
  * tile give four converter warps to the epilogue where that saves a round of
- * output chunks, 0 = never. */
+ * output chunks, and for N <= 32 split the epilogue into two groups draining
+ * alternate tiles; 0 = never.
+ * "tc_conv_groups": 2 (default) = tensor-core GEMMs with several k-blocks per
+ * tile split two stages at once (two converter groups), 1 = one at a time. */
 int spx_set_option(const char* name, int64_t value);
 int64_t spx_get_option(const char* name);
 

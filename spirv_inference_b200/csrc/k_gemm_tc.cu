@@ -47,6 +47,7 @@ namespace spx {
 
 __device__ int g_tc_status = 0;
 int g_tc_epi12 = 1;
+int g_tc_conv2 = 1;
 
 #ifdef SPX_TC_TRACE
 // Development-only pipeline trace of CTA 0 (not compiled into the library).
@@ -103,6 +104,7 @@ struct TcArgs {
   uint32_t a_tx;  // bytes one A load delivers
   int groups;     // epilogue groups taking alternate tiles (1, or 2 for N <= 32 with TMA stores)
   int nacc;       // TMEM accumulators: 2 per group
+  int conv_groups;  // converter groups splitting alternate stages (1 or 2)
   int epi_warps;  // epilogue warps in use (4, 8 or 12): long k-loops trade them for stages,
                   // 1-block k-loops take 12 (warps 8-11 leave the converters)
 };
@@ -382,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       bar_init(&full[s], 1);
-      bar_init(&conv[s], conv_threads);
+      bar_init(&conv[s], conv_threads / p.conv_groups);
       bar_init(&empty[s], 1);
     }
     for (int a = 0; a < p.nacc; ++a) {
@@ -502,23 +504,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= conv_lo) {
     // ---------------- converters (hi/lo split) ----------------
-    const int ct = threadIdx.x - conv_lo * 32;
+    // With conv_groups = 2 the two halves take the even and the odd stages
+    // of an even-sized ring, so two stages are split at once.
+    const int gthreads = conv_threads / p.conv_groups;
+    const int cg = (threadIdx.x - conv_lo * 32) / gthreads;
+    const int ct = (threadIdx.x - conv_lo * 32) % gthreads;
     int s = 0;
     uint32_t ph = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       for (int kb = 0; kb < p.k_blocks; ++kb) {
-        if (!bar_wait(&full[s], ph, abort_flag, kTimeoutNs, 256)) goto conv_done;
-        if (kb == 0 && ct == 0) TC_TRACE(7, (t - blockIdx.x) / gridDim.x);
-        uint8_t* st = smem + (size_t)s * p.stage_bytes;
-        split_lo_buffer((const float4*)st, (float4*)(st + kATileBytes), kATileBytes / 16, ct,
-                     conv_threads);
-        if (!p.presplit)
-          split_buffer((float4*)(st + 2 * kATileBytes),
-                       (float4*)(st + 2 * kATileBytes + p.b_bytes), p.b_bytes / 16, ct,
-                       conv_threads);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        bar_arrive(&conv[s]);
-        if (kb == 0 && ct == 0) TC_TRACE(1, (t - blockIdx.x) / gridDim.x);
+        if (s % p.conv_groups == cg) {
+          if (!bar_wait(&full[s], ph, abort_flag, kTimeoutNs, 256)) goto conv_done;
+          if (kb == 0 && ct == 0) TC_TRACE(7, (t - blockIdx.x) / gridDim.x);
+          uint8_t* st = smem + (size_t)s * p.stage_bytes;
+          split_lo_buffer((const float4*)st, (float4*)(st + kATileBytes), kATileBytes / 16, ct,
+                          gthreads);
+          if (!p.presplit)
+            split_buffer((float4*)(st + 2 * kATileBytes),
+                         (float4*)(st + 2 * kATileBytes + p.b_bytes), p.b_bytes / 16, ct,
+                         gthreads);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          bar_arrive(&conv[s]);
+          if (kb == 0 && ct == 0) TC_TRACE(1, (t - blockIdx.x) / gridDim.x);
+        }
         if (++s == S) {
           s = 0;
           ph ^= 1;
@@ -1511,6 +1519,11 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   p.tma_store = p.vec4 && !conv;
   // One 32-column chunk per lane quarter: the two halves of the epilogue take
   // alternate tiles (four accumulators) so two tiles drain at once.
+  // Two converter groups own the even and the odd stages: each group then
+  // meets every one of its stages once per pass of the ring, so its mbarrier
+  // parities stay in step.  That needs an even stage count.
+  p.conv_groups =
+      (g_tc_conv2 && p.epi_warps <= kEpiWarps && p.k_blocks > 1 && p.stages % 2 == 0) ? 2 : 1;
   p.groups = (g_tc_epi12 && p.tma_store && p.BN == 32 && p.epi_warps == kEpiWarps) ? 2 : 1;
   p.nacc = 2 * p.groups;
   uint32_t cols = 32;

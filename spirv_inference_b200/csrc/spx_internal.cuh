@@ -238,6 +238,7 @@ int ar_take_status();
 // required (ineligible shapes fail with SPX_ERR_UNSUPPORTED).
 extern int g_gemm_path;
 extern int g_tc_epi12;
+extern int g_tc_conv2;
 // Depthwise path: 0 automatic (TMA tiles where the shape allows), 1 register
 // sliding-window kernel only.
 extern int g_dw_path;

@@ -28,6 +28,10 @@ def _r(*shape, scale=1.0):
 SHAPES = [  # M, N, K
     (128, 16, 32), (200, 24, 16), (1000, 96, 24), (517, 144, 96), (4096, 240, 960),
     (333, 1001, 1280), (2048, 1280, 320), (64, 1000, 1280), (130, 48, 36), (5, 8, 4),
+    # projection layers at batch 256: odd and even stage rings, two converter
+    # groups, two epilogue groups (N <= 32), three epilogue warps per quarter
+    (50176, 64, 384), (50176, 32, 192), (200704, 24, 144), (802816, 16, 32),
+    (200704, 96, 16), (200704, 160, 24),
 ]
 
 
