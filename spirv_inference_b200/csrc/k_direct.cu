@@ -137,6 +137,111 @@ __global__ void __launch_bounds__(128) conv_smallk_kernel(
   }
 }
 
+// The 3x3x3 stems (compile-time window, OC outputs): as conv_smallk, but each
+// thread computes two pixels (lane and lane + 32 of a warp's 64-pixel run),
+// so every 16-byte weight broadcast from shared memory feeds eight FMAs
+// instead of four and the kernel runs at the FMA rate rather than the
+// shared-memory rate.
+template <int OC, int KH, int KW, int IC>
+__global__ void __launch_bounds__(128) conv_stem2_kernel(
+    const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ bias,
+    const float* __restrict__ res, float* __restrict__ y, int n, int ih, int iw, int oh, int ow,
+    int sh, int sw, int pt, int pl, int act, int w_layout) {
+  constexpr int K = KH * KW * IC;
+  constexpr int kStride = OC + 4;
+  extern __shared__ float ws[];  // [K][OC], bias[OC], then per-warp 64-row output staging
+  float* stage = ws + K * OC + OC + (threadIdx.x >> 5) * 64 * kStride;
+  for (int i = threadIdx.x; i < K * OC; i += blockDim.x) {
+    const int k = i / OC, o = i % OC;
+    ws[i] = w_layout == SPX_WEIGHT_OHWI ? w[(size_t)o * K + k] : w[(size_t)k * OC + o];
+  }
+  for (int o = threadIdx.x; o < OC; o += blockDim.x) ws[K * OC + o] = bias ? bias[o] : 0.0f;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int total = n * oh * ow;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int base = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 64; base < total;
+       base += warps * 64) {
+    float acc[2][OC];
+    const float* xi[2];
+    int oy[2], ox[2];
+    bool live[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int pix = base + h * 32 + lane;
+      live[h] = pix < total;
+      const int pc = live[h] ? pix : 0;
+      ox[h] = pc % ow;
+      const int t = pc / ow;
+      oy[h] = t % oh;
+      xi[h] = x + (size_t)(t / oh) * ih * iw * IC;
+#pragma unroll
+      for (int o = 0; o < OC; ++o) acc[h][o] = ws[K * OC + o];
+    }
+#pragma unroll
+    for (int ky = 0; ky < KH; ++ky)
+#pragma unroll
+      for (int kx = 0; kx < KW; ++kx) {
+        float xv[2][IC];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int iy = oy[h] * sh + ky - pt, ix = ox[h] * sw + kx - pl;
+          const bool in = live[h] && iy >= 0 && iy < ih && ix >= 0 && ix < iw;
+          const float* xp = xi[h] + ((size_t)(in ? iy : 0) * iw + (in ? ix : 0)) * IC;
+#pragma unroll
+          for (int ci = 0; ci < IC; ++ci) xv[h][ci] = in ? __ldg(xp + ci) : 0.0f;
+        }
+#pragma unroll
+        for (int ci = 0; ci < IC; ++ci) {
+          const float4* wp = reinterpret_cast<const float4*>(ws + ((ky * KW + kx) * IC + ci) * OC);
+#pragma unroll
+          for (int o = 0; o < OC / 4; ++o) {
+            const float4 wv = wp[o];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              acc[h][4 * o + 0] = fmaf(xv[h][ci], wv.x, acc[h][4 * o + 0]);
+              acc[h][4 * o + 1] = fmaf(xv[h][ci], wv.y, acc[h][4 * o + 1]);
+              acc[h][4 * o + 2] = fmaf(xv[h][ci], wv.z, acc[h][4 * o + 2]);
+              acc[h][4 * o + 3] = fmaf(xv[h][ci], wv.w, acc[h][4 * o + 3]);
+            }
+          }
+        }
+      }
+    // Stage the warp's 64 x OC outputs, then write them out as whole rows of
+    // 16-byte vectors (coalesced), adding the residual and the activation.
+    __syncwarp();
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int o = 0; o < OC; o += 4)
+        *reinterpret_cast<float4*>(stage + (h * 32 + lane) * kStride + o) =
+            make_float4(acc[h][o], acc[h][o + 1], acc[h][o + 2], acc[h][o + 3]);
+    __syncwarp();
+    const int valid = min(64, total - base) * OC / 4;  // float4s of this warp's run
+    float* yb = y + (size_t)base * OC;
+    const float* rb = res ? res + (size_t)base * OC : nullptr;
+    with_act(act, [&](auto tag) {
+      constexpr int A = decltype(tag)::value;
+#pragma unroll
+      for (int i = 0; i < 2 * OC / 4; ++i) {
+        const int e4 = i * 32 + lane;
+        if (e4 < valid) {
+          const int px = (e4 * 4) / OC, ch = (e4 * 4) % OC;
+          float4 v = *reinterpret_cast<const float4*>(stage + px * kStride + ch);
+          if (rb) {
+            const float4 r = *reinterpret_cast<const float4*>(rb + (size_t)e4 * 4);
+            v.x += r.x; v.y += r.y; v.z += r.z; v.w += r.w;
+          }
+          v.x = act_c<A>(v.x); v.y = act_c<A>(v.y);
+          v.z = act_c<A>(v.z); v.w = act_c<A>(v.w);
+          *reinterpret_cast<float4*>(yb + (size_t)e4 * 4) = v;
+        }
+      }
+    });
+    __syncwarp();
+  }
+}
+
 template <int KH, int KW, int SH, int R>
 __global__ void __launch_bounds__(256, 2) dw_rows_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ bias,
@@ -265,6 +370,15 @@ int try_conv_smallk(cudaStream_t s, int64_t* cnt, const float* x, const float* w
                                                   p->pad_left, dh, dw, p->activation,          \
                                                   p->weight_layout)
   const bool k333 = p->kh == 3 && p->kw == 3 && p->ic == 3;
+  if (k333 && p->oc == 32 && dh == 1 && dw == 1) {
+    const size_t smem2 = ((size_t)27 * 32 + 32 + 4 * 64 * (32 + 4)) * sizeof(float);
+    cudaFuncSetAttribute(conv_stem2_kernel<32, 3, 3, 3>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
+    conv_stem2_kernel<32, 3, 3, 3><<<grid_for(total, 256, 16), 128, smem2, s>>>(
+        x, w, bias, res, y, p->n, p->ih, p->iw, p->oh, p->ow, p->stride_h, p->stride_w,
+        p->pad_top, p->pad_left, p->activation, p->weight_layout);
+    return after_launch(cnt, "conv_stem2");
+  }
   switch (p->oc) {
     case 8: SPX_SMALLK(8); break;
     case 16: SPX_SMALLK(16); break;

@@ -105,6 +105,8 @@ struct TcArgs {
   int groups;     // epilogue groups taking alternate tiles (1, or 2 for N <= 32 with TMA stores)
   int nacc;       // TMEM accumulators: 2 per group
   int conv_groups;  // converter groups splitting alternate stages (1 or 2)
+  int last_ksteps;  // 8-wide k-steps of the last k-block that hold columns < K
+  int b_resident;   // one k-block and one n-tile: pre-split B loaded once, not per stage
   int epi_warps;  // epilogue warps in use (4, 8 or 12): long k-loops trade them for stages,
                   // 1-block k-loops take 12 (warps 8-11 leave the converters)
 };
@@ -366,7 +368,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int S = p.stages;
-  uint8_t* epi = smem + (size_t)S * p.stage_bytes;  // kEpiWarps slots of kEpiSlot bytes
+  // Resident weights (one k-block, one n-tile): B hi | lo loaded once.
+  uint8_t* bres = smem + (size_t)S * p.stage_bytes;
+  uint8_t* epi = bres + (p.b_resident ? 2 * (size_t)p.b_bytes : 0);  // epi_warps slots of kEpiSlot bytes
   uint64_t* full = (uint64_t*)(epi + p.epi_warps * kEpiSlot);
   uint64_t* conv = full + kMaxStages;
   uint64_t* empty = conv + kMaxStages;
@@ -374,7 +378,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty = tfull + kMaxAcc;
   uint64_t* rfull = tempty + kMaxAcc;  // per epilogue warp: residual box landed
   uint64_t* drain = rfull + kMaxEpiWarps;
-  uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+  uint64_t* bfull = drain + 1;  // resident weights landed
+  uint32_t* tmem_slot = (uint32_t*)(bfull + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -393,6 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int w = 0; w < kMaxEpiWarps; ++w) bar_init(&rfull[w], 1);
     bar_init(drain, 1);
+    bar_init(bfull, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -413,7 +419,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0, armed = 0, armed_par = 0;
-      const uint32_t tx = p.a_tx + p.b_bytes * (p.presplit ? 2u : 1u);
+      const uint32_t tx = p.a_tx + (p.b_resident ? 0u : p.b_bytes * (p.presplit ? 2u : 1u));
+      if (p.b_resident) {
+        bar_expect_tx(bfull, 2 * p.b_bytes);
+        tma_load_2d(bres, &tmB, bfull, 0, 0);
+        tma_load_2d(bres + p.b_bytes, &tmBlo, bfull, 0, 0);
+      }
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         const int mt = t / p.n_tiles, nt = t % p.n_tiles;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
@@ -433,9 +444,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             tma_load_2d(st, &tmA, &full[s], kb * kBK, mt * kBM);
           }
-          tma_load_2d(st + 2 * kATileBytes, &tmB, &full[s], kb * kBK, nt * p.BN);
-          if (p.presplit)
-            tma_load_2d(st + 2 * kATileBytes + p.b_bytes, &tmBlo, &full[s], kb * kBK, nt * p.BN);
+          if (!p.b_resident) {
+            tma_load_2d(st + 2 * kATileBytes, &tmB, &full[s], kb * kBK, nt * p.BN);
+            if (p.presplit)
+              tma_load_2d(st + 2 * kATileBytes + p.b_bytes, &tmBlo, &full[s], kb * kBK,
+                          nt * p.BN);
+          }
           armed |= 1u << s;
           armed_par = (armed_par & ~(1u << s)) | (ph << s);
           if (++s == S) {
@@ -446,6 +460,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     producer_done:
       if (*abort_flag) {  // let this CTA's own copies land before it exits
+        if (p.b_resident) {
+          volatile int never = 0;
+          bar_wait(bfull, 0, &never, kDrainNs);
+        }
         for (int i = 0; i < S; ++i)
           if (armed & (1u << i)) {
             volatile int never = 0;
@@ -459,6 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0, acc = 0;
       uint32_t ph = 0, aph = 0;
       bool issued = false;
+      if (p.b_resident && !bar_wait(bfull, 0, abort_flag, kTimeoutNs, 64)) goto mma_done;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         if (!bar_wait(&tempty[acc], aph ^ 1, abort_flag, kTimeoutNs, 64)) goto mma_done;
         TC_TRACE(2, (t - blockIdx.x) / gridDim.x);
@@ -470,10 +489,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t a_hi = su32(smem + (size_t)s * p.stage_bytes);
           const uint32_t a_lo = a_hi + kATileBytes;
-          const uint32_t b_hi = a_hi + 2 * kATileBytes;
+          const uint32_t b_hi = p.b_resident ? su32(bres) : a_hi + 2 * kATileBytes;
           const uint32_t b_lo = b_hi + p.b_bytes;
+          // The last k-block stops at the last k-step holding real columns.
+          const int ksteps = kb == p.k_blocks - 1 ? p.last_ksteps : kBK / 8;
 #pragma unroll
           for (int k = 0; k < kBK / 8; ++k) {
+            if (k >= ksteps) break;
             const uint32_t off = k * 32;  // 8 tf32 = 32 bytes along K
             const uint64_t dah = sdesc(a_hi + off), dal = sdesc(a_lo + off);
             const uint64_t dbh = sdesc(b_hi + off), dbl = sdesc(b_lo + off);
@@ -1506,11 +1528,14 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
         wide_budget / bn_stage >= 2)
       p.epi_warps = kMaxEpiWarps;
   }
-  const int budget = 227 * 1024 - 1024 - p.epi_warps * (int)kEpiSlot - 512;
   p.n_tiles = (N + p.BN - 1) / p.BN;
   p.k_blocks = (K + kBK - 1) / kBK;
+  p.last_ksteps = conv ? kBK / 8 : (K - (p.k_blocks - 1) * kBK + 7) / 8;
   p.b_bytes = (uint32_t)p.BN * kBK * 4;
-  p.stage_bytes = 2 * kATileBytes + 2 * p.b_bytes;
+  p.b_resident = g_tc_epi12 && p.presplit && !conv && p.k_blocks == 1 && p.n_tiles == 1;
+  const int budget = 227 * 1024 - 1024 - p.epi_warps * (int)kEpiSlot - 512 -
+                     (p.b_resident ? 2 * (int)p.b_bytes : 0);
+  p.stage_bytes = 2 * kATileBytes + (p.b_resident ? 0 : 2 * p.b_bytes);
   p.stages = budget / (int)p.stage_bytes;
   if (p.stages > kMaxStages) p.stages = kMaxStages;
   if (p.stages < 2) return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_tc: tile does not fit");
@@ -1570,7 +1595,8 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
     if (res && (rc = make_map(&mr, res, M, N, ldc, 32))) return rc;
   }
   const size_t smem =
-      1024 + (size_t)p.stages * p.stage_bytes + p.epi_warps * (size_t)kEpiSlot + 512;
+      1024 + (size_t)p.stages * p.stage_bytes + (p.b_resident ? 2 * (size_t)p.b_bytes : 0) +
+      p.epi_warps * (size_t)kEpiSlot + 512;
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {

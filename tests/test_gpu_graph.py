@@ -41,6 +41,8 @@ CONV_CASES = [
     (1, 30, 30, 64, 16, 3, 2, 1, 1, _lib.ACT_RELU, True, _lib.WEIGHT_HWIO),
     (2, 10, 11, 4, 16, 3, 1, 1, 1, _lib.ACT_RELU, True, _lib.WEIGHT_HWIO),   # direct small-K
     (1, 13, 13, 3, 64, 3, 2, 1, 1, _lib.ACT_RELU6, False, _lib.WEIGHT_OHWI),  # direct small-K
+    (2, 112, 112, 3, 32, 3, 2, 1, 1, _lib.ACT_RELU6, True, _lib.WEIGHT_HWIO),  # 3x3x3 stem
+    (1, 33, 31, 3, 32, 3, 1, 1, 1, _lib.ACT_NONE, False, _lib.WEIGHT_OHWI),   # stem, ragged
 ]
 
 
