@@ -296,12 +296,12 @@ def run_spx(args) -> None:
     per_launch_bytes = d["bytes"] / d["launches"]
     per_launch_s = d["ms"] / d["launches"] / 1e3
     ach = per_launch_bytes / per_launch_s / 1e9
-    # DRAM traffic per launch, from the committed ncu capture of this kernel
-    # (profiles/gemm_tc_expand_16to96_b64.md): dram read + write = 302.9 MB
-    # against 359.6 MB algorithmic for that launch (ratio 0.842; the balance
+    # DRAM traffic per launch, from an ncu --set full capture of this kernel
+    # (expand 16 -> 96 at batch 64): dram read + write = 301.1 MB
+    # against 359.6 MB algorithmic for that launch (ratio 0.837; the balance
     # was still in L2 when the kernel ended).  Scaled to this class's average
     # algorithmic bytes per launch; only meaningful for the GEMM class.
-    traffic = round(per_launch_bytes * (302.9 / 359.6)) if top == "conv1x1" else None
+    traffic = round(per_launch_bytes * (301.1 / 359.6)) if top == "conv1x1" else None
     roofline = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": traffic,
                 "traffic_source": "ncu capture of one gemm_tc launch (expand 16->96, batch 64), "
