@@ -138,3 +138,25 @@ def test_lowering_dispatch_sequence_with_oracle(oracle_built):
     assert c["relu6.spv"] == 36 - 17 - 1 + 17
     assert c["add.spv"] == 10 and c["softmax1000.spv"] == 1
     assert out.shape == (1, 1001) and abs(float(out.sum()) - 1.0) < 1e-5
+
+
+def test_process_options(spx_built):
+    """Path options are host-side state: defaults, round trip, range errors."""
+    defaults = {"gemm_path": 0, "dw_path": 0, "pw_path": 0, "tc_wide_epilogue": 1,
+                "tc_conv_groups": 2}
+    for name, v in defaults.items():
+        assert _lib.get_option(name) == v, name
+    assert _lib.get_option("no_such_option") == -1
+    for name, v, bad in (("pw_path", 1, 2), ("tc_wide_epilogue", 0, 2), ("tc_conv_groups", 1, 3),
+                         ("dw_path", 1, 2), ("gemm_path", 2, 3)):
+        try:
+            _lib.set_option(name, v)
+            assert _lib.get_option(name) == v
+            with pytest.raises(_lib.SpxError) as e:
+                _lib.set_option(name, bad)
+            assert e.value.code == _lib.SPX_ERR_INVALID_ARGUMENT
+            assert _lib.get_option(name) == v
+        finally:
+            _lib.set_option(name, defaults[name])
+    with pytest.raises(_lib.SpxError):
+        _lib.set_option("no_such_option", 0)
