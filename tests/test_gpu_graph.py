@@ -69,6 +69,8 @@ def test_conv2d_nhwc(g, case):
 
 
 @pytest.mark.parametrize("n,ih,c,k,s,dil,act", [(2, 14, 32, 3, 1, 1, _lib.ACT_RELU6),
+                                               (1, 56, 144, 3, 1, 1, _lib.ACT_RELU6),
+                                               (2, 28, 192, 3, 1, 1, _lib.ACT_NONE),
                                                (1, 15, 96, 3, 2, 1, _lib.ACT_RELU6),
                                                (2, 9, 5, 5, 1, 1, _lib.ACT_NONE),
                                                (1, 12, 8, 3, 1, 2, _lib.ACT_RELU),
