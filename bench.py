@@ -203,12 +203,23 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+_WORKLOADS = {
+    "mobilenet_v2": "mobilenet_v2 224x224x3 fp32 NHWC inference",
+    "efficientnet_lite0": "efficientnet_lite0 224x224x3 fp32 NHWC inference",
+    "resnet50": "resnet50 v1.5 224x224x3 fp32 NHWC inference (HLO graph)",
+    "bert": "bert-base encoder fp32, seq 128 (HLO graph)",
+}
+
+
 def _config(args, world) -> dict:
-    return {"workload": f"{args.model} 224x224x3 fp32 NHWC inference, batch {args.batch} per GPU",
+    l2 = ("step working set larger than L2 (fp32 weights ~440 MB read every step, plus "
+          "activations)" if args.model == "bert" else
+          "inputs larger than L2 (each step reads a >126 MB input and writes ~GBs of "
+          "activations)")
+    return {"workload": f"{_WORKLOADS.get(args.model, args.model)}, batch {args.batch} per GPU",
             "batch_per_gpu": args.batch, "global_batch": args.batch * world,
             "parallelism": f"dp{world} (batch-sharded replicas, no collective)",
-            "l2": "inputs larger than L2 (each step reads a >126 MB input and writes ~GBs of "
-                  "activations)", "cuda_graph": True}
+            "l2": l2, "cuda_graph": True}
 
 
 def run_spx(args) -> None:
@@ -302,13 +313,28 @@ def run_spx(args) -> None:
     # was still in L2 when the kernel ended).  Scaled to this class's average
     # algorithmic bytes per launch; only meaningful for the GEMM class.
     traffic = round(per_launch_bytes * (301.1 / 359.6)) if top == "conv1x1" else None
-    roofline = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"],
-                "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": traffic,
-                "traffic_source": "ncu capture of one gemm_tc launch (expand 16->96, batch 64), "
-                                  "dram bytes / algorithmic bytes scaled to the class average",
-                "kernel": top, "peak_source": peaks["source"],
-                "note": "achieved = algorithmic bytes per launch / CUDA-event launch time, "
-                        "averaged over the class's launches in one eager pass"}
+    # The dominant class is tensor-bound when its FLOPs per byte exceed the
+    # ridge of the fp32-accurate tensor rate: 3xTF32 issues three tf32 MMAs
+    # per fp32 product and dense tf32 runs at half the measured bf16 rate.
+    fp32_tc = peaks["bf16_tflops"] / 2.0 / 3.0
+    ridge = fp32_tc * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    if d["bytes"] and d["flops"] / d["bytes"] > ridge:
+        ach_tf = d["flops"] / (d["ms"] / 1e3) / 1e12
+        roofline = {"bound": "tensor", "achieved": round(ach_tf, 2), "peak": round(fp32_tc, 1),
+                    "unit": "TFLOP/s", "frac": round(ach_tf / fp32_tc, 4), "traffic": None,
+                    "kernel": top, "peak_source": peaks["source"] + " (bf16 / 2 / 3: the "
+                    "3xTF32 fp32-accurate ceiling)",
+                    "note": "achieved = fp32 FLOPs of the class / its CUDA-event time in one "
+                            "eager pass"}
+    else:
+        roofline = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"],
+                    "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": traffic,
+                    "traffic_source": "ncu capture of one gemm_tc launch (expand 16->96, batch "
+                                      "64), dram bytes / algorithmic bytes scaled to the class "
+                                      "average",
+                    "kernel": top, "peak_source": peaks["source"],
+                    "note": "achieved = algorithmic bytes per launch / CUDA-event launch time, "
+                            "averaged over the class's launches in one eager pass"}
     sum_roof_ms = sum(max(c["bytes"] / (peaks["hbm_gbs"] * 1e9),
                           c["flops"] / (tc_eff * 1e12)) * 1e3 for c in costs)
 
