@@ -293,7 +293,9 @@ def run_spx(args) -> None:
         d["flops"] += c["flops"]
         d["launches"] += 1
     total_ms = float(times.sum())
-    tc_eff = peaks["bf16_tflops"] / 2.0  # fp32-accurate math rate bound used for FLOP ceilings
+    # fp32-accurate tensor rate for FLOP ceilings: 3xTF32 issues three tf32
+    # MMAs per fp32 product and dense tf32 runs at half the measured bf16 rate.
+    fp32_tc = peaks["bf16_tflops"] / 2.0 / 3.0
     per_class = {}
     for k, d in sorted(classes.items(), key=lambda kv: -kv[1]["ms"]):
         t_mem = d["bytes"] / (peaks["hbm_gbs"] * 1e9) * 1e3
@@ -314,9 +316,7 @@ def run_spx(args) -> None:
     # algorithmic bytes per launch; only meaningful for the GEMM class.
     traffic = round(per_launch_bytes * (301.1 / 359.6)) if top == "conv1x1" else None
     # The dominant class is tensor-bound when its FLOPs per byte exceed the
-    # ridge of the fp32-accurate tensor rate: 3xTF32 issues three tf32 MMAs
-    # per fp32 product and dense tf32 runs at half the measured bf16 rate.
-    fp32_tc = peaks["bf16_tflops"] / 2.0 / 3.0
+    # ridge of the fp32-accurate tensor rate.
     ridge = fp32_tc * 1e12 / (peaks["hbm_gbs"] * 1e9)
     if d["bytes"] and d["flops"] / d["bytes"] > ridge:
         ach_tf = d["flops"] / (d["ms"] / 1e3) / 1e12
@@ -336,7 +336,7 @@ def run_spx(args) -> None:
                     "note": "achieved = algorithmic bytes per launch / CUDA-event launch time, "
                             "averaged over the class's launches in one eager pass"}
     sum_roof_ms = sum(max(c["bytes"] / (peaks["hbm_gbs"] * 1e9),
-                          c["flops"] / (tc_eff * 1e12)) * 1e3 for c in costs)
+                          c["flops"] / (fp32_tc * 1e12)) * 1e3 for c in costs)
 
     # ---- end to end through the host API (pinned host in/out, overlapped) ----
     copy = torch.cuda.Stream()
