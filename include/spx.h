@@ -91,6 +91,16 @@ int spx_select_device(const char* selector, int* ordinal);
 int spx_set_option(const char* name, int64_t value);
 int64_t spx_get_option(const char* name);
 
+/* Diagnostics: the tensor-core GEMM's launch plan for an M x N x K product
+ * (no device work; `conv` = implicit-GEMM conv mode, `vec4` = C / residual /
+ * bias allow 16-byte access).  out[0..15] = N tile, n tiles, k-blocks,
+ * k-steps of the last k-block, ring stages, stage bytes, epilogue warps,
+ * converter groups, epilogue groups, TMEM accumulators, TMEM columns,
+ * resident weights, dynamic shared memory bytes, m tiles, converter threads,
+ * grid.  n_out >= 16. */
+int spx_gemm_tc_plan(int32_t M, int32_t N, int32_t K, int32_t presplit, int32_t conv,
+                     int32_t vec4, int32_t* out, int32_t n_out);
+
 /* ---- kernel registry (mirror of kernels.rs:12-238 + HLO kernels) ------- */
 int spx_kernel_count(void);
 /* Name of registry entry i (0 <= i < spx_kernel_count()), NULL if out of range. */

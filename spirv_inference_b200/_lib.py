@@ -93,6 +93,8 @@ _SIGS = {
     "spx_select_device": ([c_char_p, POINTER(c_int)], c_int),
     "spx_set_option": ([c_char_p, c_int64], c_int),
     "spx_get_option": ([c_char_p], c_int64),
+    "spx_gemm_tc_plan": ([c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p,
+                          c_int32], c_int),
     "spx_kernel_count": ([], c_int),
     "spx_kernel_name": ([c_int], c_char_p),
     "spx_kernel_push_count": ([c_char_p], c_int),
@@ -207,3 +209,16 @@ def last_error() -> str:
 def check(rc: int) -> None:
     if rc != SPX_OK:
         raise SpxError(rc, last_error())
+
+
+_PLAN_KEYS = ("BN", "n_tiles", "k_blocks", "last_ksteps", "stages", "stage_bytes", "epi_warps",
+              "conv_groups", "groups", "nacc", "tmem_cols", "b_resident", "smem_bytes",
+              "m_tiles", "conv_threads", "grid")
+
+
+def gemm_tc_plan(m: int, n: int, k: int, presplit: bool = True, conv: bool = False,
+                 vec4: bool = True) -> dict:
+    """The tensor-core GEMM's launch plan for an m x n x k product (host only)."""
+    out = (c_int32 * 16)()
+    check(lib().spx_gemm_tc_plan(m, n, k, int(presplit), int(conv), int(vec4), out, 16))
+    return dict(zip(_PLAN_KEYS, list(out)))

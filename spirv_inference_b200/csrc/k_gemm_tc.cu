@@ -107,6 +107,7 @@ struct TcArgs {
   int conv_groups;  // converter groups splitting alternate stages (1 or 2)
   int last_ksteps;  // 8-wide k-steps of the last k-block that hold columns < K
   int b_resident;   // one k-block and one n-tile: pre-split B loaded once, not per stage
+  uint32_t smem_bytes;  // dynamic shared memory of the launch
   int epi_warps;  // epilogue warps in use (4, 8 or 12): long k-loops trade them for stages,
                   // 1-block k-loops take 12 (warps 8-11 leave the converters)
 };
@@ -1462,20 +1463,22 @@ int launch_conv_tc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
                         q->oc, 1.0f, q->activation, &g, &mx, (q->n + tn - 1) / tn);
 }
 
-int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, const float* b,
-                   const float* b_lo, int64_t ldb, int M, int N, int K, const float* bias,
-                   const float* res, float* c, int64_t ldc, float alpha, int act,
-                   const ConvGeom* conv, const void* conv_map, int conv_img_groups) {
-  TcArgs p = {};
+// Per-shape configuration of gemm_tc_kernel (no device access): tile width,
+// ring depth, warp roles, accumulators.  `conv` marks the implicit-GEMM conv
+// mode, `m_tiles` is the number of 128-row tiles, `vec4` whether C / residual
+// / bias allow 16-byte access.
+int plan_gemm_tc(TcArgs& p, int M, int N, int K, bool presplit, bool conv, int m_tiles,
+                 bool vec4) {
+  p = TcArgs{};
   p.M = M;
   p.N = N;
   p.K = K;
-  p.presplit = b_lo != nullptr;
+  p.presplit = presplit;
   // N tile: a multiple of 32 (the epilogue's chunk), at most 256 (UMMA N),
   // halved while there are fewer than two tiles per SM.
   const int nt0 = (N + 255) / 256;
   p.BN = ((N + nt0 - 1) / nt0 + 31) / 32 * 32;
-  p.m_tiles = conv ? conv_img_groups * conv->tiles_h * conv->tiles_w : (M + kBM - 1) / kBM;
+  p.m_tiles = m_tiles;
   // More, narrower tiles only pay while the k-loop is short: every n-tile
   // re-splits the same A tiles and narrow UMMAs cost nearly as much to issue
   // as wide ones.
@@ -1539,8 +1542,7 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   p.stages = budget / (int)p.stage_bytes;
   if (p.stages > kMaxStages) p.stages = kMaxStages;
   if (p.stages < 2) return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_tc: tile does not fit");
-  auto al16 = [](const void* q) { return ((uintptr_t)q & 15) == 0; };
-  p.vec4 = (ldc % 4 == 0) && al16(c) && (!res || al16(res)) && (!bias || al16(bias));
+  p.vec4 = vec4;
   p.tma_store = p.vec4 && !conv;
   // One 32-column chunk per lane quarter: the two halves of the epilogue take
   // alternate tiles (four accumulators) so two tiles drain at once.
@@ -1558,6 +1560,22 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
             | (2u << 7) | (2u << 10)           // A, B: TF32
             | ((uint32_t)(p.BN >> 3) << 17)    // N
             | ((uint32_t)(kBM >> 4) << 24);    // M
+  p.smem_bytes = 1024 + (uint32_t)p.stages * p.stage_bytes +
+                 (p.b_resident ? 2 * p.b_bytes : 0u) + (uint32_t)p.epi_warps * kEpiSlot + 512;
+  return SPX_OK;
+}
+
+int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, const float* b,
+                   const float* b_lo, int64_t ldb, int M, int N, int K, const float* bias,
+                   const float* res, float* c, int64_t ldc, float alpha, int act,
+                   const ConvGeom* conv, const void* conv_map, int conv_img_groups) {
+  TcArgs p;
+  auto al16 = [](const void* q) { return ((uintptr_t)q & 15) == 0; };
+  const bool vec4 = (ldc % 4 == 0) && al16(c) && (!res || al16(res)) && (!bias || al16(bias));
+  const int m_tiles =
+      conv ? conv_img_groups * conv->tiles_h * conv->tiles_w : (M + kBM - 1) / kBM;
+  int rc0 = plan_gemm_tc(p, M, N, K, b_lo != nullptr, conv != nullptr, m_tiles, vec4);
+  if (rc0) return rc0;
   p.bias = bias;
   p.res = res;
   p.c = c;
@@ -1594,9 +1612,7 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
     if ((rc = make_map(&mc, c, M, N, ldc, 32))) return rc;
     if (res && (rc = make_map(&mr, res, M, N, ldc, 32))) return rc;
   }
-  const size_t smem =
-      1024 + (size_t)p.stages * p.stage_bytes + (p.b_resident ? 2 * (size_t)p.b_bytes : 0) +
-      p.epi_warps * (size_t)kEpiSlot + 512;
+  const size_t smem = p.smem_bytes;
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
@@ -1699,6 +1715,29 @@ extern "C" int spx_tc_trace_fetch(unsigned long long* out) {
   return cudaMemcpyFromSymbol(out, g_tc_trace, sizeof(g_tc_trace)) == cudaSuccess ? 0 : 3;
 }
 #endif
+
+// Host-side view of the tensor-core GEMM's per-shape plan (no device work):
+// out[0..15] = BN, n_tiles, k_blocks, last_ksteps, stages, stage_bytes,
+// epi_warps, conv_groups, epilogue groups, accumulators, TMEM columns,
+// resident weights, dynamic smem bytes, m_tiles, converter threads, grid.
+extern "C" int spx_gemm_tc_plan(int32_t M, int32_t N, int32_t K, int32_t presplit, int32_t conv,
+                                int32_t vec4, int32_t* out, int32_t n_out) {
+  if (!out || n_out < 16 || M <= 0 || N <= 0 || K <= 0)
+    return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_tc_plan: bad arguments");
+  TcArgs p;
+  const int m_tiles = (M + kBM - 1) / kBM;
+  int rc = plan_gemm_tc(p, M, N, K, presplit != 0, conv != 0, m_tiles, vec4 != 0);
+  if (rc) return rc;
+  const int conv_lo = p.epi_warps > kEpiWarps ? p.epi_warps : kEpiWarps;
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int32_t v[16] = {p.BN, p.n_tiles, p.k_blocks, p.last_ksteps, p.stages,
+                         (int32_t)p.stage_bytes, p.epi_warps, p.conv_groups, p.groups, p.nacc,
+                         (int32_t)p.tmem_cols, p.b_resident, (int32_t)p.smem_bytes, p.m_tiles,
+                         (kEpiWarps + kConvWarps - conv_lo) * 32,
+                         tiles < sm_count() ? tiles : sm_count()};
+  for (int i = 0; i < 16; ++i) out[i] = v[i];
+  return SPX_OK;
+}
 
 int launch_expand_dw_tc(cudaStream_t s, int64_t* cnt, const float* x, const float* we_hi,
                         const float* we_lo, const float* be, const float* wd, const float* bd,
