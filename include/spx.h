@@ -87,7 +87,10 @@ int spx_select_device(const char* selector, int* ordinal);
  * output chunks, and for N <= 32 split the epilogue into two groups draining
  * alternate tiles; 0 = never.
  * "tc_conv_groups": 2 (default) = tensor-core GEMMs with several k-blocks per
- * tile split two stages at once (two converter groups), 1 = one at a time. */
+ * tile split two stages at once (two converter groups), 1 = one at a time.
+ * "tc_lo_tmem": 1 = with pre-split weights and several k-blocks the
+ * activations' tf32 lo terms are written to tensor memory and the lo*hi MMA
+ * reads its A operand from there; 0 (default) = lo terms in shared memory. */
 int spx_set_option(const char* name, int64_t value);
 int64_t spx_get_option(const char* name);
 
@@ -97,7 +100,7 @@ int64_t spx_get_option(const char* name);
  * k-steps of the last k-block, ring stages, stage bytes, epilogue warps,
  * converter groups, epilogue groups, TMEM accumulators, TMEM columns,
  * resident weights, dynamic shared memory bytes, m tiles, converter threads,
- * grid.  n_out >= 16. */
+ * grid, lo terms in tensor memory.  n_out >= 17. */
 int spx_gemm_tc_plan(int32_t M, int32_t N, int32_t K, int32_t presplit, int32_t conv,
                      int32_t vec4, int32_t* out, int32_t n_out);
 

@@ -213,12 +213,12 @@ def check(rc: int) -> None:
 
 _PLAN_KEYS = ("BN", "n_tiles", "k_blocks", "last_ksteps", "stages", "stage_bytes", "epi_warps",
               "conv_groups", "groups", "nacc", "tmem_cols", "b_resident", "smem_bytes",
-              "m_tiles", "conv_threads", "grid")
+              "m_tiles", "conv_threads", "grid", "lo_tmem")
 
 
 def gemm_tc_plan(m: int, n: int, k: int, presplit: bool = True, conv: bool = False,
                  vec4: bool = True) -> dict:
     """The tensor-core GEMM's launch plan for an m x n x k product (host only)."""
-    out = (c_int32 * 16)()
-    check(lib().spx_gemm_tc_plan(m, n, k, int(presplit), int(conv), int(vec4), out, 16))
+    out = (c_int32 * 17)()
+    check(lib().spx_gemm_tc_plan(m, n, k, int(presplit), int(conv), int(vec4), out, 17))
     return dict(zip(_PLAN_KEYS, list(out)))

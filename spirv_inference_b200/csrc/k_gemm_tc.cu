@@ -48,6 +48,7 @@ namespace spx {
 __device__ int g_tc_status = 0;
 int g_tc_epi12 = 1;
 int g_tc_conv2 = 1;
+int g_tc_lo_tmem = 0;
 
 #ifdef SPX_TC_TRACE
 // Development-only pipeline trace of CTA 0 (not compiled into the library).
@@ -107,6 +108,8 @@ struct TcArgs {
   int conv_groups;  // converter groups splitting alternate stages (1 or 2)
   int last_ksteps;  // 8-wide k-steps of the last k-block that hold columns < K
   int b_resident;   // one k-block and one n-tile: pre-split B loaded once, not per stage
+  int lo_tmem;      // activation lo terms in two TMEM slots (A operand from TMEM)
+  int lo_col;       // first TMEM column of the two 32-column lo slots
   uint32_t smem_bytes;  // dynamic shared memory of the launch
   int epi_warps;  // epilogue warps in use (4, 8 or 12): long k-loops trade them for stages,
                   // 1-block k-loops take 12 (warps 8-11 leave the converters)
@@ -229,6 +232,26 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
           su32(bar))
       : "memory");
 }
+// A operand from tensor memory (lane = row, one 32-bit column per k element).
+__device__ __forceinline__ void umma_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate));
+}
+// This thread's TMEM lane, 16 consecutive columns from taddr.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -380,7 +403,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* rfull = tempty + kMaxAcc;  // per epilogue warp: residual box landed
   uint64_t* drain = rfull + kMaxEpiWarps;
   uint64_t* bfull = drain + 1;  // resident weights landed
-  uint32_t* tmem_slot = (uint32_t*)(bfull + 1);
+  uint64_t* lo_empty = bfull + 1;  // [2]: MMAs reading a TMEM lo slot are done
+  uint32_t* tmem_slot = (uint32_t*)(lo_empty + 2);
+  // B's offset within a stage: after the raw A tile and, unless the lo terms
+  // live in TMEM, the A lo tile.
+  const uint32_t b_off = p.lo_tmem ? kATileBytes : 2 * kATileBytes;
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -400,6 +427,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = 0; w < kMaxEpiWarps; ++w) bar_init(&rfull[w], 1);
     bar_init(drain, 1);
     bar_init(bfull, 1);
+    bar_init(&lo_empty[0], 1);
+    bar_init(&lo_empty[1], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -446,9 +475,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(st, &tmA, &full[s], kb * kBK, mt * kBM);
           }
           if (!p.b_resident) {
-            tma_load_2d(st + 2 * kATileBytes, &tmB, &full[s], kb * kBK, nt * p.BN);
+            tma_load_2d(st + b_off, &tmB, &full[s], kb * kBK, nt * p.BN);
             if (p.presplit)
-              tma_load_2d(st + 2 * kATileBytes + p.b_bytes, &tmBlo, &full[s], kb * kBK,
+              tma_load_2d(st + b_off + p.b_bytes, &tmBlo, &full[s], kb * kBK,
                           nt * p.BN);
           }
           armed |= 1u << s;
@@ -490,7 +519,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t a_hi = su32(smem + (size_t)s * p.stage_bytes);
           const uint32_t a_lo = a_hi + kATileBytes;
-          const uint32_t b_hi = p.b_resident ? su32(bres) : a_hi + 2 * kATileBytes;
+          const uint32_t b_hi = p.b_resident ? su32(bres) : a_hi + b_off;
+          const uint32_t lo_t = tmem + (uint32_t)p.lo_col + (uint32_t)((s & 1) * kBK);
           const uint32_t b_lo = b_hi + p.b_bytes;
           // The last k-block stops at the last k-step holding real columns.
           const int ksteps = kb == p.k_blocks - 1 ? p.last_ksteps : kBK / 8;
@@ -500,12 +530,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t off = k * 32;  // 8 tf32 = 32 bytes along K
             const uint64_t dah = sdesc(a_hi + off), dal = sdesc(a_lo + off);
             const uint64_t dbh = sdesc(b_hi + off), dbl = sdesc(b_lo + off);
-            umma_tf32(d, dal, dbh, p.idesc, (kb | k) ? 1u : 0u);
+            if (p.lo_tmem)
+              umma_tf32_ta(d, lo_t + (uint32_t)(k * 8), dbh, p.idesc, (kb | k) ? 1u : 0u);
+            else
+              umma_tf32(d, dal, dbh, p.idesc, (kb | k) ? 1u : 0u);
             umma_tf32(d, dah, dbl, p.idesc, 1u);
             umma_tf32(d, dah, dbh, p.idesc, 1u);
           }
           issued = true;
           umma_commit(&empty[s]);
+          if (p.lo_tmem) umma_commit(&lo_empty[s & 1]);
           if (++s == S) {
             s = 0;
             ph ^= 1;
@@ -533,23 +567,58 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int cg = (threadIdx.x - conv_lo * 32) / gthreads;
     const int ct = (threadIdx.x - conv_lo * 32) % gthreads;
     int s = 0;
-    uint32_t ph = 0;
+    uint32_t ph = 0, lph[2] = {0, 0};
+    // TMEM lo: thread = tile row (its warp's TMEM lane quarter), the group's
+    // warps of one quarter share the row's 32 columns.
+    const int wpq = gthreads / 128;  // warps per lane quarter in a group (1 or 2)
+    const int lo_cols = kBK / wpq;
+    const int lo_c0 = ((ct >> 5) >> 2) * lo_cols;
+    const int lo_row = (warp & 3) * 32 + lane;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       for (int kb = 0; kb < p.k_blocks; ++kb) {
         if (s % p.conv_groups == cg) {
           if (!bar_wait(&full[s], ph, abort_flag, kTimeoutNs, 256)) goto conv_done;
           if (kb == 0 && ct == 0) TC_TRACE(7, (t - blockIdx.x) / gridDim.x);
           uint8_t* st = smem + (size_t)s * p.stage_bytes;
+          if (p.lo_tmem) {
+            // The slot's previous readers (the MMAs of stage s - 2) are done.
+            if (!bar_wait(&lo_empty[s & 1], lph[s & 1] ^ 1, abort_flag, kTimeoutNs, 64))
+              goto conv_done;
+            lph[s & 1] ^= 1;
+            tc_fence_after();
+            const uint8_t* rowp = st + lo_row * 128;
+            const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) +
+                                   (uint32_t)(p.lo_col + (s & 1) * kBK + lo_c0);
+            for (int h = 0; h < lo_cols; h += 16) {
+              uint32_t r[16];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int c4 = (lo_c0 + h) / 4 + q;  // 16-byte chunk of the 128-byte row
+                const float4 v =
+                    *reinterpret_cast<const float4*>(rowp + ((c4 ^ (lo_row & 7)) << 4));
+                r[4 * q + 0] = __float_as_uint(lo_of_raw(v.x));
+                r[4 * q + 1] = __float_as_uint(lo_of_raw(v.y));
+                r[4 * q + 2] = __float_as_uint(lo_of_raw(v.z));
+                r[4 * q + 3] = __float_as_uint(lo_of_raw(v.w));
+              }
+              tmem_st16(taddr + (uint32_t)h, r);
+            }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            bar_arrive(&conv[s]);
+            if (kb == 0 && ct == 0) TC_TRACE(1, (t - blockIdx.x) / gridDim.x);
+            goto next_stage;
+          }
           split_lo_buffer((const float4*)st, (float4*)(st + kATileBytes), kATileBytes / 16, ct,
                           gthreads);
           if (!p.presplit)
-            split_buffer((float4*)(st + 2 * kATileBytes),
-                         (float4*)(st + 2 * kATileBytes + p.b_bytes), p.b_bytes / 16, ct,
-                         gthreads);
+            split_buffer((float4*)(st + b_off), (float4*)(st + b_off + p.b_bytes),
+                         p.b_bytes / 16, ct, gthreads);
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           bar_arrive(&conv[s]);
           if (kb == 0 && ct == 0) TC_TRACE(1, (t - blockIdx.x) / gridDim.x);
         }
+      next_stage:
         if (++s == S) {
           s = 0;
           ph ^= 1;
@@ -1536,25 +1605,34 @@ int plan_gemm_tc(TcArgs& p, int M, int N, int K, bool presplit, bool conv, int m
   p.last_ksteps = conv ? kBK / 8 : (K - (p.k_blocks - 1) * kBK + 7) / 8;
   p.b_bytes = (uint32_t)p.BN * kBK * 4;
   p.b_resident = g_tc_epi12 && p.presplit && !conv && p.k_blocks == 1 && p.n_tiles == 1;
-  const int budget = 227 * 1024 - 1024 - p.epi_warps * (int)kEpiSlot - 512 -
-                     (p.b_resident ? 2 * (int)p.b_bytes : 0);
-  p.stage_bytes = 2 * kATileBytes + (p.b_resident ? 0 : 2 * p.b_bytes);
-  p.stages = budget / (int)p.stage_bytes;
-  if (p.stages > kMaxStages) p.stages = kMaxStages;
-  if (p.stages < 2) return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_tc: tile does not fit");
   p.vec4 = vec4;
   p.tma_store = p.vec4 && !conv;
   // One 32-column chunk per lane quarter: the two halves of the epilogue take
   // alternate tiles (four accumulators) so two tiles drain at once.
+  p.groups = (g_tc_epi12 && p.tma_store && p.BN == 32 && p.epi_warps == kEpiWarps) ? 2 : 1;
+  p.nacc = 2 * p.groups;
+  // Several k-blocks with pre-split weights: the activations' lo terms go to
+  // two 32-column TMEM slots after the accumulators (registers -> TMEM, the
+  // lo*hi MMA reads A from TMEM), so a stage holds only the raw A tile and B.
+  p.lo_tmem = g_tc_lo_tmem && p.presplit && p.k_blocks >= 2 && p.epi_warps <= kEpiWarps &&
+              p.nacc * p.BN + 2 * kBK <= 512;
+  p.lo_col = p.nacc * p.BN;
+  const int budget = 227 * 1024 - 1024 - p.epi_warps * (int)kEpiSlot - 512 -
+                     (p.b_resident ? 2 * (int)p.b_bytes : 0);
+  p.stage_bytes = (p.lo_tmem ? 1 : 2) * kATileBytes + (p.b_resident ? 0 : 2 * p.b_bytes);
+  p.stages = budget / (int)p.stage_bytes;
+  if (p.stages > kMaxStages) p.stages = kMaxStages;
+  if (p.stages < 2) return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_tc: tile does not fit");
+  // The lo-in-TMEM rings are deep enough to give up a stage for an even
+  // count (two converter groups, below).
+  if (p.lo_tmem && g_tc_conv2 && p.stages % 2 && p.stages > 2) --p.stages;
   // Two converter groups own the even and the odd stages: each group then
   // meets every one of its stages once per pass of the ring, so its mbarrier
   // parities stay in step.  That needs an even stage count.
   p.conv_groups =
       (g_tc_conv2 && p.epi_warps <= kEpiWarps && p.k_blocks > 1 && p.stages % 2 == 0) ? 2 : 1;
-  p.groups = (g_tc_epi12 && p.tma_store && p.BN == 32 && p.epi_warps == kEpiWarps) ? 2 : 1;
-  p.nacc = 2 * p.groups;
   uint32_t cols = 32;
-  while (cols < (uint32_t)(p.nacc * p.BN)) cols <<= 1;
+  while (cols < (uint32_t)(p.nacc * p.BN + (p.lo_tmem ? 2 * kBK : 0))) cols <<= 1;
   p.tmem_cols = cols;
   p.idesc = (1u << 4)                          // accumulator F32
             | (2u << 7) | (2u << 10)           // A, B: TF32
@@ -1719,10 +1797,11 @@ extern "C" int spx_tc_trace_fetch(unsigned long long* out) {
 // Host-side view of the tensor-core GEMM's per-shape plan (no device work):
 // out[0..15] = BN, n_tiles, k_blocks, last_ksteps, stages, stage_bytes,
 // epi_warps, conv_groups, epilogue groups, accumulators, TMEM columns,
-// resident weights, dynamic smem bytes, m_tiles, converter threads, grid.
+// resident weights, dynamic smem bytes, m_tiles, converter threads, grid,
+// lo terms in TMEM.
 extern "C" int spx_gemm_tc_plan(int32_t M, int32_t N, int32_t K, int32_t presplit, int32_t conv,
                                 int32_t vec4, int32_t* out, int32_t n_out) {
-  if (!out || n_out < 16 || M <= 0 || N <= 0 || K <= 0)
+  if (!out || n_out < 17 || M <= 0 || N <= 0 || K <= 0)
     return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_tc_plan: bad arguments");
   TcArgs p;
   const int m_tiles = (M + kBM - 1) / kBM;
@@ -1730,12 +1809,12 @@ extern "C" int spx_gemm_tc_plan(int32_t M, int32_t N, int32_t K, int32_t prespli
   if (rc) return rc;
   const int conv_lo = p.epi_warps > kEpiWarps ? p.epi_warps : kEpiWarps;
   const int tiles = p.m_tiles * p.n_tiles;
-  const int32_t v[16] = {p.BN, p.n_tiles, p.k_blocks, p.last_ksteps, p.stages,
+  const int32_t v[17] = {p.BN, p.n_tiles, p.k_blocks, p.last_ksteps, p.stages,
                          (int32_t)p.stage_bytes, p.epi_warps, p.conv_groups, p.groups, p.nacc,
                          (int32_t)p.tmem_cols, p.b_resident, (int32_t)p.smem_bytes, p.m_tiles,
                          (kEpiWarps + kConvWarps - conv_lo) * 32,
-                         tiles < sm_count() ? tiles : sm_count()};
-  for (int i = 0; i < 16; ++i) out[i] = v[i];
+                         tiles < sm_count() ? tiles : sm_count(), p.lo_tmem};
+  for (int i = 0; i < 17; ++i) out[i] = v[i];
   return SPX_OK;
 }
 

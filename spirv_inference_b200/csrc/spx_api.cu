@@ -471,6 +471,11 @@ int spx_set_option(const char* name, int64_t value) {
     g_tc_epi12 = (int)value;
     return SPX_OK;
   }
+  if (n == "tc_lo_tmem") {
+    if (value < 0 || value > 1) return fail(SPX_ERR_INVALID_ARGUMENT, "tc_lo_tmem must be 0..1");
+    g_tc_lo_tmem = (int)value;
+    return SPX_OK;
+  }
   if (n == "tc_conv_groups") {
     if (value < 1 || value > 2) return fail(SPX_ERR_INVALID_ARGUMENT, "tc_conv_groups must be 1..2");
     g_tc_conv2 = value == 2;
@@ -496,6 +501,7 @@ int64_t spx_get_option(const char* name) {
   if (n == "pw_path") return g_pw_path;
   if (n == "tc_wide_epilogue") return g_tc_epi12;
   if (n == "tc_conv_groups") return g_tc_conv2 ? 2 : 1;
+  if (n == "tc_lo_tmem") return g_tc_lo_tmem;
   return -1;
 }
 

@@ -239,6 +239,7 @@ int ar_take_status();
 extern int g_gemm_path;
 extern int g_tc_epi12;
 extern int g_tc_conv2;
+extern int g_tc_lo_tmem;
 // Depthwise path: 0 automatic (TMA tiles where the shape allows), 1 register
 // sliding-window kernel only.
 extern int g_dw_path;

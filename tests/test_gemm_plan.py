@@ -55,7 +55,12 @@ def _check(plan, m, n, k):
         assert bn == 32 and plan["epi_warps"] == 8
     assert plan["nacc"] == 2 * plan["groups"]
     cols = plan["tmem_cols"]
-    assert cols & (cols - 1) == 0 and 32 <= cols <= 512 and cols >= plan["nacc"] * bn
+    lo_cols = 64 if plan["lo_tmem"] else 0
+    assert cols & (cols - 1) == 0 and 32 <= cols <= 512
+    assert cols >= plan["nacc"] * bn + lo_cols
+    if plan["lo_tmem"]:  # two 32-column lo slots after the accumulators
+        assert plan["k_blocks"] >= 2 and plan["epi_warps"] <= 8
+        assert plan["stage_bytes"] == 16384 + 2 * bn * 128
     if plan["b_resident"]:
         assert plan["k_blocks"] == 1 and plan["n_tiles"] == 1
     # every 32-column chunk of a tile has an epilogue warp per lane quarter
@@ -71,7 +76,7 @@ def test_plan_invariants(spx_built, m, n, k):
             plan = _lib.gemm_tc_plan(m, n, k, presplit=presplit, vec4=vec4)
             _check(plan, m, n, k)
             if not presplit:
-                assert plan["b_resident"] == 0
+                assert plan["b_resident"] == 0 and plan["lo_tmem"] == 0
             if not vec4:  # no TMA stores: one epilogue group
                 assert plan["groups"] == 1
 
@@ -80,13 +85,15 @@ def test_plan_options_restore_plain_layout(spx_built):
     try:
         _lib.set_option("tc_wide_epilogue", 0)
         _lib.set_option("tc_conv_groups", 1)
+        _lib.set_option("tc_lo_tmem", 0)
         for m, n, k in SHAPES:
             p = _lib.gemm_tc_plan(m, n, k)
             assert p["epi_warps"] in (4, 8) and p["groups"] == 1 and p["conv_groups"] == 1
-            assert p["b_resident"] == 0
+            assert p["b_resident"] == 0 and p["lo_tmem"] == 0
     finally:
         _lib.set_option("tc_wide_epilogue", 1)
         _lib.set_option("tc_conv_groups", 2)
+        _lib.set_option("tc_lo_tmem", 0)
 
 
 def test_plan_known_configurations(spx_built):
@@ -98,7 +105,26 @@ def test_plan_known_configurations(spx_built):
     assert (p["BN"], p["groups"], p["nacc"]) == (32, 2, 4)
     # project 144 -> 24: five k-blocks, two converter groups on an even ring
     p = _lib.gemm_tc_plan(802816, 24, 144)
-    assert p["k_blocks"] == 5 and p["conv_groups"] == 2 and p["stages"] % 2 == 0
+    assert p["k_blocks"] == 5 and p["lo_tmem"] == 0
+    assert p["conv_groups"] == 2 and p["stages"] % 2 == 0
+    # with the lo terms in TMEM the stages shrink to raw A + B and the ring deepens
+    _lib.set_option("tc_lo_tmem", 1)
+    try:
+        q = _lib.gemm_tc_plan(802816, 24, 144)
+    finally:
+        _lib.set_option("tc_lo_tmem", 0)
+    assert q["lo_tmem"] == 1 and q["stages"] > p["stages"] and q["stages"] % 2 == 0
+    assert q["tmem_cols"] >= q["nacc"] * q["BN"] + 64
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_plan_invariants_lo_in_tmem(spx_built, m, n, k):
+    _lib.set_option("tc_lo_tmem", 1)
+    try:
+        for presplit in (True, False):
+            _check(_lib.gemm_tc_plan(m, n, k, presplit=presplit), m, n, k)
+    finally:
+        _lib.set_option("tc_lo_tmem", 0)
 
 
 def test_plan_rejects_bad_arguments(spx_built):

@@ -141,3 +141,51 @@ def test_conv_tc_implicit_gemm(g, n, ih, ic, oc, k, s, pad):
     K = k * k * ic
     err = np.abs(outs[0] - ref).max() / np.abs(ref).max()
     assert err <= 2.5e-8 * K + 1e-6, err
+
+
+@pytest.mark.parametrize("M,N,K", [(802816, 24, 144), (50176, 64, 384), (4096, 768, 768),
+                                   (517, 144, 96), (12544, 1280, 320)])
+def test_tc_lo_terms_in_tmem_match_shared_memory(g, M, N, K):
+    """Option tc_lo_tmem: the activations' lo terms written to tensor memory
+    (the lo*hi MMA reads A from TMEM) give bit-identical results to the
+    shared-memory lo tiles — the same tf32 terms in the same MMA order."""
+    a = _r(M, K)
+    w = _r(N, K, scale=1.0 / np.sqrt(K))
+    bias = _r(N)
+    da, dw, db = g.tensor(a), g.tensor(w), g.tensor(bias)
+    split = g.weights_split(dw)
+    outs = []
+    for lo_tmem in (0, 1):
+        _lib.set_option("tc_lo_tmem", lo_tmem)
+        try:
+            dc = g.alloc((M, N))
+            g.gemm(da, dw, dc, m=M, n=N, k=K, a_strides=(0, K, 1), b_strides=(0, 1, K),
+                   c_strides=(0, N), bias=db, activation=_lib.ACT_RELU6, b_split=split)
+            outs.append(dc.download())
+        finally:
+            _lib.set_option("tc_lo_tmem", 0)
+    np.testing.assert_array_equal(outs[0], outs[1])
+    ref = np.clip(a[:4096].astype(np.float64) @ w.T.astype(np.float64) + bias, 0, 6)
+    err = np.abs(outs[1][:4096] - ref).max() / max(np.abs(ref).max(), 1e-30)
+    assert err <= 2.5e-8 * K + 1e-6, err
+
+
+def test_conv_tc_lo_terms_in_tmem(g):
+    n, ih, ic, oc, k, s, pad = 2, 28, 64, 96, 3, 1, 1
+    oh = (ih + 2 * pad - k) // s + 1
+    x = _r(n, ih, ih, ic)
+    w = _r(oc, k, k, ic, scale=1.0 / np.sqrt(k * k * ic))
+    b = _r(oc)
+    dx, dw, db = g.tensor(x), g.tensor(w), g.tensor(b)
+    split = g.weights_split(dw)
+    outs = []
+    for lo_tmem in (0, 1):
+        _lib.set_option("tc_lo_tmem", lo_tmem)
+        try:
+            dy = g.alloc((n, oh, oh, oc))
+            g.conv2d_nhwc(dx, dw, db, dy, stride=(s, s), pad=(pad, pad),
+                          activation=_lib.ACT_RELU, w_split=split)
+            outs.append(dy.download())
+        finally:
+            _lib.set_option("tc_lo_tmem", 0)
+    np.testing.assert_array_equal(outs[0], outs[1])
