@@ -161,3 +161,18 @@ def test_process_options(spx_built):
             _lib.set_option(name, defaults[name])
     with pytest.raises(_lib.SpxError):
         _lib.set_option("no_such_option", 0)
+
+
+def test_plain_c_host_against_header_and_library(spx_built, tmp_path):
+    """include/spx.h compiles as C99 and a C program linked against libspx.so
+    (the view of a cgo / FFI binding) passes its host-side checks."""
+    here = Path(__file__).resolve().parent
+    lib = Path(spx_built)
+    exe = tmp_path / "host_check"
+    cc = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", str(here.parent / "include"),
+                         str(here / "c_host" / "host_check.c"), "-L", str(lib.parent), "-lspx",
+                         f"-Wl,-rpath,{lib.parent}", "-o", str(exe)],
+                        capture_output=True, text=True)
+    assert cc.returncode == 0, cc.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
