@@ -149,6 +149,18 @@ def reference_pass(name: str, batch: int):
     return lambda: hlo.run_hlo(g, feeds, oracle.run_kernel)
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo), for the baseline lines."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
 def cpu_baseline(name: str, seconds: float = 10.0, max_images: int = 64) -> dict:
     """The reference semantics on the CPU oracle (OpenMP over all host
     cores), one image / sequence per pass, until `seconds` have elapsed."""
@@ -162,6 +174,7 @@ def cpu_baseline(name: str, seconds: float = 10.0, max_images: int = 64) -> dict
         n += 1
     dt = time.perf_counter() - t0
     return {"value": n / dt, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+            "cpu": cpu_model(),
             "sample": f"{n} single-{'sequence' if name == 'bert' else 'image'} {name} passes "
                       f"through the reference executor semantics on the C++ oracle ({dt:.1f} s)"}
 
@@ -193,8 +206,9 @@ def run_reference(args) -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded U[-1,1] input, seeded He-normal weights)",
-        "config": _config(args, world),
+        "config": _ref_config(args, world),
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+                         "cpu": cpu_model(),
                          "sample": f"{per_step} image(s) per step through the reference "
                                    "scheduler lowering (scheduler.rs semantics) on the C++ "
                                    "restatement of the reference kernels"},
@@ -220,6 +234,19 @@ def _config(args, world) -> dict:
             "batch_per_gpu": args.batch, "global_batch": args.batch * world,
             "parallelism": f"dp{world} (batch-sharded replicas, no collective)",
             "l2": l2, "cuda_graph": True}
+
+
+def _ref_config(args, world) -> dict:
+    """The reference arm's own configuration: the same model and image size,
+    but a reduced batch of --ref-images images per step, reported as a
+    per-image rate (batch 256 of the CPU path would take minutes per step)."""
+    unit = "sequences" if args.model == "bert" else "images"
+    return {"workload": f"{_WORKLOADS.get(args.model, args.model)}, reduced batch: "
+                        f"{args.ref_images} {unit} per step (batch {args.batch} impractical "
+                        f"on the CPU path), per-{unit[:-1]} rate",
+            "batch_per_step": args.ref_images, "global_batch": args.ref_images,
+            "parallelism": "host cores of rank 0 (OpenMP over outputs)",
+            "cuda_graph": False}
 
 
 def run_spx(args) -> None:
@@ -440,7 +467,7 @@ def llama_cpu_baseline(W, seconds: float) -> dict:
         step()
         n += 1
     dt = time.perf_counter() - t0
-    return {"value": n / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+    return {"value": n / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port", "cpu": cpu_model(),
             "sample": f"{n} greedy token(s) of one sequence through the reference's decode loop "
                       f"(full 64-position llama_step per token, numpy fp32 BLAS; {dt:.1f} s)"}
 
@@ -466,7 +493,7 @@ def run_llama_reference(args) -> None:
         "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded uniform prompt ids, seeded N(0,0.02) weights)",
         "config": _llama_config(args, world),
-        "cpu_baseline": {"value": v, "unit": UNIT_, "cores": os.cpu_count(), "kind": "port",
+        "cpu_baseline": {"value": v, "unit": UNIT_, "cores": os.cpu_count(), "kind": "port", "cpu": cpu_model(),
                          "sample": "1 greedy token of one sequence per step through the "
                                    "reference's decode loop (full 64-position re-computation, "
                                    "numpy fp32 BLAS)"},

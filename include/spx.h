@@ -73,6 +73,19 @@ int spx_device_count(void);
  * source/tflite_loader/src/vulkan.rs:204-231) or a decimal ordinal to a CUDA
  * ordinal.  "intel" has no CUDA device and fails with SPX_ERR_NO_DEVICE. */
 int spx_select_device(const char* selector, int* ordinal);
+/* Compute capability (major * 10 + minor) the library's device code was built
+ * for, read through cudaFuncGetAttributes on `device`: 100 for this sm_100a
+ * build.  No counterpart in the reference (a build check). */
+int spx_binary_version(int device, int* version);
+/* Device-side error status of this process's libspx kernels: SPX_OK, or
+ * SPX_ERR_CUDA with spx_last_error() naming the wait that ran out (a pipeline
+ * or peer wait past its bound).  Reading clears it.  spx_graph_sync and
+ * spx_run_kernel check it themselves; callers that enqueue on their own
+ * streams (spx_conv2d_nchw_noalloc) call it after synchronising.
+ * libspx keeps per-device state (cached buffers, the no-alloc scratch
+ * address): do not cudaDeviceReset a device while the library is in use on
+ * it. */
+int spx_device_status(void);
 
 /* Process-wide options.  "gemm_path": 0 = automatic (tensor cores where the
  * operands allow, exact-fp32 SIMT otherwise), 1 = SIMT only, 2 = tensor cores
@@ -88,6 +101,8 @@ int spx_select_device(const char* selector, int* ordinal);
  * alternate tiles; 0 = never.
  * "tc_conv_groups": 2 (default) = tensor-core GEMMs with several k-blocks per
  * tile split two stages at once (two converter groups), 1 = one at a time.
+ * "ar_wait_limit_us": bound of the peer all-reduce's wait for the other ranks
+ * (default 2,000,000; 1,000 .. 60,000,000).
  * "tc_lo_tmem": 1 = with pre-split weights and several k-blocks the
  * activations' tf32 lo terms are written to tensor memory and the lo*hi MMA
  * reads its A operand from there; 0 (default) = lo terms in shared memory. */
@@ -150,7 +165,10 @@ int spx_run_kernel(const char* kernel, const float* input0, size_t input0_len,
  * array's device address; make that first call before any stream capture.
  * All calls share the array: calls that can overlap on the GPU (other
  * streams, other host threads) race and must be serialised by the caller.
- * No cudaMalloc, cudaFree or allocating library routine is called. */
+ * No cudaMalloc, cudaFree or allocating library routine is called.
+ * pad_top / pad_left must lie in [0, kernel extent).  The call only enqueues
+ * work: a bounded pipeline wait that ran out inside it is reported by
+ * spx_device_status() once the caller has synchronised `stream`. */
 int spx_conv2d_nchw_noalloc(const float* x, const float* w, float* y, const int32_t* push,
                             size_t push_len, void* stream);
 
@@ -334,6 +352,14 @@ int spx_op_unary(spx_graph* g, int32_t op, const float* x, float* y, int64_t n, 
 #define SPX_BIN_POW 4
 #define SPX_BIN_MIN 5
 #define SPX_BIN_MAX 6
+/* HLO `compare` (compiler.rs runs it on the host): 1.0f where the relation
+ * holds, 0.0f elsewhere (NaN compares false except NE). */
+#define SPX_BIN_GT 7
+#define SPX_BIN_GE 8
+#define SPX_BIN_LT 9
+#define SPX_BIN_LE 10
+#define SPX_BIN_EQ 11
+#define SPX_BIN_NE 12
 /* y[i0,i1,i2,i3] = a[.] op b[.] over a rank-4 output with element strides
  * for a and b (0 = broadcast along that axis), replacing the reference's CPU
  * broadcast before every HLO elementwise dispatch (compiler.rs:705-729). */
@@ -344,6 +370,18 @@ typedef struct spx_bcast_params {
 } spx_bcast_params;
 int spx_op_binary(spx_graph* g, int32_t op, const float* a, const float* b, float* y,
                   const spx_bcast_params* p);
+/* HLO `select` (host-side in the reference, compiler.rs CPU ops): y = pred != 0
+ * ? a : b elementwise over the rank-4 output p->d; pred, a and b each have
+ * their own element strides (0 = broadcast).  Exact: the branch not taken is
+ * never combined arithmetically, so inf / NaN there do not leak. */
+typedef struct spx_select_params {
+  int32_t d[4];
+  int64_t p_stride[4];
+  int64_t a_stride[4];
+  int64_t b_stride[4];
+} spx_select_params;
+int spx_op_select(spx_graph* g, const float* pred, const float* a, const float* b, float* y,
+                  const spx_select_params* p);
 
 /* hlo_reduce_rank4 with the reference's 15 push constants
  * (compiler.rs:975-991): rank,d0..d3,od0..od3,r0..r3,kind,total. */
@@ -442,8 +480,12 @@ int spx_op_argmax_merge(spx_graph* g, const float* packed, int32_t parts, int32_
  * partial sum into spx_ar_slot(a, s); spx_op_allreduce sums slot s of all
  * ranks into out (out must not alias a slot).  Consecutive all-reduces must
  * alternate slots 0 / 1 and be issued in the same order on every rank.
- * Waits for peers are bounded (2 s); a timeout is reported as SPX_ERR_CUDA
- * at the next graph sync. */
+ * Waits for peers are bounded (2 s, or the "ar_wait_limit_us" option,
+ * 1 ms .. 60 s); a timeout is reported as SPX_ERR_CUDA at the next graph sync
+ * and leaves that all-reduce's output untouched.  The communicators are then
+ * out of step: every rank calls spx_ar_reset (zeroes its own flags and
+ * epochs, synchronous) between two host-side barriers before the next
+ * all-reduce. */
 typedef struct spx_ar spx_ar;
 int spx_ar_create(int32_t device, int32_t rank, int32_t world, size_t max_bytes, spx_ar** out);
 size_t spx_ar_handle_size(void);
@@ -451,6 +493,7 @@ int spx_ar_handle(spx_ar* a, void* handle, size_t handle_bytes);
 int spx_ar_open(spx_ar* a, const void* handles);
 float* spx_ar_slot(spx_ar* a, int32_t slot);
 int spx_op_allreduce(spx_graph* g, spx_ar* a, int32_t slot, float* out, int64_t n);
+int spx_ar_reset(spx_ar* a);
 int spx_ar_destroy(spx_ar* a);
 
 /* Rank-4 constant pad (pad.comp with the reference's 13 push constants

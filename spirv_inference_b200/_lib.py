@@ -27,7 +27,8 @@ POOL_SUM, POOL_MAX, POOL_AVG = 0, 1, 2
 UNARY = {"abs": 0, "exp": 1, "log": 2, "neg": 3, "sqrt": 4, "rsqrt": 5, "sigmoid": 6,
          "tanh": 7, "relu": 8, "relu6": 9, "leaky_relu": 10, "sin": 11, "copy": 12,
          "gelu_erf": 13, "silu": 14}
-BINARY = {"add": 0, "sub": 1, "mul": 2, "div": 3, "pow": 4, "min": 5, "max": 6}
+BINARY = {"add": 0, "sub": 1, "mul": 2, "div": 3, "pow": 4, "min": 5, "max": 6,
+          "gt": 7, "ge": 8, "lt": 9, "le": 10, "eq": 11, "ne": 12}
 
 
 class SpxError(RuntimeError):
@@ -82,6 +83,11 @@ class BcastParams(Structure):
     _fields_ = [("d", c_int32 * 4), ("a_stride", c_int64 * 4), ("b_stride", c_int64 * 4)]
 
 
+class SelectParams(Structure):
+    _fields_ = [("d", c_int32 * 4), ("p_stride", c_int64 * 4), ("a_stride", c_int64 * 4),
+                ("b_stride", c_int64 * 4)]
+
+
 _FP = POINTER(c_float)
 _IP = POINTER(c_int32)
 _lib = None
@@ -91,6 +97,8 @@ _SIGS = {
     "spx_version": ([], c_char_p),
     "spx_device_count": ([], c_int),
     "spx_select_device": ([c_char_p, POINTER(c_int)], c_int),
+    "spx_binary_version": ([c_int, POINTER(c_int)], c_int),
+    "spx_device_status": ([], c_int),
     "spx_set_option": ([c_char_p, c_int64], c_int),
     "spx_get_option": ([c_char_p], c_int64),
     "spx_gemm_tc_plan": ([c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p,
@@ -136,6 +144,8 @@ _SIGS = {
     "spx_op_unary": ([c_void_p, c_int32, c_void_p, c_void_p, c_int64, c_float], c_int),
     "spx_op_binary": ([c_void_p, c_int32, c_void_p, c_void_p, c_void_p, POINTER(BcastParams)],
                       c_int),
+    "spx_op_select": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, POINTER(SelectParams)],
+                      c_int),
     "spx_op_reduce_rank4": ([c_void_p, c_void_p, c_void_p, _IP], c_int),
     "spx_op_layernorm": ([c_void_p] + [c_void_p] * 6 + [c_int32, c_int32, c_float], c_int),
     "spx_op_rmsnorm": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float],
@@ -164,6 +174,7 @@ _SIGS = {
     "spx_ar_open": ([c_void_p, c_void_p], c_int),
     "spx_ar_slot": ([c_void_p, c_int32], c_void_p),
     "spx_op_allreduce": ([c_void_p, c_void_p, c_int32, c_void_p, c_int64], c_int),
+    "spx_ar_reset": ([c_void_p], c_int),
     "spx_ar_destroy": ([c_void_p], c_int),
     "spx_op_expand_dw_nhwc": ([c_void_p] + [c_void_p] * 6 + [POINTER(ExpandDwParams)], c_int),
     "spx_op_expand_dw_nhwc_split": ([c_void_p] + [c_void_p] * 8 + [POINTER(ExpandDwParams)],

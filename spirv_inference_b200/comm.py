@@ -19,10 +19,21 @@ from ._lib import check
 from .graph import DeviceTensor, Graph
 
 
+def _all_gather_bytes(mine: bytes, device: int, world: int, group) -> bytes:
+    import torch
+    import torch.distributed as dist
+    dev = torch.device("cuda", device)
+    t = torch.tensor(np.frombuffer(mine, np.uint8).copy(), device=dev)
+    every = torch.empty(world * len(mine), dtype=torch.uint8, device=dev)
+    dist.all_gather_into_tensor(every, t, group=group)
+    return every.cpu().numpy().tobytes()
+
+
 class PeerAllReduce:
-    def __init__(self, device: int, rank: int, world: int, max_bytes: int, group=None):
-        import torch
-        import torch.distributed as dist
+    def __init__(self, device: int, rank: int, world: int, max_bytes: int, group=None,
+                 exchange=None):
+        """`exchange(mine: bytes) -> bytes` returns every rank's handle in rank
+        order; by default an all-gather over torch.distributed (`group`)."""
         self._l = _lib.lib()
         self.rank, self.world = rank, world
         self.max_bytes = int((max_bytes + 15) // 16 * 16)
@@ -32,11 +43,12 @@ class PeerAllReduce:
         hs = int(self._l.spx_ar_handle_size())
         buf = (ctypes.c_char * hs)()
         check(self._l.spx_ar_handle(h, buf, hs))
-        dev = torch.device("cuda", device)
-        mine = torch.tensor(np.frombuffer(bytes(buf), np.uint8).copy(), device=dev)
-        every = torch.empty(world * hs, dtype=torch.uint8, device=dev)
-        dist.all_gather_into_tensor(every, mine, group=group)
-        handles = every.cpu().numpy().tobytes()
+        if exchange is None:
+            exchange = lambda mine: _all_gather_bytes(mine, device, world, group)  # noqa: E731
+        handles = exchange(bytes(buf))
+        if len(handles) != world * hs:
+            raise ValueError(f"handle exchange returned {len(handles)} bytes, "
+                             f"expected {world} x {hs}")
         check(self._l.spx_ar_open(h, handles))
         self.slots = [int(self._l.spx_ar_slot(h, s)) for s in (0, 1)]
 
@@ -45,6 +57,11 @@ class PeerAllReduce:
 
     def allreduce(self, graph: Graph, slot: int, out: DeviceTensor, n: int) -> None:
         check(self._l.spx_op_allreduce(graph.h, self.h, slot, ctypes.c_void_p(out.ptr), n))
+
+    def reset(self) -> None:
+        """Zeroes this rank's flags and epochs after a timed-out all-reduce;
+        every rank calls it between two barriers."""
+        check(self._l.spx_ar_reset(self.h))
 
     def close(self) -> None:
         if self.h:

@@ -11,8 +11,9 @@
 //   2. publishes it to flags[cta][my rank] of every peer (release, system
 //      scope, after a system fence that orders the partial sums),
 //   3. waits until every peer's epoch for this CTA has reached its own
-//      (acquire loads; bounded by a 2 s %globaltimer limit, after which it
-//      records an error status and returns),
+//      (acquire loads; bounded by a %globaltimer limit, 2 s unless the
+//      "ar_wait_limit_us" option says otherwise, after which it records an
+//      error status and returns without touching the output),
 //   4. sums its slice of slot s over all ranks with plain loads from the
 //      peers' memory into the local output.
 // Consecutive all-reduces must alternate the two slots: a rank rewrites slot
@@ -45,7 +46,6 @@ constexpr int kArMaxCtas = 32;
 constexpr int kArMaxRanks = 8;
 constexpr size_t kFlagBytes = (size_t)kArMaxCtas * kArMaxRanks * 8;
 constexpr size_t kEpochBytes = (size_t)kArMaxCtas * 8;
-constexpr unsigned long long kArTimeoutNs = 2000000000ull;
 
 __device__ __forceinline__ unsigned long long ar_now() {
   unsigned long long t;
@@ -65,7 +65,7 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
 __global__ void __launch_bounds__(512) allreduce_kernel(
     float* const* __restrict__ peers, unsigned long long* const* __restrict__ flags,
     unsigned long long* __restrict__ epochs, int rank, int world, int64_t slot_off, float* out,
-    int64_t n4) {
+    int64_t n4, unsigned long long limit_ns) {
   __shared__ int s_ok;
   const int cta = blockIdx.x;
   if (threadIdx.x == 0) {
@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(512) allreduce_kernel(
     for (int r = 0; r < world && ok; ++r) {
       const unsigned long long* f = flags[rank] + cta * kArMaxRanks + r;
       while (ld_acquire_sys(f) < e) {
-        if (ar_now() - t0 > kArTimeoutNs) {
+        if (ar_now() - t0 > limit_ns) {
           atomicExch(&g_ar_status, 1);
           ok = 0;
           break;
@@ -232,8 +232,19 @@ int spx_op_allreduce(spx_graph* g, spx_ar* a, int32_t slot, float* out, int64_t 
       (unsigned long long*)(a->base + 2 * a->max_bytes + kFlagBytes);
   allreduce_kernel<<<ctas, 512, 0, g->stream>>>(a->d_peers, a->d_flags, epochs, a->rank,
                                                  a->world, (int64_t)slot * (int64_t)(a->max_bytes / 4),
-                                                 out, n4);
+                                                 out, n4,
+                                                 (unsigned long long)g_ar_wait_limit_us * 1000ull);
   return after_launch(&g->launches, "allreduce");
+}
+
+int spx_ar_reset(spx_ar* a) {
+  if (!a) return fail(SPX_ERR_INVALID_ARGUMENT, "ar_reset: null");
+  int rc = check_cuda(cudaSetDevice(a->device), "ar_reset: cudaSetDevice");
+  if (!rc)
+    rc = check_cuda(cudaMemset(a->base + 2 * a->max_bytes, 0, kFlagBytes + kEpochBytes),
+                    "ar_reset: cudaMemset");
+  if (!rc) rc = check_cuda(cudaDeviceSynchronize(), "ar_reset: sync");
+  return rc;
 }
 
 int spx_ar_destroy(spx_ar* a) {

@@ -70,7 +70,13 @@ __device__ __forceinline__ float binary_op(int op, float a, float b) {
     case SPX_BIN_DIV: return a / b;
     case SPX_BIN_POW: return powf(a, b);
     case SPX_BIN_MIN: return fminf(a, b);
-    default: return fmaxf(a, b);  // SPX_BIN_MAX
+    case SPX_BIN_MAX: return fmaxf(a, b);
+    case SPX_BIN_GT: return a > b ? 1.0f : 0.0f;
+    case SPX_BIN_GE: return a >= b ? 1.0f : 0.0f;
+    case SPX_BIN_LT: return a < b ? 1.0f : 0.0f;
+    case SPX_BIN_LE: return a <= b ? 1.0f : 0.0f;
+    case SPX_BIN_EQ: return a == b ? 1.0f : 0.0f;
+    default: return a != b ? 1.0f : 0.0f;  // SPX_BIN_NE
   }
 }
 
@@ -101,6 +107,28 @@ __global__ void binary_bcast(int op, const float* __restrict__ a, const float* _
     int64_t ia = c0 * p.as[0] + c1 * p.as[1] + c2 * p.as[2] + c3 * p.as[3];
     int64_t ib = c0 * p.bs[0] + c1 * p.bs[1] + c2 * p.bs[2] + c3 * p.bs[3];
     y[i] = binary_op(op, a[ia], b[ib]);
+  }
+}
+
+struct Sel {
+  int32_t d[4];
+  int64_t ps[4], as[4], bs[4];
+};
+
+__global__ void select_kernel(const float* __restrict__ pr, const float* __restrict__ a,
+                              const float* __restrict__ b, float* __restrict__ y, Sel p,
+                              int64_t n) {
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    int64_t t = i;
+    int64_t c3 = t % p.d[3]; t /= p.d[3];
+    int64_t c2 = t % p.d[2]; t /= p.d[2];
+    int64_t c1 = t % p.d[1]; t /= p.d[1];
+    int64_t c0 = t;
+    int64_t ip = c0 * p.ps[0] + c1 * p.ps[1] + c2 * p.ps[2] + c3 * p.ps[3];
+    int64_t ia = c0 * p.as[0] + c1 * p.as[1] + c2 * p.as[2] + c3 * p.as[3];
+    int64_t ib = c0 * p.bs[0] + c1 * p.bs[1] + c2 * p.bs[2] + c3 * p.bs[3];
+    y[i] = pr[ip] != 0.0f ? a[ia] : b[ib];
   }
 }
 
@@ -194,7 +222,7 @@ int launch_unary(cudaStream_t s, int64_t* cnt, int op, const float* x, float* y,
 
 int launch_binary(cudaStream_t s, int64_t* cnt, int op, const float* a, const float* b,
                   float* y, const spx_bcast_params* p) {
-  if (op < 0 || op > SPX_BIN_MAX) return fail(SPX_ERR_UNSUPPORTED, "binary op %d unknown", op);
+  if (op < 0 || op > SPX_BIN_NE) return fail(SPX_ERR_UNSUPPORTED, "binary op %d unknown", op);
   int64_t n = 1;
   for (int i = 0; i < 4; ++i) {
     if (p->d[i] < 0) return fail(SPX_ERR_INVALID_ARGUMENT, "binary: negative dim");
@@ -219,6 +247,23 @@ int launch_binary(cudaStream_t s, int64_t* cnt, int op, const float* a, const fl
     binary_bcast<<<grid_for(n, 256), 256, 0, s>>>(op, a, b, y, q, n);
   }
   return after_launch(cnt, "binary");
+}
+
+int launch_select(cudaStream_t s, int64_t* cnt, const float* pr, const float* a, const float* b,
+                  float* y, const spx_select_params* p) {
+  int64_t n = 1;
+  Sel q;
+  for (int i = 0; i < 4; ++i) {
+    if (p->d[i] < 0) return fail(SPX_ERR_INVALID_ARGUMENT, "select: negative dim");
+    n *= p->d[i];
+    q.d[i] = p->d[i] > 0 ? p->d[i] : 1;
+    q.ps[i] = p->p_stride[i];
+    q.as[i] = p->a_stride[i];
+    q.bs[i] = p->b_stride[i];
+  }
+  if (n == 0) return SPX_OK;
+  select_kernel<<<grid_for(n, 256), 256, 0, s>>>(pr, a, b, y, q, n);
+  return after_launch(cnt, "select");
 }
 
 int launch_swiglu(cudaStream_t s, int64_t* cnt, const float* gate, const float* up, float* y,
@@ -281,3 +326,19 @@ int launch_embedding(cudaStream_t s, int64_t* cnt, const float* table, const int
 }
 
 }  // namespace spx
+
+// Compute capability the loaded device code was compiled for (major * 10 +
+// minor, from cudaFuncGetAttributes on one of the library's kernels): 100 for
+// the sm_100a build.  Lets a test confirm the architecture without any binary
+// tool.
+extern "C" int spx_binary_version(int device, int* version) {
+  using namespace spx;
+  if (!version) return fail(SPX_ERR_INVALID_ARGUMENT, "binary_version: null version");
+  int rc;
+  if ((rc = check_cuda(cudaSetDevice(device), "cudaSetDevice"))) return rc;
+  cudaFuncAttributes a{};
+  if ((rc = check_cuda(cudaFuncGetAttributes(&a, unary_kernel), "cudaFuncGetAttributes")))
+    return rc;
+  *version = a.binaryVersion;
+  return SPX_OK;
+}

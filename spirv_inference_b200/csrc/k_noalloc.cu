@@ -67,6 +67,15 @@ extern "C" int spx_conv2d_nchw_noalloc(const float* x, const float* w, float* y,
     if (q[i] <= 0) return fail(SPX_ERR_INVALID_ARGUMENT, "conv2d_noalloc: push[%d] <= 0", i);
   const int N = q[0], IC = q[1], IH = q[2], IW = q[3], OC = q[4], OH = q[5], OW = q[6],
             KH = q[7], KW = q[8];
+  const int PT = q[12], PL = q[13];
+  if (PT < 0 || PT >= KH || PL < 0 || PL >= KW)
+    return fail(SPX_ERR_INVALID_ARGUMENT,
+                "conv2d_noalloc: pad_top %d / pad_left %d outside [0, kernel extent %d x %d)", PT,
+                PL, KH, KW);
+  if ((int64_t)(OH - 1) * q[9] - PT >= IH || (int64_t)(OW - 1) * q[10] - PL >= IW)
+    return fail(SPX_ERR_INVALID_ARGUMENT,
+                "conv2d_noalloc: output %d x %d with stride %d x %d and pads %d, %d reads past "
+                "the %d x %d input", OH, OW, q[9], q[10], PT, PL, IH, IW);
   const int64_t in_el = (int64_t)N * IC * IH * IW, w_el = (int64_t)OC * IC * KH * KW;
   const int64_t total = (int64_t)N * OC * OH * OW;
   if (total != q[14])
@@ -94,7 +103,7 @@ extern "C" int spx_conv2d_nchw_noalloc(const float* x, const float* w, float* y,
   int32_t t_out[13] = {N, OH, OW, OC, N, OC, OH, OW, 0, 3, 1, 2, (int32_t)total};
   if ((rc = launch_transpose4(s, nullptr, x, x_nhwc, t_in))) return rc;
   if ((rc = launch_transpose4(s, nullptr, w, w_ohwi, t_w))) return rc;
-  spx_conv_params p = {N, IH, IW, IC, OC, OH, OW, KH, KW, q[9], q[10], q[12], q[13], 1, 1,
+  spx_conv_params p = {N, IH, IW, IC, OC, OH, OW, KH, KW, q[9], q[10], PT, PL, 1, 1,
                        SPX_WEIGHT_OHWI, SPX_ACT_NONE};
   if ((rc = launch_conv_nhwc(s, nullptr, x_nhwc, w_ohwi, nullptr, nullptr, w + w_el, nullptr,
                              y_nhwc, &p)))

@@ -41,6 +41,7 @@ int after_launch(int64_t* counter, const char* what) {
 }
 
 int g_gemm_path = 0;
+int64_t g_ar_wait_limit_us = 2000000;
 int g_dw_path = 0;
 int g_pw_path = 0;
 
@@ -486,6 +487,12 @@ int spx_set_option(const char* name, int64_t value) {
     g_pw_path = (int)value;
     return SPX_OK;
   }
+  if (n == "ar_wait_limit_us") {
+    if (value < 1000 || value > 60000000)
+      return fail(SPX_ERR_INVALID_ARGUMENT, "ar_wait_limit_us must be 1000..60000000");
+    g_ar_wait_limit_us = value;
+    return SPX_OK;
+  }
   if (n == "gemm_path") {
     if (value < 0 || value > 2) return fail(SPX_ERR_INVALID_ARGUMENT, "gemm_path must be 0..2");
     g_gemm_path = (int)value;
@@ -502,6 +509,7 @@ int64_t spx_get_option(const char* name) {
   if (n == "tc_wide_epilogue") return g_tc_epi12;
   if (n == "tc_conv_groups") return g_tc_conv2 ? 2 : 1;
   if (n == "tc_lo_tmem") return g_tc_lo_tmem;
+  if (n == "ar_wait_limit_us") return g_ar_wait_limit_us;
   return -1;
 }
 
@@ -512,9 +520,14 @@ static int device_status(const char* what) {
     return fail(SPX_ERR_CUDA, "%s: a tensor-core pipeline wait timed out; tiles were abandoned",
                 what);
   if (ar_take_status())
-    return fail(SPX_ERR_CUDA, "%s: an all-reduce waited 2 s for a peer rank and gave up", what);
+    return fail(SPX_ERR_CUDA,
+                "%s: an all-reduce waited %lld us for a peer rank and gave up; reset the "
+                "communicator on every rank (spx_ar_reset) before its next use",
+                what, (long long)g_ar_wait_limit_us);
   return SPX_OK;
 }
+
+int spx_device_status(void) { return device_status("device status"); }
 
 int spx_kernel_count(void) { return kNumKernels; }
 const char* spx_kernel_name(int i) { return i >= 0 && i < kNumKernels ? kKernels[i].name : nullptr; }
@@ -825,6 +838,13 @@ int spx_op_binary(spx_graph* g, int32_t op, const float* a, const float* b, floa
   SPX_G(g);
   if (!a || !b || !y || !p) return fail(SPX_ERR_INVALID_ARGUMENT, "binary: null argument");
   return launch_binary(g->stream, &g->launches, op, a, b, y, p);
+}
+
+int spx_op_select(spx_graph* g, const float* pred, const float* a, const float* b, float* y,
+                  const spx_select_params* p) {
+  SPX_G(g);
+  if (!pred || !a || !b || !y || !p) return fail(SPX_ERR_INVALID_ARGUMENT, "select: null argument");
+  return launch_select(g->stream, &g->launches, pred, a, b, y, p);
 }
 
 int spx_op_reduce_rank4(spx_graph* g, const float* x, float* y, const int32_t push[15]) {

@@ -113,6 +113,8 @@ int launch_unary(cudaStream_t s, int64_t* cnt, int op, const float* x, float* y,
                  float alpha);
 int launch_binary(cudaStream_t s, int64_t* cnt, int op, const float* a, const float* b,
                   float* y, const spx_bcast_params* p);
+int launch_select(cudaStream_t s, int64_t* cnt, const float* pr, const float* a, const float* b,
+                  float* y, const spx_select_params* p);
 // w_hi / w_lo (both or neither): the weights pre-split by launch_weights_split,
 // used when the tensor-core path runs; w itself feeds every other path.
 int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
@@ -237,6 +239,8 @@ int ar_take_status();
 // Process-wide dense-contraction path: 0 auto, 1 SIMT only, 2 tensor cores
 // required (ineligible shapes fail with SPX_ERR_UNSUPPORTED).
 extern int g_gemm_path;
+// Bound of the peer all-reduce's wait for the other ranks, microseconds.
+extern int64_t g_ar_wait_limit_us;
 extern int g_tc_epi12;
 extern int g_tc_conv2;
 extern int g_tc_lo_tmem;

@@ -605,6 +605,32 @@ class HloExecutor:
                 return
         self._elementwise(op, "mul")
     def _op_divide(self, op): self._elementwise(op, "div")
+
+    _CMP = {"GT": "gt", "GE": "ge", "LT": "lt", "LE": "le", "EQ": "eq", "NE": "ne"}
+
+    def _op_compare(self, op):
+        # a 0 / 1 float mask; the reference evaluates compare on the host
+        self._elementwise(op, self._CMP[op.attrs.get("direction", "GT")])
+
+    def _op_select(self, op):
+        views = [self.v[o] for o in op.operands]
+        out = self._new(op.shape)
+        r = len(op.shape)
+        ops_ = []
+        for v in views:
+            t, st = self._operand(v)
+            ops_.append((t, [0] * r if st is None else list(st)))
+        d, strides = self._pad4(op.shape, *(st for _, st in ops_))
+        self.plan.append(("select", ops_[0][0], ops_[1][0], ops_[2][0], out.t, d, *strides))
+        self._set(op.name, out)
+
+    def _op_tuple(self, op):
+        self._set(op.name, self.v[op.operands[0]])
+
+    def _op_get_tuple_element(self, op):
+        if op.attrs.get("index", 0) != 0:
+            raise NotImplementedError("get-tuple-element of a tuple element other than 0")
+        self._set(op.name, self.v[op.operands[0]])
     def _op_maximum(self, op): self._elementwise(op, "max")
     def _op_minimum(self, op): self._elementwise(op, "min")
     def _op_power(self, op): self._elementwise(op, "pow")
@@ -634,6 +660,9 @@ class HloExecutor:
                 g.binary(opn, ta, tb, ty, d, sa, sb)
             elif k == "unary":
                 g.unary(step[1], step[2], step[3])
+            elif k == "select":
+                _, tp, ta, tb, ty, d, sp, sa, sb = step
+                g.select(tp, ta, tb, ty, d, sp, sa, sb)
             elif k == "conv":
                 p = step[1]
                 g.conv2d_nhwc(p["x"], p["w"], p["bias"], p["y"], stride=p["stride"], pad=p["pad"],

@@ -234,6 +234,12 @@ class Graph:
         check(self._l.spx_op_binary(self.h, _lib.BINARY[op], self._p(a), self._p(b), self._p(y),
                                     ctypes.byref(p)))
 
+    def select(self, pred, a, b, y, dims, p_strides, a_strides, b_strides):
+        p = _lib.SelectParams((ctypes.c_int32 * 4)(*dims), (ctypes.c_int64 * 4)(*p_strides),
+                              (ctypes.c_int64 * 4)(*a_strides), (ctypes.c_int64 * 4)(*b_strides))
+        check(self._l.spx_op_select(self.h, self._p(pred), self._p(a), self._p(b), self._p(y),
+                                    ctypes.byref(p)))
+
     def add(self, a, b, y):
         n = y.size
         self.binary("add", a, b, y, (1, 1, 1, n), (0, 0, 0, 1), (0, 0, 0, 1))

@@ -12,6 +12,7 @@ Run from the repository root in a checkout that has the reference mounted:
     python tests/golden/make_golden.py /path/to/SPIRV_INFERENCE
 """
 import hashlib
+import os
 import json
 import shutil
 import subprocess
@@ -40,4 +41,7 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SPX_REFERENCE_ROOT")
+    if not root:
+        raise SystemExit("usage: make_golden.py <reference root> (or set SPX_REFERENCE_ROOT)")
+    main(root)

@@ -42,6 +42,14 @@ def test_kernel_output_info(gpu):
     assert r.elapsed_ms >= 0.0
 
 
+def test_loaded_code_is_sm100(gpu):
+    import ctypes
+    from spirv_inference_b200 import _lib
+    v = ctypes.c_int(0)
+    assert _lib.lib().spx_binary_version(gpu, ctypes.byref(v)) == 0, _lib.lib().spx_last_error()
+    assert v.value == 100
+
+
 RNG = np.random.default_rng(11)
 
 

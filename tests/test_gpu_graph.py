@@ -229,6 +229,33 @@ def test_binary_broadcast_and_unary(g):
     np.testing.assert_allclose(du.download(), ref, rtol=1e-5, atol=1e-6)
 
 
+def test_compare_and_select(g):
+    a = _r(2, 3, 4, 5)
+    b = _r(1, 3, 1, 5)
+    a[0, 0, 0, :2] = b[0, 0, 0, :2]                 # equal entries
+    da, db = g.tensor(a), g.tensor(b)
+    st_a, st_b = (60, 20, 5, 1), (0, 5, 0, 1)
+    bb = np.broadcast_to(b, a.shape)
+    for op, f in (("gt", np.greater), ("ge", np.greater_equal), ("lt", np.less),
+                  ("le", np.less_equal), ("eq", np.equal), ("ne", np.not_equal)):
+        dy = g.alloc(a.shape)
+        g.binary(op, da, db, dy, a.shape, st_a, st_b)
+        np.testing.assert_array_equal(dy.download(), f(a, bb).astype(np.float32))
+    # select never mixes the branches: inf / nan in the branch not taken stay out
+    t = a.copy()
+    t[0, 1, 2, 3] = np.inf
+    e = _r(2, 3, 4, 5)
+    e[1, 2, 3, 4] = np.nan
+    pred = (a > 0).astype(np.float32)
+    dp, dt, de, dy = g.tensor(pred), g.tensor(t), g.tensor(e), g.alloc(a.shape)
+    g.select(dp, dt, de, dy, a.shape, st_a, st_a, st_a)
+    np.testing.assert_array_equal(dy.download(), np.where(pred != 0, t, e))
+    # broadcast predicate and scalar branch
+    dz = g.alloc(a.shape)
+    g.select(db, dt, g.tensor(np.array([5.0], np.float32)), dz, a.shape, st_b, st_a, (0, 0, 0, 0))
+    np.testing.assert_array_equal(dz.download(), np.where(bb != 0, t, np.float32(5.0)))
+
+
 def test_cuda_graph_capture_and_launch_count(g):
     x = _r(2, 8, 8, 16)
     dx, dy, dz = g.tensor(x), g.alloc((2, 8, 8, 16)), g.alloc((2, 8, 8, 16))
