@@ -246,6 +246,27 @@ typedef struct spx_dw_params {
 int spx_op_depthwise_conv2d_nhwc(spx_graph* g, const float* x, const float* w,
                                  const float* bias, float* y, const spx_dw_params* p);
 
+/* Fused back half of an inverted-residual block: 3x3 depthwise conv (stride
+ * 1 or 2, bias b_dw, activation act_dw) followed by the 1x1 projection to
+ * `cout` channels (pre-split tf32 hi / lo weights [cout][c] from
+ * spx_weights_split, bias b_proj, activation act_proj) and, when `residual`
+ * is non-null, the residual add; the depthwise output stays on chip.
+ * Replaces the DepthwiseConv2d + Conv2d (+ Add) dispatches of
+ * source/tflite_loader/src/scheduler.rs:321-548 and :144-211.  x is NHWC
+ * [n][ih][iw][c], w_dw [3][3][c], y and residual NHWC [n][oh][ow][cout].
+ * c and cout must be multiples of 4, cout <= 512, every tensor 16-byte
+ * aligned; other shapes fail with SPX_ERR_UNSUPPORTED (nothing launched). */
+typedef struct spx_dwproj_params {
+  int32_t n, ih, iw, c, oh, ow;
+  int32_t kernel, stride, pad_top, pad_left;
+  int32_t act_dw, cout, act_proj;
+} spx_dwproj_params;
+int spx_op_dw_project_nhwc(spx_graph* g, const float* x, const float* w_dw, const float* b_dw,
+                           const float* w_proj_hi, const float* w_proj_lo, const float* b_proj,
+                           const float* residual, float* y, const spx_dwproj_params* p);
+/* 1 when spx_op_dw_project_nhwc takes this shape, 0 otherwise (no device work). */
+int spx_dw_project_supported(const spx_dwproj_params* p);
+
 /* Fused MobileNet block front half (no counterpart op in the reference,
  * which dispatches conv2d.comp then depthwise_conv2d.comp with the expanded
  * tensor in memory between them, scheduler.rs:321-548):

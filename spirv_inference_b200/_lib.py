@@ -68,6 +68,11 @@ class ExpandDwParams(Structure):
                                        "pad_top", "pad_left", "act_expand", "act_dw")]
 
 
+class DwProjParams(Structure):
+    _fields_ = [(n, c_int32) for n in ("n", "ih", "iw", "c", "oh", "ow", "kernel", "stride",
+                                       "pad_top", "pad_left", "act_dw", "cout", "act_proj")]
+
+
 class KvParams(Structure):
     _fields_ = [(n, c_int32) for n in ("batch", "q_len", "q_heads", "kv_heads", "head_dim",
                                        "max_seq")]
@@ -176,6 +181,8 @@ _SIGS = {
     "spx_op_allreduce": ([c_void_p, c_void_p, c_int32, c_void_p, c_int64], c_int),
     "spx_ar_reset": ([c_void_p], c_int),
     "spx_ar_destroy": ([c_void_p], c_int),
+    "spx_op_dw_project_nhwc": ([c_void_p] + [c_void_p] * 8 + [POINTER(DwProjParams)], c_int),
+    "spx_dw_project_supported": ([POINTER(DwProjParams)], c_int),
     "spx_op_expand_dw_nhwc": ([c_void_p] + [c_void_p] * 6 + [POINTER(ExpandDwParams)], c_int),
     "spx_op_expand_dw_nhwc_split": ([c_void_p] + [c_void_p] * 8 + [POINTER(ExpandDwParams)],
                                     c_int),

@@ -1,0 +1,677 @@
+// Fused depthwise 3x3 -> pointwise projection (the back half of an inverted
+// residual block: depthwise_conv2d.comp followed by the 1x1 conv2d.comp
+// projection and, where the block has one, the residual add.comp), with the
+// depthwise output never leaving the SM.
+//
+// Reference ops fused: the DepthwiseConv2d and Conv2d lowerings and the Add
+// of source/tflite_loader/src/scheduler.rs:321-548 and :144-211, each a
+// separate dispatch with a full HBM round trip of the 6x-expanded tensor.
+//
+// A persistent CTA (one per SM) walks output tiles of TH x TW pixels of one
+// image (128 GEMM rows) and, for each, every 32-channel block of the
+// depthwise width (the GEMM's K):
+//   warp 16     TMA producer: per K block the pre-split projection weights
+//               (hi and lo, NP x 32, 128-byte swizzle) into one of two
+//               stages, and per CB-channel sub-block the input halo box
+//               ((TH-1)*S+3) x ((TW-1)*S+3) x CB into a ring (the tensor map's
+//               zero fill is the depthwise padding);
+//   warps 0-15  builders: the depthwise conv of the sub-block on CUDA cores
+//               (exact fp32 FMAs, bias and activation fused; a thread owns 2
+//               channels of R rows in one column and reads each input row of
+//               its window once), written straight into the stage's A tile in
+//               the UMMA K-major 128-byte-swizzled layout: the raw value (the
+//               MMA's tf32 hi) and its tf32 lo term.  The depthwise taps and
+//               bias of the sub-block arrive in the same halo slot (TMA).
+//               Each builder warp hands a slot back after its lanes' reads
+//               (__syncwarp, then one elected proxy fence + arrive), so the
+//               TMA refill cannot overtake a slow lane;
+//   warp 17     MMA issuer: 3xTF32 (lo*hi + hi*lo + hi*hi) tcgen05.mma into one
+//               of two TMEM accumulators (NP columns each), a commit per K
+//               block frees the stage, a commit per tile hands the
+//               accumulator to the epilogue;
+//   warps 18-21 epilogue: TMEM lane quarter -> registers -> padded shared tile
+//               -> projection bias, residual, activation -> whole 128-byte
+//               channel runs of the NHWC output.
+// HBM traffic per tile: the halo (interior read once; the overlap between
+// neighbouring tiles mostly hits L2), the output, and the residual.
+//
+// Every wait is bounded (globaltimer, 2 s); on timeout the CTA raises an
+// abort flag, records a device status, drains its own copies and MMAs, frees
+// TMEM and exits.  The host reads the status at the next sync.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "sm100_prims.cuh"
+#include "spx_internal.cuh"
+
+namespace spx {
+
+__device__ int g_dwp_status = 0;
+
+#ifdef SPX_DWP_TRACE
+// Development-only timeline of CTA 0 (not compiled into the library).
+__device__ unsigned long long g_dwp_trace[12][256];
+#define DWP_TRACE(ev, i)                                                         \
+  do {                                                                           \
+    if (blockIdx.x == 0 && (i) < 256) g_dwp_trace[ev][i] = sm100::gtime();      \
+  } while (0)
+#else
+#define DWP_TRACE(ev, i) \
+  do {                   \
+  } while (0)
+#endif
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kBuildWarps = 16;
+constexpr int kProdWarp = 16;
+constexpr int kMmaWarp = 17;
+constexpr int kEpiWarp0 = 18;
+constexpr int kThreads = 22 * 32;
+constexpr int kEpiStride = 36;                  // floats per row of an epilogue tile
+constexpr uint32_t kEpiTileBytes = 32 * kEpiStride * 4;
+constexpr uint32_t kAHalf = 128 * 32 * 4;        // one 128 x 32 fp32 A tile: 16 KB
+constexpr unsigned long long kWaitNs = 2000000000ull;
+constexpr unsigned long long kDrainNs = 200000000ull;
+constexpr int kMaxHalo = 4;
+
+struct DwpArgs {
+  int n, ih, iw, ce, oh, ow, cout, np, n_ntiles, pt, pl, tiles_h, tiles_w, kblocks, total;
+  int hst;                 // halo ring depth
+  uint32_t halo_buf;       // bytes per halo slot (1024-aligned)
+  uint32_t stage_bytes;    // A raw | A lo | B hi | B lo
+  uint32_t b_bytes;        // NP x 128
+  uint32_t idesc, tmem_cols;
+  const float* wd;         // depthwise weights [3][3][ce]
+  const float* bd;         // depthwise bias [ce] or null
+  int act_d;
+  const float* bp;         // projection bias [cout] or null
+  const float* res;        // residual [n][oh][ow][cout] or null
+  float* y;                // output [n][oh][ow][cout]
+  int act_p;
+};
+
+template <int KS, int S, int TH, int TW, int CB, int R>
+__global__ void __launch_bounds__(kThreads, 1)
+    dwproj_kernel(const __grid_constant__ CUtensorMap tmX,
+                  const __grid_constant__ CUtensorMap tmBhi,
+                  const __grid_constant__ CUtensorMap tmBlo,
+                  const __grid_constant__ CUtensorMap tmWd,
+                  const __grid_constant__ CUtensorMap tmBd, const DwpArgs p) {
+  constexpr int IH = (TH - 1) * S + KS, IW = (TW - 1) * S + KS;
+  constexpr int CG = CB / 2;  // channel pairs per sub-block
+  constexpr int SUBS = 32 / CB;
+  constexpr uint32_t kHaloBytes = IH * IW * CB * 4;
+  // A halo slot: the input box, then the sub-block's depthwise taps [KS*KS][CB]
+  // and its bias [CB] (TMA boxes of the weight tensors; zero past c).
+  constexpr uint32_t kWOff = (kHaloBytes + 127) / 128 * 128;
+  constexpr uint32_t kWBytes = KS * KS * CB * 4;
+  constexpr uint32_t kBOff = kWOff + (kWBytes + 127) / 128 * 128;  // TMA: 128-byte aligned
+  const uint32_t slot_tx = kHaloBytes + kWBytes + (p.bd ? CB * 4 : 0);
+  static_assert(CG * TW * (TH / R) == kBuildWarps * 32, "one builder thread per (rows, col, pair)");
+  static_assert(TH * TW <= 128, "a tile is at most 128 GEMM rows");
+  static_assert(TH % R == 0 && 32 % CB == 0, "tile shape");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* halo = smem;
+  uint8_t* stages = halo + (size_t)p.hst * p.halo_buf;
+  float* epi = (float*)(stages + 2 * (size_t)p.stage_bytes);
+  uint64_t* hfull = (uint64_t*)((uint8_t*)epi + 4 * kEpiTileBytes);
+  uint64_t* hempty = hfull + kMaxHalo;
+  uint64_t* afull = hempty + kMaxHalo;
+  uint64_t* bfull = afull + 2;
+  uint64_t* empty = bfull + 2;
+  uint64_t* tfull = empty + 2;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int h = 0; h < p.hst; ++h) {
+      mb_init(&hfull[h], 1);
+      mb_init(&hempty[h], kBuildWarps);
+    }
+    for (int j = 0; j < 2; ++j) {
+      mb_init(&afull[j], kBuildWarps);
+      mb_init(&bfull[j], 1);
+      mb_init(&empty[j], 1);
+      mb_init(&tfull[j], 1);
+      mb_init(&tempty[j], 4 * 32);
+    }
+    mb_init(drain, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     sa(tmem_slot)),
+                 "r"(p.tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_before();
+  __syncthreads();
+  tc_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto decode = [&](int t, int& nt, int& img, int& ty, int& tx) {
+    nt = t % p.n_ntiles;
+    int r = t / p.n_ntiles;
+    tx = r % p.tiles_w;
+    r /= p.tiles_w;
+    ty = r % p.tiles_h;
+    img = r / p.tiles_h;
+  };
+
+  if (warp == kProdWarp) {
+    // ---------------- TMA producers ----------------
+    // Lane 0 streams the halo slots (input box + depthwise taps + bias) as far
+    // ahead as the ring allows; lane 1 streams the projection weights into
+    // the A/B stages as they free up.  Independent lanes, so a stage still
+    // under the MMA never holds back the next halo prefetch.
+    if (lane == 0) {
+      int h = 0;
+      uint32_t hph = 0, h_armed = 0, h_par = 0;
+      for (int t = blockIdx.x; t < p.total; t += gridDim.x) {
+        int nt, img, ty, tx;
+        decode(t, nt, img, ty, tx);
+        const int x0 = tx * TW * S - p.pl, y0 = ty * TH * S - p.pt;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          for (int sub = 0; sub < SUBS; ++sub) {
+            if (!mb_wait(&hempty[h], hph ^ 1, abort_flag, &g_dwp_status, kWaitNs, 64))
+              goto halo_done;
+            if (sub == 0) DWP_TRACE(0, ((t - (int)blockIdx.x) / (int)gridDim.x) * p.kblocks + kb);
+            uint8_t* slot = halo + (size_t)h * p.halo_buf;
+            const int c0 = kb * 32 + sub * CB;
+            mb_expect_tx(&hfull[h], slot_tx);
+            tma_4d(slot, &tmX, &hfull[h], c0, x0, y0, img);
+            tma_2d(slot + kWOff, &tmWd, &hfull[h], c0, 0);
+            if (p.bd) tma_2d(slot + kBOff, &tmBd, &hfull[h], c0, 0);
+            h_armed |= 1u << h;
+            h_par = (h_par & ~(1u << h)) | (hph << h);
+            if (++h == p.hst) {
+              h = 0;
+              hph ^= 1;
+            }
+          }
+        }
+      }
+    halo_done:
+      if (*abort_flag) {  // let this CTA's own copies land before it exits
+        volatile int never = 0;
+        for (int q = 0; q < p.hst; ++q)
+          if (h_armed & (1u << q))
+            mb_wait(&hfull[q], (h_par >> q) & 1, &never, &g_dwp_status, kDrainNs, 64);
+      }
+    } else if (lane == 1) {
+      int j = 0;
+      uint32_t eph = 0, b_armed = 0, b_par = 0;
+      for (int t = blockIdx.x; t < p.total; t += gridDim.x) {
+        const int nt = t % p.n_ntiles;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mb_wait(&empty[j], eph ^ 1, abort_flag, &g_dwp_status, kWaitNs, 64))
+            goto b_done;
+          uint8_t* st = stages + (size_t)j * p.stage_bytes;
+          mb_expect_tx(&bfull[j], 2 * p.b_bytes);
+          tma_2d(st + 2 * kAHalf, &tmBhi, &bfull[j], kb * 32, nt * p.np);
+          tma_2d(st + 2 * kAHalf + p.b_bytes, &tmBlo, &bfull[j], kb * 32, nt * p.np);
+          b_armed |= 1u << j;
+          b_par = (b_par & ~(1u << j)) | (eph << j);
+          if (++j == 2) {
+            j = 0;
+            eph ^= 1;
+          }
+        }
+      }
+    b_done:
+      if (*abort_flag) {
+        volatile int never = 0;
+        for (int q = 0; q < 2; ++q)
+          if (b_armed & (1u << q))
+            mb_wait(&bfull[q], (b_par >> q) & 1, &never, &g_dwp_status, kDrainNs, 64);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int j = 0, acc = 0;
+      uint32_t ph = 0, aph = 0;
+      bool issued = false;
+      for (int t = blockIdx.x; t < p.total; t += gridDim.x) {
+        if (!mb_wait(&tempty[acc], aph ^ 1, abort_flag, &g_dwp_status, kWaitNs, 64)) break;
+        tc_after();
+        const uint32_t d = tmem + (uint32_t)(acc * p.np);
+        bool ok = true;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mb_wait(&afull[j], ph, abort_flag, &g_dwp_status, kWaitNs, 32) ||
+              !mb_wait(&bfull[j], ph, abort_flag, &g_dwp_status, kWaitNs, 32)) {
+            ok = false;
+            break;
+          }
+          tc_after();
+          DWP_TRACE(5, ((t - (int)blockIdx.x) / (int)gridDim.x) * p.kblocks + kb);
+          const uint32_t a_raw = sa(stages + (size_t)j * p.stage_bytes);
+          const uint32_t a_lo = a_raw + kAHalf;
+          const uint32_t b_hi = a_raw + 2 * kAHalf;
+          const uint32_t b_lo = b_hi + p.b_bytes;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t off = k * 32;  // 8 tf32 along K
+            mma_tf32(d, sw128_desc(a_lo + off), sw128_desc(b_hi + off), p.idesc,
+                     (kb | k) ? 1u : 0u);
+            mma_tf32(d, sw128_desc(a_raw + off), sw128_desc(b_lo + off), p.idesc, 1u);
+            mma_tf32(d, sw128_desc(a_raw + off), sw128_desc(b_hi + off), p.idesc, 1u);
+          }
+          issued = true;
+          mma_commit(&empty[j]);
+          if (++j == 2) {
+            j = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          aph ^= 1;
+        }
+      }
+      if (*abort_flag && issued) {  // this CTA's MMAs finish before TMEM is freed
+        mma_commit(drain);
+        volatile int never = 0;
+        mb_wait(drain, 0, &never, &g_dwp_status, kDrainNs, 64);
+      }
+    }
+  } else if (warp < kBuildWarps) {
+    // ---------------- builders: depthwise conv -> A tile (raw, lo) ----------------
+    // Warps run independently; each hands a halo slot back after its lanes'
+    // reads (__syncwarp, then one elected proxy fence + arrive: the TMA
+    // refill cannot overtake a slow lane) and marks its part of the A tile
+    // written the same way.  Wait results are voted per warp, so a wait that
+    // gave up makes the whole warp leave together.
+    const int tid = threadIdx.x;
+    const int cg = tid % CG;
+    const int ox_l = (tid / CG) % TW;
+    const int rg = tid / (CG * TW);
+    int j = 0, h = 0;
+    uint32_t eph = 0, hph = 0;
+    int step = 0;
+    for (int t = blockIdx.x; t < p.total; t += gridDim.x) {
+      bool ok = true;
+      for (int kb = 0; kb < p.kblocks && ok; ++kb, ++step) {
+        // The stage's previous MMAs are done before its A tile is rewritten.
+        ok = __all_sync(0xffffffffu,
+                        mb_wait(&empty[j], eph ^ 1, abort_flag, &g_dwp_status, kWaitNs, 64));
+        if (!ok) break;
+        uint8_t* a_raw = stages + (size_t)j * p.stage_bytes;
+        uint8_t* a_lo = a_raw + kAHalf;
+        for (int sub = 0; sub < SUBS; ++sub) {
+          const int cl = sub * CB + cg * 2;  // channel within the 32-channel K block
+          if (tid == 0 && sub == 0) DWP_TRACE(1, step);
+          ok = __all_sync(0xffffffffu,
+                          mb_wait(&hfull[h], hph, abort_flag, &g_dwp_status, kWaitNs, 32));
+          if (!ok) break;
+          if (tid == 0 && sub == 0) DWP_TRACE(2, step);
+          const uint8_t* slot = halo + (size_t)h * p.halo_buf;
+          const float* in = reinterpret_cast<const float*>(slot);
+          const float* wsm = reinterpret_cast<const float*>(slot + kWOff);
+          float2 wr[KS][KS];
+#pragma unroll
+          for (int ky = 0; ky < KS; ++ky)
+#pragma unroll
+            for (int kx = 0; kx < KS; ++kx)
+              wr[ky][kx] = *reinterpret_cast<const float2*>(wsm + (ky * KS + kx) * CB + cg * 2);
+          const float2 bv = p.bd ? *reinterpret_cast<const float2*>(slot + kBOff + cg * 8)
+                                 : make_float2(0.f, 0.f);
+          float2 acc[R];
+#pragma unroll
+          for (int r = 0; r < R; ++r) acc[r] = bv;
+#pragma unroll
+          for (int jj = 0; jj < (R - 1) * S + KS; ++jj) {
+            const int iy = rg * R * S + jj;
+            float2 row[KS];
+#pragma unroll
+            for (int kx = 0; kx < KS; ++kx)
+              row[kx] = *reinterpret_cast<const float2*>(in + ((iy * IW) + ox_l * S + kx) * CB +
+                                                         cg * 2);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+              const int ky = jj - r * S;
+              if (ky < 0 || ky >= KS) continue;
+#pragma unroll
+              for (int kx = 0; kx < KS; ++kx) {
+                acc[r].x = fmaf(row[kx].x, wr[ky][kx].x, acc[r].x);
+                acc[r].y = fmaf(row[kx].y, wr[ky][kx].y, acc[r].y);
+              }
+            }
+          }
+          if (tid == 0 && sub == 0) DWP_TRACE(3, step);
+          __syncwarp();
+          if (tid == 0 && sub == 0) DWP_TRACE(10, step);
+          if (lane == 0) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mb_arrive(&hempty[h]);
+          }
+          if (++h == p.hst) {
+            h = 0;
+            hph ^= 1;
+          }
+          const int c16 = cl >> 2;  // 16-byte chunk within the 128-byte A row
+          const uint32_t in16 = (uint32_t)(cl & 3) * 4;  // byte offset inside the chunk
+          with_act(p.act_d, [&](auto tag) {
+            constexpr int A = decltype(tag)::value;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+              const int m = (rg * R + r) * TW + ox_l;  // GEMM row of this pixel
+              float2 v = acc[r];
+              v.x = act_c<A>(v.x);
+              v.y = act_c<A>(v.y);
+              const uint32_t off = (uint32_t)m * 128u + (uint32_t)((c16 ^ (m & 7)) * 16) + in16;
+              *reinterpret_cast<float2*>(a_raw + off) = v;
+              *reinterpret_cast<float2*>(a_lo + off) = make_float2(tf32_lo(v.x), tf32_lo(v.y));
+            }
+          });
+        }
+        if (!ok) break;
+        if (tid == 0) DWP_TRACE(8, step);
+        // Generic-proxy writes of the A tile become visible to the tensor core.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        if (tid == 0) DWP_TRACE(9, step);
+        __syncwarp();
+        if (lane == 0) mb_arrive(&afull[j]);
+        if (tid == 0) DWP_TRACE(4, step);
+        if (++j == 2) {
+          j = 0;
+          eph ^= 1;
+        }
+      }
+      if (!ok) break;
+    }
+  } else {
+    // ---------------- epilogue (warps 18-21) ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    float* tile = epi + (warp - kEpiWarp0) * (32 * kEpiStride);
+    const int sub_r = lane >> 3, sub_c = (lane & 7) * 4;
+    int acc = 0;
+    uint32_t aph = 0;
+    for (int t = blockIdx.x; t < p.total; t += gridDim.x) {
+      int nt, img, ty, tx;
+      decode(t, nt, img, ty, tx);
+      const bool ok = mb_wait(&tfull[acc], aph, abort_flag, &g_dwp_status, kWaitNs, 128);
+      if (__any_sync(0xffffffffu, !ok)) break;
+      tc_after();
+      if (warp == kEpiWarp0 + 2 && lane == 0) DWP_TRACE(6, (t - (int)blockIdx.x) / (int)gridDim.x);
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * p.np);
+      for (int c0 = 0; c0 < p.np; c0 += 32) {
+        const int n0 = nt * p.np + c0;
+        if (n0 >= p.cout) break;  // uniform across the warp
+        float v[32];
+        tmem_ld_32x32(tbase + (uint32_t)c0, v);
+        float4* trow = reinterpret_cast<float4*>(tile + lane * kEpiStride);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          trow[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+        __syncwarp();
+        const int n = n0 + sub_c;
+        const bool nlive = n < p.cout;
+        const float4 b4 = (nlive && p.bp) ? __ldg(reinterpret_cast<const float4*>(p.bp + n))
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        // All eight residual loads are issued before any store.
+        float4 r4[8];
+        int64_t off[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int m = q * 32 + i * 4 + sub_r;
+          const int oy = ty * TH + m / TW, ox = tx * TW + m % TW;
+          const bool v = m < TH * TW && oy < p.oh && ox < p.ow && nlive;
+          off[i] = v ? (((int64_t)img * p.oh + oy) * p.ow + ox) * p.cout + n : -1;
+          r4[i] = (v && p.res) ? __ldg(reinterpret_cast<const float4*>(p.res + off[i]))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        with_act(p.act_p, [&](auto tag) {
+          constexpr int A = decltype(tag)::value;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if (off[i] < 0) continue;
+            float4 o = *reinterpret_cast<const float4*>(tile + (i * 4 + sub_r) * kEpiStride + sub_c);
+            o.x = act_c<A>(o.x + b4.x + r4[i].x);
+            o.y = act_c<A>(o.y + b4.y + r4[i].y);
+            o.z = act_c<A>(o.z + b4.z + r4[i].z);
+            o.w = act_c<A>(o.w + b4.w + r4[i].w);
+            *reinterpret_cast<float4*>(p.y + off[i]) = o;
+          }
+        });
+        __syncwarp();
+      }
+      tc_before();
+      mb_arrive(&tempty[acc]);
+      if (warp == kEpiWarp0 + 2 && lane == 0) DWP_TRACE(7, (t - (int)blockIdx.x) / (int)gridDim.x);
+      if (++acc == 2) {
+        acc = 0;
+        aph ^= 1;
+      }
+    }
+  }
+
+  tc_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(p.tmem_cols));
+  }
+}
+
+typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                             const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                             const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                             CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encoder() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* q = nullptr;
+    cudaDriverEntryPointQueryResult r;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &q, cudaEnableDefault, &r) ==
+            cudaSuccess &&
+        r == cudaDriverEntryPointSuccess)
+      fn = (EncodeFn)q;
+  });
+  return fn;
+}
+
+int num_sms() {
+  static int v = 0;
+  if (!v) {
+    int d = 0;
+    cudaGetDevice(&d);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, d);
+    if (v <= 0) v = kNumSms;
+  }
+  return v;
+}
+
+// Tile configuration of one instantiation.
+struct DwpCfg {
+  int th, tw, cb;
+};
+
+template <int KS, int S, int TH, int TW, int CB, int R>
+int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, const float* bd,
+               const float* w_hi, const float* w_lo, const float* bp, const float* res, float* y,
+               const spx_dwproj_params* q, bool dry_run, uint32_t* smem_out) {
+  constexpr int IH = (TH - 1) * S + KS, IW = (TW - 1) * S + KS;
+  constexpr uint32_t kHaloBytes = IH * IW * CB * 4;
+  DwpArgs p{};
+  p.n = q->n;
+  p.ih = q->ih;
+  p.iw = q->iw;
+  p.ce = q->c;
+  p.oh = q->oh;
+  p.ow = q->ow;
+  p.cout = q->cout;
+  p.n_ntiles = q->cout <= 256 ? 1 : (int)ceil_div(q->cout, 256);
+  const int per = (int)ceil_div(q->cout, p.n_ntiles);
+  p.np = (int)ceil_div(per, 32) * 32;
+  p.pt = q->pad_top;
+  p.pl = q->pad_left;
+  p.tiles_h = (int)ceil_div(q->oh, TH);
+  p.tiles_w = (int)ceil_div(q->ow, TW);
+  p.kblocks = (int)ceil_div(q->c, 32);
+  const int64_t total = (int64_t)p.n_ntiles * q->n * p.tiles_h * p.tiles_w;
+  if (total > INT32_MAX) return fail(SPX_ERR_UNSUPPORTED, "dw_project: too many tiles");
+  p.total = (int)total;
+  constexpr uint32_t kSlotBytes =
+      (kHaloBytes + 127) / 128 * 128 + (KS * KS * CB * 4 + 127) / 128 * 128 + CB * 4;
+  p.halo_buf = (kSlotBytes + 1023) / 1024 * 1024;
+  p.b_bytes = (uint32_t)p.np * 128;
+  p.stage_bytes = 2 * kAHalf + 2 * p.b_bytes;
+  uint32_t cols = 32;
+  while (cols < (uint32_t)(2 * p.np)) cols <<= 1;
+  p.tmem_cols = cols;
+  p.idesc = idesc_tf32(128, p.np);
+  p.wd = wd;
+  p.bd = bd;
+  p.act_d = q->act_dw;
+  p.bp = bp;
+  p.res = res;
+  p.y = y;
+  p.act_p = q->act_proj;
+  const uint32_t fixed = 1024 + 2 * p.stage_bytes + 4 * kEpiTileBytes + 256;
+  const uint32_t cap = 227 * 1024;
+  int hst = 0;
+  while (hst < 3 && fixed + (uint32_t)(hst + 1) * p.halo_buf <= cap) ++hst;
+  if (hst < 2)
+    return fail(SPX_ERR_UNSUPPORTED, "dw_project: tile buffers exceed shared memory");
+  p.hst = hst;
+  const uint32_t smem = fixed + (uint32_t)hst * p.halo_buf;
+  if (smem_out) *smem_out = smem;
+  if (dry_run) return SPX_OK;
+
+  EncodeFn fn = encoder();
+  if (!fn) return fail(SPX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  CUtensorMap mx, mh, ml, mw, mb;
+  {
+    cuuint64_t dims[4] = {(cuuint64_t)q->c, (cuuint64_t)q->iw, (cuuint64_t)q->ih,
+                          (cuuint64_t)q->n};
+    cuuint64_t strides[3] = {(cuuint64_t)q->c * 4, (cuuint64_t)q->iw * q->c * 4,
+                             (cuuint64_t)q->ih * q->iw * q->c * 4};
+    cuuint32_t box[4] = {(cuuint32_t)CB, (cuuint32_t)IW, (cuuint32_t)IH, 1};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    CUresult r = fn(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)x, dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SPX_ERR_CUDA, "dw_project: halo map encode failed (%d)", (int)r);
+  }
+  for (int b = 0; b < 2; ++b) {
+    cuuint64_t dims[2] = {(cuuint64_t)q->c, (cuuint64_t)q->cout};
+    cuuint64_t strides[1] = {(cuuint64_t)q->c * 4};
+    cuuint32_t box[2] = {32, (cuuint32_t)p.np};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(b ? &ml : &mh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                    (void*)(b ? w_lo : w_hi), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(SPX_ERR_CUDA, "dw_project: weight map encode failed (%d)", (int)r);
+  }
+  // Depthwise taps [KS*KS][c] and bias [1][c]: CB-channel boxes per sub-block.
+  for (int b = 0; b < 2; ++b) {
+    if (b == 1 && !bd) {
+      mb = mw;  // unused: the kernel loads no bias box without a bias
+      break;
+    }
+    cuuint64_t dims[2] = {(cuuint64_t)q->c, (cuuint64_t)(b ? 1 : KS * KS)};
+    cuuint64_t strides[1] = {(cuuint64_t)q->c * 4};
+    cuuint32_t box[2] = {(cuuint32_t)CB, (cuuint32_t)(b ? 1 : KS * KS)};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(b ? &mb : &mw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                    (void*)(b ? bd : wd), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(SPX_ERR_CUDA, "dw_project: depthwise weight map encode failed (%d)", (int)r);
+  }
+  auto kern = dwproj_kernel<KS, S, TH, TW, CB, R>;
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [&] {
+    attr = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+  });
+  if (attr != cudaSuccess) return check_cuda(attr, "dw_project: smem attribute");
+  const int grid = (int)(p.total < num_sms() ? p.total : num_sms());
+  kern<<<grid, kThreads, smem, s>>>(mx, mh, ml, mw, mb, p);
+  return after_launch(cnt, "dw_project");
+}
+
+bool al16(const void* v) { return ((uintptr_t)v & 15) == 0; }
+
+}  // namespace
+
+#ifdef SPX_DWP_TRACE
+extern "C" int spx_dwp_trace(unsigned long long* out) {
+  return cudaMemcpyFromSymbol(out, g_dwp_trace, sizeof(g_dwp_trace)) == cudaSuccess ? 0 : 3;
+}
+#endif
+
+int dwp_take_status() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_dwp_status, sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (v) {
+    int zero = 0;
+    cudaMemcpyToSymbol(g_dwp_status, &zero, sizeof(int));
+  }
+  return v;
+}
+
+// Returns SPX_ERR_UNSUPPORTED (without launching) for shapes the fused kernel
+// does not take; `dry_run` only checks eligibility.
+int launch_dw_project(cudaStream_t s, int64_t* cnt, const float* x, const float* wd,
+                      const float* bd, const float* w_hi, const float* w_lo, const float* bp,
+                      const float* res, float* y, const spx_dwproj_params* q, bool dry_run) {
+  if (!q) return fail(SPX_ERR_INVALID_ARGUMENT, "dw_project: null params");
+  if (q->n <= 0 || q->ih <= 0 || q->iw <= 0 || q->c <= 0 || q->oh <= 0 || q->ow <= 0 ||
+      q->cout <= 0)
+    return fail(SPX_ERR_INVALID_ARGUMENT, "dw_project: non-positive size");
+  if (q->kernel != 3 || (q->stride != 1 && q->stride != 2))
+    return fail(SPX_ERR_UNSUPPORTED, "dw_project: 3x3 depthwise with stride 1 or 2 only");
+  if (q->c % 4 || q->cout % 4)
+    return fail(SPX_ERR_UNSUPPORTED, "dw_project: channel counts must be multiples of 4");
+  if (q->cout > 512) return fail(SPX_ERR_UNSUPPORTED, "dw_project: at most 512 outputs");
+  if (q->pad_top < 0 || q->pad_left < 0 || q->pad_top > 2 || q->pad_left > 2)
+    return fail(SPX_ERR_INVALID_ARGUMENT, "dw_project: pads must be 0..2");
+  if ((int64_t)(q->oh - 1) * q->stride - q->pad_top + 3 <= 0 ||
+      (int64_t)(q->oh - 1) * q->stride - q->pad_top >= q->ih ||
+      (int64_t)(q->ow - 1) * q->stride - q->pad_left >= q->iw)
+    return fail(SPX_ERR_INVALID_ARGUMENT, "dw_project: output size does not match the input");
+  if (!dry_run) {
+    if (!x || !wd || !w_hi || !w_lo || !y)
+      return fail(SPX_ERR_INVALID_ARGUMENT, "dw_project: null tensor");
+    if (!al16(x) || !al16(wd) || !al16(w_hi) || !al16(w_lo) || !al16(y) || (bd && !al16(bd)) ||
+        (bp && !al16(bp)) || (res && !al16(res)))
+      return fail(SPX_ERR_INVALID_ARGUMENT, "dw_project: tensors must be 16-byte aligned");
+  }
+  if (q->stride == 1) {
+    if (q->ow <= 8)
+      return launch_cfg<3, 1, 8, 8, 32, 2>(s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run,
+                                           nullptr);
+    return launch_cfg<3, 1, 8, 16, 32, 4>(s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run,
+                                          nullptr);
+  }
+  if (q->ow <= 8)
+    return launch_cfg<3, 2, 8, 8, 16, 1>(s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run,
+                                         nullptr);
+  return launch_cfg<3, 2, 8, 16, 16, 2>(s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run,
+                                        nullptr);
+}
+
+}  // namespace spx

@@ -1,0 +1,152 @@
+// Blackwell (sm_100a) primitives shared by the fused tensor-core kernels:
+// mbarriers with bounded waits, TMA tensor loads, tcgen05 MMA / TMEM access and
+// the 3xTF32 lo-term split.  Everything is inline PTX; nothing here allocates.
+#pragma once
+
+#include <cuda.h>
+#include <stdint.h>
+
+namespace spx {
+namespace sm100 {
+
+__device__ __forceinline__ uint32_t sa(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mb_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sa(b)), "r"(count));
+}
+__device__ __forceinline__ void mb_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sa(b)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mb_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sa(b)) : "memory");
+}
+__device__ __forceinline__ bool mb_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(sa(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of the given parity.  False when the CTA is
+// aborting (another role gave up) or this wait ran past `limit_ns`, in which
+// case it raises the abort flag and the device status `status`.
+__device__ __forceinline__ bool mb_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag,
+                                        int* status, unsigned long long limit_ns,
+                                        int max_sleep_ns) {
+  if (mb_try(b, parity)) return true;
+  const unsigned long long t0 = gtime();
+  int sleep_ns = 16;
+  for (;;) {
+    if (max_sleep_ns > 0) {
+      __nanosleep(sleep_ns);
+      sleep_ns = sleep_ns * 2 < max_sleep_ns ? sleep_ns * 2 : max_sleep_ns;
+    }
+#pragma unroll 1
+    for (int i = 0; i < 4; ++i)
+      if (mb_try(b, parity)) return true;
+    if (*abort_flag) return false;
+    if (gtime() - t0 > limit_ns) {
+      *abort_flag = 1;
+      atomicExch(status, 1);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
+                                       int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(sa(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(sa(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                       int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(sa(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(sa(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand in 128-byte-swizzled
+// 8-row (1024-byte) atoms, one 128-byte row per M / N index.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);  // start address
+  d |= (uint64_t)1 << 16;                     // leading byte offset (unused: K fits one row)
+  d |= (uint64_t)(1024 >> 4) << 32;           // stride byte offset: next 8-row atom
+  d |= (uint64_t)1 << 46;                     // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                     // swizzle: 128B
+  return d;
+}
+// Instruction descriptor: tf32 A and B, f32 accumulator, M x N.
+__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
+}
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          sa(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tc_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// 32 TMEM lanes (this warp's quarter) x 32 consecutive columns from taddr.
+__device__ __forceinline__ void tmem_ld_32x32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// tf32 lo term of an operand the MMA reads raw.  kind::tf32 uses the upper 19
+// bits of each 32-bit element, so the raw fp32 value already is
+// hi = trunc_tf32(x); lo = rna_tf32(x - hi) (exact difference, rounded to
+// nearest with ties away on the bit pattern: add bit 12, clear the low 13).
+// inf / nan give lo = 0 (the raw special value carries the product).
+__device__ __forceinline__ float tf32_lo(float x) {
+  const uint32_t b = __float_as_uint(x);
+  if ((b & 0x7F800000u) == 0x7F800000u) return 0.0f;
+  const float r = x - __uint_as_float(b & 0xFFFFE000u);
+  return __uint_as_float((__float_as_uint(r) + 0x1000u) & 0xFFFFE000u);
+}
+
+}  // namespace sm100
+}  // namespace spx

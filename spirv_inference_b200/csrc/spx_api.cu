@@ -516,6 +516,8 @@ int64_t spx_get_option(const char* name) {
 static int device_status(const char* what) {
   if (dw_take_status())
     return fail(SPX_ERR_CUDA, "%s: a depthwise tile load wait timed out", what);
+  if (dwp_take_status())
+    return fail(SPX_ERR_CUDA, "%s: a fused depthwise-projection pipeline wait timed out", what);
   if (tc_take_status())
     return fail(SPX_ERR_CUDA, "%s: a tensor-core pipeline wait timed out; tiles were abandoned",
                 what);
@@ -838,6 +840,21 @@ int spx_op_binary(spx_graph* g, int32_t op, const float* a, const float* b, floa
   SPX_G(g);
   if (!a || !b || !y || !p) return fail(SPX_ERR_INVALID_ARGUMENT, "binary: null argument");
   return launch_binary(g->stream, &g->launches, op, a, b, y, p);
+}
+
+int spx_op_dw_project_nhwc(spx_graph* g, const float* x, const float* w_dw, const float* b_dw,
+                           const float* w_proj_hi, const float* w_proj_lo, const float* b_proj,
+                           const float* residual, float* y, const spx_dwproj_params* p) {
+  SPX_G(g);
+  return launch_dw_project(g->stream, &g->launches, x, w_dw, b_dw, w_proj_hi, w_proj_lo, b_proj,
+                           residual, y, p, false);
+}
+
+int spx_dw_project_supported(const spx_dwproj_params* p) {
+  return launch_dw_project(nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                           nullptr, nullptr, nullptr, p, true) == SPX_OK
+             ? 1
+             : 0;
 }
 
 int spx_op_select(spx_graph* g, const float* pred, const float* a, const float* b, float* y,

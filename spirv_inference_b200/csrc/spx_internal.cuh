@@ -234,6 +234,12 @@ int launch_weights_split(cudaStream_t s, int64_t* cnt, const float* w, float* hi
 // Returns and clears the device status of the tensor-core pipeline (0 = ok,
 // 1 = a pipeline wait timed out and the kernel aborted its tiles).
 int tc_take_status();
+int dwp_take_status();
+// Fused depthwise 3x3 -> 1x1 projection (k_dwproj.cu).  dry_run: eligibility
+// check only (SPX_OK or SPX_ERR_UNSUPPORTED), nothing launched.
+int launch_dw_project(cudaStream_t s, int64_t* cnt, const float* x, const float* wd,
+                      const float* bd, const float* w_hi, const float* w_lo, const float* bp,
+                      const float* res, float* y, const spx_dwproj_params* q, bool dry_run);
 int ar_take_status();
 
 // Process-wide dense-contraction path: 0 auto, 1 SIMT only, 2 tensor cores

@@ -10,6 +10,9 @@ issues activations and residual adds as extra dispatches
 * keeps every activation in HBM in NHWC,
 * fuses bias + activation into every conv / depthwise / FC epilogue and the
   residual ADD of an inverted-residual block into the projecting 1x1 conv,
+* by default (fuse_dw_project) runs a block's 3x3 depthwise conv, the 1x1
+  projection after it and the residual add as one kernel
+  (spx_op_dw_project_nhwc), the depthwise output staying on chip,
 * optionally (fuse_expand_dw) runs a block's 1x1 expand conv and the 3x3
   depthwise after it as one kernel, the expanded tensor staying on chip;
   off by default: its CUDA-core expand (exact fp32, ~14 TFLOP/s) is slower
@@ -29,15 +32,24 @@ from .lowering import same_padding_offsets
 from .nets import Model, Op
 
 
+class _Shape:
+    """Shape-only stand-in for a DeviceTensor (eligibility checks at planning)."""
+
+    def __init__(self, shape):
+        self.shape = tuple(shape)
+
+
 class CnnExecutor:
     def __init__(self, model: Model, batch: int, device: int = 0, graph: Graph | None = None,
                  fuse_residual: bool = True, presplit: bool = True,
-                 fuse_expand_dw: bool = False):
+                 fuse_expand_dw: bool = False, fuse_dw_project: bool = True):
         self.model = model
         self.batch = batch
         self.g = graph or Graph(device)
         self.fuse_residual = fuse_residual
         self.fuse_expand_dw = fuse_expand_dw
+        self.fuse_dw_project = fuse_dw_project and presplit
+        self.fused_away: set[str] = set()   # tensors that never reach HBM
         self.presplit = presplit
         self._splits: dict = {}
         self.w: dict[str, DeviceTensor] = {}
@@ -109,9 +121,69 @@ class CnnExecutor:
                     continue
                 expand_of[op.output] = p
                 expanded.add(p.output)
+        # Depthwise -> projection fusion: a 3x3 depthwise (SAME, no dilation,
+        # depth multiplier 1, equal strides 1 / 2) whose only consumer is a
+        # 1x1 stride-1 conv; the conv's residual ADD (if fused) comes along.
+        proj_of: dict[str, Op] = {}   # depthwise output -> projecting conv
+        if self.fuse_dw_project:
+            consumers: dict[str, list] = {}
+            for op in m.ops:
+                for i in op.inputs:
+                    consumers.setdefault(i, []).append(op)
+            for op in m.ops:
+                if op.type != "DEPTHWISE_CONV_2D" or op.output in expand_of:
+                    continue
+                a = op.attrs
+                wd = m.weights[op.inputs[1]]
+                cs = consumers.get(op.output, [])
+                if len(cs) != 1 or cs[0].type != "CONV_2D":
+                    continue
+                pc = cs[0]
+                wp = m.weights[pc.inputs[1]]
+                if (wp.shape[1:3] != (1, 1) or tuple(pc.attrs["stride"]) != (1, 1)
+                        or pc.inputs[0] != op.output or wd.shape[1:3] != (3, 3)
+                        or tuple(a.get("dilation", (1, 1))) != (1, 1)
+                        or a.get("depth_multiplier", 1) != 1
+                        or a["stride"][0] != a["stride"][1]):
+                    continue
+                h, w_, c = m.shapes[op.inputs[0]]
+                oh, ow, cout = m.shapes[pc.output]
+                pt, pl = same_padding_offsets(a["padding"], h, w_, oh, ow, 3, 3, *a["stride"])
+                if not self.g.dw_project_supported(
+                        _Shape((self.batch, h, w_, c)), _Shape((self.batch, oh, ow, cout)),
+                        stride=a["stride"][0], pad=(pt, pl), act_dw=a.get("activation", 0),
+                        act_proj=pc.attrs.get("activation", 0)):
+                    continue
+                proj_of[op.output] = pc
+        proj_convs = {pc.output: d for d, pc in proj_of.items()}
         self._buf(m.input)
         for op in m.ops:
             a = op.attrs
+            if op.type == "DEPTHWISE_CONV_2D" and op.output in proj_of:
+                self.fused_away.add(op.output)
+                continue  # runs inside the projection that consumes it
+            if op.type == "CONV_2D" and op.output in proj_convs:
+                dname = proj_convs[op.output]
+                dop = next(o for o in m.ops if o.output == dname)
+                da = dop.attrs
+                x = self._buf(dop.inputs[0])
+                res = None
+                out_name = op.output
+                if op.output in fused_into:
+                    out_name, skip = fused_into[op.output]
+                    res = self._buf(skip)
+                y = self._buf(out_name)
+                self.t[op.output] = y
+                pt, pl = same_padding_offsets(da["padding"], x.shape[1], x.shape[2], y.shape[1],
+                                              y.shape[2], 3, 3, *da["stride"])
+                wd = self.w[dop.inputs[1]]
+                self._plan.append(("dwproj", dict(
+                    x=x, wd=wd.view((3, 3, wd.shape[3])), bd=self.w[dop.inputs[2]],
+                    w=self.w[op.inputs[1]], w_split=self._split(op.inputs[1]),
+                    bp=self.w[op.inputs[2]], y=y, residual=res, stride=da["stride"][0],
+                    pad=(pt, pl), act_dw=da.get("activation", 0),
+                    act_proj=a.get("activation", 0))))
+                continue
             if op.type == "CONV_2D" and op.output in expanded:
                 continue  # runs inside the depthwise that consumes it
             if op.type == "DEPTHWISE_CONV_2D" and op.output in expand_of:
@@ -202,6 +274,10 @@ class CnnExecutor:
                 g.expand_dw_nhwc(p["x"], p["we"], p["be"], p["wd"], p["bd"], p["y"],
                                  stride=p["stride"], pad=p["pad"], act_expand=p["act_e"],
                                  act_dw=p["act_d"], w_split=p["we_split"])
+            elif kind == "dwproj":
+                g.dw_project_nhwc(p["x"], p["wd"], p["bd"], p["w_split"], p["bp"], p["y"],
+                                  stride=p["stride"], pad=p["pad"], act_dw=p["act_dw"],
+                                  act_proj=p["act_proj"], residual=p["residual"])
             elif kind == "dw":
                 g.depthwise_nhwc(p["x"], p["w"], p["bias"], p["y"], stride=p["stride"],
                                  pad=p["pad"], dilation=p["dilation"], activation=p["activation"])
@@ -239,6 +315,14 @@ class CnnExecutor:
                 f = 2 * e_px * ce * cin + 2 * y.size * 9
                 b = x.size + we.size + ce + p["wd"].size + ce + y.size
                 label = "expand_dw"
+            elif kind == "dwproj":
+                x, wd, w, y = p["x"], p["wd"], p["w"], p["y"]
+                c, cout = x.shape[-1], y.shape[-1]
+                px = y.size // cout
+                f = 2 * px * c * 9 + 2 * px * c * cout
+                b = (x.size + wd.size + c + w.size + cout + y.size
+                     + (y.size if p["residual"] is not None else 0))
+                label = "dw_project"
             elif kind == "dw":
                 x, w, y = p["x"], p["w"], p["y"]
                 f = 2 * y.size * w.shape[0] * w.shape[1]
@@ -286,6 +370,9 @@ class CnnExecutor:
         return self.g.download(self.output)
 
     def tensor(self, name: str) -> np.ndarray:
+        if name in self.fused_away:
+            raise KeyError(f"{name} stays on chip inside a fused kernel (fuse_dw_project=False "
+                           "keeps it)")
         return self.g.download(self.t[name])
 
     def close(self) -> None:

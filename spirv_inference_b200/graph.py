@@ -289,6 +289,29 @@ class Graph:
                                             self._p(b_expand), self._p(w_dw), self._p(b_dw),
                                             self._p(y), ctypes.byref(p)))
 
+    @staticmethod
+    def _dwproj_params(x, y, *, stride, pad, act_dw, act_proj, kernel=3):
+        n, ih, iw, c = x.shape
+        _, oh, ow, cout = y.shape
+        return _lib.DwProjParams(n, ih, iw, c, oh, ow, kernel, stride, pad[0], pad[1], act_dw,
+                                 cout, act_proj)
+
+    def dw_project_supported(self, x, y, *, stride, pad, act_dw=_lib.ACT_RELU6,
+                             act_proj=_lib.ACT_NONE, kernel=3) -> bool:
+        p = self._dwproj_params(x, y, stride=stride, pad=pad, act_dw=act_dw, act_proj=act_proj,
+                                kernel=kernel)
+        return bool(self._l.spx_dw_project_supported(ctypes.byref(p)))
+
+    def dw_project_nhwc(self, x, w_dw, b_dw, w_split, b_proj, y, *, stride, pad,
+                        act_dw=_lib.ACT_RELU6, act_proj=_lib.ACT_NONE, residual=None):
+        """Fused 3x3 depthwise + 1x1 projection (+ residual): x NHWC
+        [n][ih][iw][c], w_dw [3][3][c], w_split = pre-split projection weights
+        (hi, lo) [cout][c], y NHWC [n][oh][ow][cout]."""
+        p = self._dwproj_params(x, y, stride=stride, pad=pad, act_dw=act_dw, act_proj=act_proj)
+        check(self._l.spx_op_dw_project_nhwc(
+            self.h, self._p(x), self._p(w_dw), self._p(b_dw), self._p(w_split[0]),
+            self._p(w_split[1]), self._p(b_proj), self._p(residual), self._p(y), ctypes.byref(p)))
+
     # -- decode path -------------------------------------------------------
     def rope_kv_append(self, qkv, ld_qkv, cos_t, sin_t, state, q_out, k_cache, v_cache, *,
                        batch, q_len, q_heads, kv_heads, head_dim, max_seq):

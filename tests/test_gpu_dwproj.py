@@ -1,0 +1,129 @@
+"""GPU tests of the fused depthwise 3x3 -> 1x1 projection (+ residual)
+kernel, spx_op_dw_project_nhwc: against a float64 formulation of the two
+reference shaders (depthwise_conv2d.comp then conv2d.comp, plus add.comp),
+over every tile configuration (stride 1 / 2, maps wider and narrower than
+8 columns), projection widths from 16 to 320 (two n tiles), ragged map
+edges, channel counts that are not multiples of 32, and with and without
+the residual.  Tolerance: the 3xTF32 bound the tensor-core GEMM tests use,
+normwise (2.5e-8 K + 1e-6) relative to the output scale."""
+import numpy as np
+import pytest
+
+import _np_ref as R
+from spirv_inference_b200 import _lib, lowering, nets
+from spirv_inference_b200.executor import CnnExecutor
+from spirv_inference_b200.graph import Graph
+
+pytestmark = pytest.mark.gpu
+RNG = np.random.default_rng(23)
+
+
+def _r(*shape, scale=1.0):
+    return (RNG.uniform(-1, 1, size=shape) * scale).astype(np.float32)
+
+
+@pytest.fixture
+def g(gpu):
+    with Graph(gpu) as graph:
+        yield graph
+
+
+CASES = [
+    # n, ih, c, s, cout, residual
+    (2, 16, 32, 1, 16, False),
+    (2, 19, 96, 2, 24, False),     # ragged 10x10 output, s2 (16-channel halo sub-blocks)
+    (1, 56, 144, 1, 24, True),     # MobileNetV2 block 3 shape, K = 144 (4.5 K blocks)
+    (1, 56, 144, 2, 32, False),
+    (2, 28, 192, 1, 32, True),
+    (2, 14, 384, 1, 64, True),
+    (2, 14, 384, 1, 96, False),    # np = 96: second accumulator at TMEM column 96
+    (3, 14, 576, 1, 96, True),
+    (3, 112, 32, 1, 16, False),    # MobileNetV2's first block at full map size
+    (3, 112, 96, 2, 24, False),    # even map, stride 2: no top / left padding
+    (2, 14, 576, 2, 160, False),   # 7x7 output: the narrow-map tile
+    (3, 7, 960, 1, 160, True),
+    (2, 7, 960, 1, 320, False),    # two n tiles of 160
+    (1, 9, 40, 1, 52, False),      # c and cout not multiples of 32
+]
+
+
+@pytest.mark.parametrize("n,ih,c,s,cout,residual", CASES)
+def test_dw_project_matches_float64(g, n, ih, c, s, cout, residual):
+    oh = -(-ih // s)
+    tot = max((oh - 1) * s + 3 - ih, 0)
+    pt = tot // 2
+    x = _r(n, ih, ih, c, scale=2.0)
+    wd, bd = _r(3, 3, c), _r(c, scale=0.1)
+    wp = _r(cout, c, scale=np.sqrt(3.0 / c))
+    bp = _r(cout, scale=0.1)
+    res = _r(n, oh, oh, cout) if residual else None
+    dwp = g.tensor(wp)
+    split = g.weights_split(dwp)
+    dy = g.alloc((n, oh, oh, cout))
+    dx = g.tensor(x)
+    assert g.dw_project_supported(dx, dy, stride=s, pad=(pt, pt))
+    g.dw_project_nhwc(dx, g.tensor(wd), g.tensor(bd), split, g.tensor(bp), dy, stride=s,
+                      pad=(pt, pt), act_dw=_lib.ACT_RELU6,
+                      residual=g.tensor(res) if residual else None)
+    d = np.clip(R.depthwise_nhwc(x, wd, bd, (s, s), (pt, pt), (oh, oh)), 0, 6)
+    ref = d @ wp.T.astype(np.float64) + bp
+    if residual:
+        ref = ref + res
+    got = dy.download()
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    assert err <= 2.5e-8 * c + 1e-6, err
+    # and the unfused depthwise + tensor-core conv of the library agree
+    dd = g.alloc((n, oh, oh, c))
+    g.depthwise_nhwc(dx, g.tensor(wd), g.tensor(bd), dd, stride=(s, s), pad=(pt, pt),
+                     activation=_lib.ACT_RELU6)
+    dz = g.alloc((n, oh, oh, cout))
+    g.conv2d_nhwc(dd, dwp.view((cout, 1, 1, c)), g.tensor(bp), dz,
+                  residual=g.tensor(res) if residual else None, w_split=split)
+    assert np.abs(got - dz.download()).max() / np.abs(ref).max() <= 2 * (2.5e-8 * c + 1e-6)
+
+
+def test_dw_project_rejects_unsupported(g):
+    x, y = g.alloc((1, 8, 8, 30)), g.alloc((1, 8, 8, 16))
+    assert not g.dw_project_supported(x, y, stride=1, pad=(1, 1))     # c % 4
+    x2, y2 = g.alloc((1, 8, 8, 32)), g.alloc((1, 8, 8, 600))
+    assert not g.dw_project_supported(x2, y2, stride=1, pad=(1, 1))   # cout > 512
+    with pytest.raises(_lib.SpxError):
+        g.dw_project_nhwc(x, g.alloc((3, 3, 30)), None, (g.alloc((16, 30)), g.alloc((16, 30))),
+                          None, y, stride=1, pad=(1, 1))
+
+
+def test_mobilenet_v2_fusion_plan_and_parity(gpu, oracle_built):
+    m = nets.mobilenet_v2(seed=0)
+    x = nets.make_input(m, 3, seed=5)
+    outs = []
+    for fuse in (True, False):
+        ex = CnnExecutor(m, batch=3, device=gpu, fuse_dw_project=fuse)
+        try:
+            if fuse:
+                assert sum(k == "dwproj" for k, _ in ex._plan) == 17
+                assert not any(k == "dw" for k, _ in ex._plan)
+            outs.append(ex.forward(x))
+        finally:
+            ex.close()
+    ref, _ = lowering.run_graph(m, x, oracle_built.run_kernel)
+    # the fused kernel reproduces the unfused depthwise + tensor-core GEMM
+    # pipeline bit for bit (same split, same MMA order)
+    np.testing.assert_array_equal(outs[0], outs[1])
+    for o in outs:
+        np.testing.assert_array_equal(lowering.top1(o), lowering.top1(ref))
+        assert np.abs(o - ref).max() <= 1e-4
+
+
+def test_fused_forward_is_deterministic(gpu):
+    """Repeated runs of the fused MobileNetV2 step give bit-identical outputs
+    (a halo slot refilled while a slow builder still read it, or an A tile
+    rewritten under the MMA, would show up as run-to-run differences)."""
+    m = nets.mobilenet_v2(seed=0)
+    x = nets.make_input(m, 16, seed=5)
+    ex = CnnExecutor(m, batch=16, device=gpu)
+    try:
+        first = ex.forward(x)
+        for _ in range(12):
+            np.testing.assert_array_equal(ex.forward(x), first)
+    finally:
+        ex.close()

@@ -175,3 +175,30 @@ def test_plain_c_host_against_header_and_library(spx_built, tmp_path):
     assert cc.returncode == 0, cc.stderr
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
+
+
+def test_ctypes_signatures_match_header():
+    """Every ctypes binding declares as many arguments as include/spx.h."""
+    text = (ROOT / "include" / "spx.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    decls = dict(re.findall(r"\b(spx_[a-z0-9_]+)\s*\(([^()]*)\)\s*;", text))
+    assert decls
+    for name, (args, _) in _lib._SIGS.items():
+        assert name in decls, name
+        params = decls[name].strip()
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        assert n == len(args), (name, n, len(args))
+
+
+def test_dw_project_eligibility_on_host(spx_built):
+    """Shape eligibility of the fused depthwise -> projection kernel is decided
+    on the host (no device needed)."""
+    l = _lib.lib()
+    ok = _lib.DwProjParams(2, 56, 56, 144, 56, 56, 3, 1, 1, 1, 3, 24, 0)
+    assert l.spx_dw_project_supported(ctypes.byref(ok)) == 1
+    for field, bad in (("kernel", 5), ("c", 30), ("cout", 600), ("stride", 3)):
+        q = _lib.DwProjParams(2, 56, 56, 144, 56, 56, 3, 1, 1, 1, 3, 24, 0)
+        setattr(q, field, bad)
+        assert l.spx_dw_project_supported(ctypes.byref(q)) == 0, field
+    assert l.spx_op_dw_project_nhwc(None, *([None] * 8), ctypes.byref(ok)) == \
+        _lib.SPX_ERR_INVALID_ARGUMENT
