@@ -66,11 +66,11 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kBuildWarps = 16;
-constexpr int kProdWarp = 16;
-constexpr int kMmaWarp = 17;
-constexpr int kEpiWarp0 = 18;
-constexpr int kThreads = 22 * 32;
+constexpr int kBuildWarps = 8;
+constexpr int kProdWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kEpiWarp0 = 10;
+constexpr int kThreads = 14 * 32;
 constexpr int kEpiStride = 36;                  // floats per row of an epilogue tile
 constexpr uint32_t kEpiTileBytes = 32 * kEpiStride * 4;
 constexpr uint32_t kAHalf = 128 * 32 * 4;        // one 128 x 32 fp32 A tile: 16 KB
@@ -85,6 +85,8 @@ struct DwpArgs {
   uint32_t stage_bytes;    // A raw | A lo | B hi | B lo
   uint32_t b_bytes;        // NP x 128
   uint32_t idesc, tmem_cols;
+  uint32_t idesc2;         // N = 2 NP (hi and lo weight tiles as one operand)
+  int cat;                 // 1: raw*[hi;lo] + lo*hi (two MMAs per k-step), acc stride 2 NP
   const float* wd;         // depthwise weights [3][3][ce]
   const float* bd;         // depthwise bias [ce] or null
   int act_d;
@@ -104,6 +106,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int IH = (TH - 1) * S + KS, IW = (TW - 1) * S + KS;
   constexpr int CG = CB / 2;  // channel pairs per sub-block
   constexpr int SUBS = 32 / CB;
+  constexpr int CW = 2;       // output columns per builder thread
+  constexpr int WIN = (CW - 1) * S + KS;  // input columns a thread's window spans
   constexpr uint32_t kHaloBytes = IH * IW * CB * 4;
   // A halo slot: the input box, then the sub-block's depthwise taps [KS*KS][CB]
   // and its bias [CB] (TMA boxes of the weight tensors; zero past c).
@@ -111,7 +115,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kWBytes = KS * KS * CB * 4;
   constexpr uint32_t kBOff = kWOff + (kWBytes + 127) / 128 * 128;  // TMA: 128-byte aligned
   const uint32_t slot_tx = kHaloBytes + kWBytes + (p.bd ? CB * 4 : 0);
-  static_assert(CG * TW * (TH / R) == kBuildWarps * 32, "one builder thread per (rows, col, pair)");
+  static_assert(CG * (TW / CW) * (TH / R) == kBuildWarps * 32,
+                "one builder thread per (rows, column pair, channel pair)");
   static_assert(TH * TW <= 128, "a tile is at most 128 GEMM rows");
   static_assert(TH % R == 0 && 32 % CB == 0, "tile shape");
 
@@ -245,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; t < p.total; t += gridDim.x) {
         if (!mb_wait(&tempty[acc], aph ^ 1, abort_flag, &g_dwp_status, kWaitNs, 64)) break;
         tc_after();
-        const uint32_t d = tmem + (uint32_t)(acc * p.np);
+        const uint32_t d = tmem + (uint32_t)(acc * p.np * (1 + p.cat));
         bool ok = true;
         for (int kb = 0; kb < p.kblocks; ++kb) {
           if (!mb_wait(&afull[j], ph, abort_flag, &g_dwp_status, kWaitNs, 32) ||
@@ -259,13 +264,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a_lo = a_raw + kAHalf;
           const uint32_t b_hi = a_raw + 2 * kAHalf;
           const uint32_t b_lo = b_hi + p.b_bytes;
+          if (p.cat) {
+            // The hi and lo weight tiles are contiguous 128-byte rows: one
+            // N = 2 NP operand.  Columns [0, NP) collect raw*hi + lo*hi,
+            // columns [NP, 2 NP) raw*lo; the epilogue adds the two halves.
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint32_t off = k * 32;  // 8 tf32 along K
-            mma_tf32(d, sw128_desc(a_lo + off), sw128_desc(b_hi + off), p.idesc,
-                     (kb | k) ? 1u : 0u);
-            mma_tf32(d, sw128_desc(a_raw + off), sw128_desc(b_lo + off), p.idesc, 1u);
-            mma_tf32(d, sw128_desc(a_raw + off), sw128_desc(b_hi + off), p.idesc, 1u);
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t off = k * 32;  // 8 tf32 along K
+              mma_tf32(d, sw128_desc(a_raw + off), sw128_desc(b_hi + off), p.idesc2,
+                       (kb | k) ? 1u : 0u);
+              mma_tf32(d, sw128_desc(a_lo + off), sw128_desc(b_hi + off), p.idesc, 1u);
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t off = k * 32;  // 8 tf32 along K
+              mma_tf32(d, sw128_desc(a_lo + off), sw128_desc(b_hi + off), p.idesc,
+                       (kb | k) ? 1u : 0u);
+              mma_tf32(d, sw128_desc(a_raw + off), sw128_desc(b_lo + off), p.idesc, 1u);
+              mma_tf32(d, sw128_desc(a_raw + off), sw128_desc(b_hi + off), p.idesc, 1u);
+            }
           }
           issued = true;
           mma_commit(&empty[j]);
@@ -296,8 +314,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // gave up makes the whole warp leave together.
     const int tid = threadIdx.x;
     const int cg = tid % CG;
-    const int ox_l = (tid / CG) % TW;
-    const int rg = tid / (CG * TW);
+    const int ox_l = ((tid / CG) % (TW / CW)) * CW;  // first of this thread's columns
+    const int rg = tid / (CG * (TW / CW));
     int j = 0, h = 0;
     uint32_t eph = 0, hph = 0;
     int step = 0;
@@ -328,26 +346,30 @@ __global__ void __launch_bounds__(kThreads, 1)
               wr[ky][kx] = *reinterpret_cast<const float2*>(wsm + (ky * KS + kx) * CB + cg * 2);
           const float2 bv = p.bd ? *reinterpret_cast<const float2*>(slot + kBOff + cg * 8)
                                  : make_float2(0.f, 0.f);
-          float2 acc[R];
+          float2 acc[R][CW];
 #pragma unroll
-          for (int r = 0; r < R; ++r) acc[r] = bv;
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int c = 0; c < CW; ++c) acc[r][c] = bv;
 #pragma unroll
           for (int jj = 0; jj < (R - 1) * S + KS; ++jj) {
             const int iy = rg * R * S + jj;
-            float2 row[KS];
+            float2 row[WIN];
 #pragma unroll
-            for (int kx = 0; kx < KS; ++kx)
-              row[kx] = *reinterpret_cast<const float2*>(in + ((iy * IW) + ox_l * S + kx) * CB +
+            for (int ix = 0; ix < WIN; ++ix)
+              row[ix] = *reinterpret_cast<const float2*>(in + ((iy * IW) + ox_l * S + ix) * CB +
                                                          cg * 2);
 #pragma unroll
             for (int r = 0; r < R; ++r) {
               const int ky = jj - r * S;
               if (ky < 0 || ky >= KS) continue;
 #pragma unroll
-              for (int kx = 0; kx < KS; ++kx) {
-                acc[r].x = fmaf(row[kx].x, wr[ky][kx].x, acc[r].x);
-                acc[r].y = fmaf(row[kx].y, wr[ky][kx].y, acc[r].y);
-              }
+              for (int c = 0; c < CW; ++c)
+#pragma unroll
+                for (int kx = 0; kx < KS; ++kx) {
+                  acc[r][c].x = fmaf(row[c * S + kx].x, wr[ky][kx].x, acc[r][c].x);
+                  acc[r][c].y = fmaf(row[c * S + kx].y, wr[ky][kx].y, acc[r][c].y);
+                }
             }
           }
           if (tid == 0 && sub == 0) DWP_TRACE(3, step);
@@ -361,19 +383,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             h = 0;
             hph ^= 1;
           }
-          const int c16 = cl >> 2;  // 16-byte chunk within the 128-byte A row
-          const uint32_t in16 = (uint32_t)(cl & 3) * 4;  // byte offset inside the chunk
+          // GEMM row m = (rg*R + r)*TW + ox_l + c; TW is a multiple of 8, so the
+          // 128-byte swizzle phase m & 7 = (ox_l + c) & 7 does not depend on r.
+          const uint32_t c16s = (uint32_t)(cl >> 2) << 4;  // 16-byte chunk, in bytes
+          const uint32_t in16 = (uint32_t)(cl & 3) * 4;    // byte offset inside the chunk
+          const uint32_t row0 = (uint32_t)((rg * R * TW + ox_l) * 128) + in16;
           with_act(p.act_d, [&](auto tag) {
             constexpr int A = decltype(tag)::value;
+            // Clamped activations cannot produce inf: the lo term needs no
+            // special-value check there.
+            constexpr bool kFinite = A == SPX_ACT_RELU6 || A == SPX_ACT_RELU_N1_TO_1;
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-              const int m = (rg * R + r) * TW + ox_l;  // GEMM row of this pixel
-              float2 v = acc[r];
-              v.x = act_c<A>(v.x);
-              v.y = act_c<A>(v.y);
-              const uint32_t off = (uint32_t)m * 128u + (uint32_t)((c16 ^ (m & 7)) * 16) + in16;
-              *reinterpret_cast<float2*>(a_raw + off) = v;
-              *reinterpret_cast<float2*>(a_lo + off) = make_float2(tf32_lo(v.x), tf32_lo(v.y));
+            for (int c = 0; c < CW; ++c) {
+              const uint32_t colo = row0 + (uint32_t)(c * 128) +
+                                    (c16s ^ ((uint32_t)((ox_l + c) & 7) << 4));
+#pragma unroll
+              for (int r = 0; r < R; ++r) {
+                float2 v = acc[r][c];
+                v.x = act_c<A>(v.x);
+                v.y = act_c<A>(v.y);
+                const uint32_t off = colo + (uint32_t)(r * TW * 128);
+                *reinterpret_cast<float2*>(a_raw + off) = v;
+                *reinterpret_cast<float2*>(a_lo + off) =
+                    kFinite ? make_float2(tf32_lo_finite(v.x), tf32_lo_finite(v.y))
+                            : make_float2(tf32_lo(v.x), tf32_lo(v.y));
+              }
             }
           });
         }
@@ -406,12 +440,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (__any_sync(0xffffffffu, !ok)) break;
       tc_after();
       if (warp == kEpiWarp0 + 2 && lane == 0) DWP_TRACE(6, (t - (int)blockIdx.x) / (int)gridDim.x);
-      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * p.np);
+      const uint32_t tbase =
+          tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * p.np * (1 + p.cat));
       for (int c0 = 0; c0 < p.np; c0 += 32) {
         const int n0 = nt * p.np + c0;
         if (n0 >= p.cout) break;  // uniform across the warp
         float v[32];
         tmem_ld_32x32(tbase + (uint32_t)c0, v);
+        if (p.cat) {
+          float v2[32];
+          tmem_ld_32x32(tbase + (uint32_t)(p.np + c0), v2);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] += v2[e];
+        }
         float4* trow = reinterpret_cast<float4*>(tile + lane * kEpiStride);
 #pragma unroll
         for (int e = 0; e < 8; ++e)
@@ -532,10 +573,12 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
   p.halo_buf = (kSlotBytes + 1023) / 1024 * 1024;
   p.b_bytes = (uint32_t)p.np * 128;
   p.stage_bytes = 2 * kAHalf + 2 * p.b_bytes;
+  p.cat = p.np <= 128 ? 1 : 0;
   uint32_t cols = 32;
-  while (cols < (uint32_t)(2 * p.np)) cols <<= 1;
+  while (cols < (uint32_t)(2 * p.np * (1 + p.cat))) cols <<= 1;
   p.tmem_cols = cols;
   p.idesc = idesc_tf32(128, p.np);
+  p.idesc2 = idesc_tf32(128, 2 * p.np);
   p.wd = wd;
   p.bd = bd;
   p.act_d = q->act_dw;

@@ -148,5 +148,11 @@ __device__ __forceinline__ float tf32_lo(float x) {
   return __uint_as_float((__float_as_uint(r) + 0x1000u) & 0xFFFFE000u);
 }
 
+// The same for a finite x (no special-value check).
+__device__ __forceinline__ float tf32_lo_finite(float x) {
+  const float r = x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+  return __uint_as_float((__float_as_uint(r) + 0x1000u) & 0xFFFFE000u);
+}
+
 }  // namespace sm100
 }  // namespace spx

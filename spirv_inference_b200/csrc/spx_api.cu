@@ -120,6 +120,11 @@ int launch_gemm(cudaStream_t s, int64_t* cnt, const float* a, const float* b, co
       (!split || ((uintptr_t)b_lo & 15) == 0))
     return launch_gemm_tc(s, cnt, a, p->a_ms, bb, split ? b_lo : nullptr, p->b_ns, p->m, p->n,
                           p->k, bias, res, c, p->c_ms, p->alpha, p->activation);
+  // Batched products with a short reduction (attention Q.K^T and P.V).
+  if (g_gemm_path != 1 && !single && b) {
+    const int rc = try_bgemm_tc(s, cnt, a, b, bias, res, c, p);
+    if (rc != -1) return rc;
+  }
   if (g_gemm_path == 2)
     return fail(SPX_ERR_UNSUPPORTED, "gemm: operands not eligible for the tensor-core path");
   return launch_gemm_simt(s, cnt, a, b, bias, res, c, p);
@@ -516,6 +521,8 @@ int64_t spx_get_option(const char* name) {
 static int device_status(const char* what) {
   if (dw_take_status())
     return fail(SPX_ERR_CUDA, "%s: a depthwise tile load wait timed out", what);
+  if (bg_take_status())
+    return fail(SPX_ERR_CUDA, "%s: a batched tensor-core GEMM wait timed out", what);
   if (dwp_take_status())
     return fail(SPX_ERR_CUDA, "%s: a fused depthwise-projection pipeline wait timed out", what);
   if (tc_take_status())

@@ -235,6 +235,11 @@ int launch_weights_split(cudaStream_t s, int64_t* cnt, const float* w, float* hi
 // 1 = a pipeline wait timed out and the kernel aborted its tiles).
 int tc_take_status();
 int dwp_take_status();
+int bg_take_status();
+// Batched 3xTF32 tensor-core GEMM for K <= 128 (k_bgemm.cu): -1 when the
+// operands are not eligible (caller falls back), else SPX_OK or an error.
+int try_bgemm_tc(cudaStream_t s, int64_t* cnt, const float* a, const float* b, const float* bias,
+                 const float* res, float* c, const spx_gemm_params* q);
 // Fused depthwise 3x3 -> 1x1 projection (k_dwproj.cu).  dry_run: eligibility
 // check only (SPX_OK or SPX_ERR_UNSUPPORTED), nothing launched.
 int launch_dw_project(cudaStream_t s, int64_t* cnt, const float* x, const float* wd,

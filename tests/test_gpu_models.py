@@ -39,8 +39,11 @@ def test_fused_executor_matches_oracle(gpu, oracle_outputs, name):
         assert got.shape == ref.shape
         np.testing.assert_array_equal(lowering.top1(got), lowering.top1(ref))
         assert float(np.abs(got - ref).max()) <= SOFTMAX_ATOL
-        # an intermediate feature map, NHWC on the device vs NCHW in the oracle
-        mid = [op.output for op in m.ops if op.type == "DEPTHWISE_CONV_2D"][8]
+        # an intermediate feature map (an expand conv's output: the depthwise
+        # outputs stay on chip in the fused kernel), NHWC on the device vs NCHW
+        # in the oracle
+        mid = [op.inputs[0] for op in m.ops if op.type == "DEPTHWISE_CONV_2D"][8]
+        assert mid not in ex.fused_away
         h, w, c = m.shapes[mid]
         ref_mid = rep["tensors"][mid].reshape(x.shape[0], c, h, w).transpose(0, 2, 3, 1)
         np.testing.assert_allclose(ex.tensor(mid), ref_mid, rtol=1e-3, atol=1e-3)
