@@ -249,6 +249,27 @@ def _ref_config(args, world) -> dict:
             "cuda_graph": False}
 
 
+def run_dry(args) -> None:
+    """The multi-rank plumbing of run_spx without a GPU (CPU tests): gloo
+    process group, barrier, MAX over ranks of a stand-in per-rank step time
+    (1 + rank ms), whole-job throughput, one JSON line from rank 0."""
+    import torch.distributed as dist
+    from spirv_inference_b200.sharding import max_over_ranks, throughput
+    world, rank, _ = dist_setup()
+    if world > 1:
+        dist.init_process_group("gloo")
+        dist.barrier()
+    ms = max_over_ranks(1.0 + rank)
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        print(json.dumps({"metric": METRICS[args.model][0], "value": throughput(args.batch, world, ms),
+                          "unit": METRICS[args.model][1], "n_gpus": world, "ms_per_step": ms,
+                          "config": _config(args, world), "dry_run": True}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def run_spx(args) -> None:
     import torch
 
@@ -674,10 +695,14 @@ def main():
     ap.add_argument("--ref-images", type=int, default=2, help="images per reference-arm step")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--dry-run", action="store_true",
+                    help="exercise the rank plumbing on CPU (tests); no GPU work, no timing")
     args = ap.parse_args()
     if args.batch is None:
         args.batch = DEFAULT_BATCH[args.model]
-    if args.model == "tinyllama":
+    if args.dry_run:
+        run_dry(args)
+    elif args.model == "tinyllama":
         run_llama_reference(args) if args.impl == "reference" else run_llama_spx(args)
     elif args.impl == "reference":
         run_reference(args)

@@ -10,28 +10,28 @@
 // A persistent CTA (one per SM) walks output tiles of TH x TW pixels of one
 // image (128 GEMM rows) and, for each, every 32-channel block of the
 // depthwise width (the GEMM's K):
-//   warp 16     TMA producer: per K block the pre-split projection weights
+//   warp 8      TMA producers: per K block the pre-split projection weights
 //               (hi and lo, NP x 32, 128-byte swizzle) into one of two
 //               stages, and per CB-channel sub-block the input halo box
 //               ((TH-1)*S+3) x ((TW-1)*S+3) x CB into a ring (the tensor map's
 //               zero fill is the depthwise padding);
-//   warps 0-15  builders: the depthwise conv of the sub-block on CUDA cores
+//   warps 0-7   builders: the depthwise conv of the sub-block on CUDA cores
 //               (exact fp32 FMAs, bias and activation fused; a thread owns 2
-//               channels of R rows in one column and reads each input row of
-//               its window once), written straight into the stage's A tile in
+//               channels of R rows x 2 columns and reads each input row of its
+//               window once), written straight into the stage's A tile in
 //               the UMMA K-major 128-byte-swizzled layout: the raw value (the
 //               MMA's tf32 hi) and its tf32 lo term.  The depthwise taps and
 //               bias of the sub-block arrive in the same halo slot (TMA).
 //               Each builder warp hands a slot back after its lanes' reads
 //               (__syncwarp, then one elected proxy fence + arrive), so the
 //               TMA refill cannot overtake a slow lane;
-//   warp 17     MMA issuer: 3xTF32 (lo*hi + hi*lo + hi*hi) tcgen05.mma into one
+//   warp 9      MMA issuer: 3xTF32 (lo*hi + hi*lo + hi*hi) tcgen05.mma into one
 //               of two TMEM accumulators (NP columns each), a commit per K
 //               block frees the stage, a commit per tile hands the
 //               accumulator to the epilogue;
-//   warps 18-21 epilogue: TMEM lane quarter -> registers -> padded shared tile
-//               -> projection bias, residual, activation -> whole 128-byte
-//               channel runs of the NHWC output.
+//   warps 10-13 epilogue: TMEM lane quarter -> registers (a lane = an output
+//               pixel, 32 channels) -> projection bias, residual, activation
+//               -> one contiguous 128-byte channel run of the NHWC output.
 // HBM traffic per tile: the halo (interior read once; the overlap between
 // neighbouring tiles mostly hits L2), the output, and the residual.
 //
@@ -71,8 +71,6 @@ constexpr int kProdWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kEpiWarp0 = 10;
 constexpr int kThreads = 14 * 32;
-constexpr int kEpiStride = 36;                  // floats per row of an epilogue tile
-constexpr uint32_t kEpiTileBytes = 32 * kEpiStride * 4;
 constexpr uint32_t kAHalf = 128 * 32 * 4;        // one 128 x 32 fp32 A tile: 16 KB
 constexpr unsigned long long kWaitNs = 2000000000ull;
 constexpr unsigned long long kDrainNs = 200000000ull;
@@ -124,8 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* halo = smem;
   uint8_t* stages = halo + (size_t)p.hst * p.halo_buf;
-  float* epi = (float*)(stages + 2 * (size_t)p.stage_bytes);
-  uint64_t* hfull = (uint64_t*)((uint8_t*)epi + 4 * kEpiTileBytes);
+  uint64_t* hfull = (uint64_t*)(stages + 2 * (size_t)p.stage_bytes);
   uint64_t* hempty = hfull + kMaxHalo;
   uint64_t* afull = hempty + kMaxHalo;
   uint64_t* bfull = afull + 2;
@@ -427,10 +424,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
     }
   } else {
-    // ---------------- epilogue (warps 18-21) ----------------
+    // ---------------- epilogue (warps 10-13) ----------------
+    // A lane owns one GEMM row (one output pixel): tcgen05.ld gives it 32
+    // consecutive output channels, which it writes (with bias, residual and
+    // activation) as one contiguous 128-byte run of the NHWC output.
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    float* tile = epi + (warp - kEpiWarp0) * (32 * kEpiStride);
-    const int sub_r = lane >> 3, sub_c = (lane & 7) * 4;
     int acc = 0;
     uint32_t aph = 0;
     for (int t = blockIdx.x; t < p.total; t += gridDim.x) {
@@ -442,9 +440,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (warp == kEpiWarp0 + 2 && lane == 0) DWP_TRACE(6, (t - (int)blockIdx.x) / (int)gridDim.x);
       const uint32_t tbase =
           tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * p.np * (1 + p.cat));
+      const int m = q * 32 + lane;
+      const int oy = ty * TH + m / TW, ox = tx * TW + m % TW;
+      const bool live = m < TH * TW && oy < p.oh && ox < p.ow;
+      const int64_t pix = live ? ((int64_t)img * p.oh + oy) * p.ow + ox : 0;
       for (int c0 = 0; c0 < p.np; c0 += 32) {
         const int n0 = nt * p.np + c0;
         if (n0 >= p.cout) break;  // uniform across the warp
+        const int nv = min(32, p.cout - n0);  // live channels of this chunk (a multiple of 4)
         float v[32];
         tmem_ld_32x32(tbase + (uint32_t)c0, v);
         if (p.cat) {
@@ -453,41 +456,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] += v2[e];
         }
-        float4* trow = reinterpret_cast<float4*>(tile + lane * kEpiStride);
+        const int64_t base = pix * p.cout + n0;
+        float4 r4[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e)
-          trow[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
-        __syncwarp();
-        const int n = n0 + sub_c;
-        const bool nlive = n < p.cout;
-        const float4 b4 = (nlive && p.bp) ? __ldg(reinterpret_cast<const float4*>(p.bp + n))
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-        // All eight residual loads are issued before any store.
-        float4 r4[8];
-        int64_t off[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int m = q * 32 + i * 4 + sub_r;
-          const int oy = ty * TH + m / TW, ox = tx * TW + m % TW;
-          const bool v = m < TH * TW && oy < p.oh && ox < p.ow && nlive;
-          off[i] = v ? (((int64_t)img * p.oh + oy) * p.ow + ox) * p.cout + n : -1;
-          r4[i] = (v && p.res) ? __ldg(reinterpret_cast<const float4*>(p.res + off[i]))
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+          r4[e] = (live && p.res && 4 * e < nv)
+                      ? __ldg(reinterpret_cast<const float4*>(p.res + base) + e)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
         with_act(p.act_p, [&](auto tag) {
           constexpr int A = decltype(tag)::value;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            if (off[i] < 0) continue;
-            float4 o = *reinterpret_cast<const float4*>(tile + (i * 4 + sub_r) * kEpiStride + sub_c);
-            o.x = act_c<A>(o.x + b4.x + r4[i].x);
-            o.y = act_c<A>(o.y + b4.y + r4[i].y);
-            o.z = act_c<A>(o.z + b4.z + r4[i].z);
-            o.w = act_c<A>(o.w + b4.w + r4[i].w);
-            *reinterpret_cast<float4*>(p.y + off[i]) = o;
+          for (int e = 0; e < 8; ++e) {
+            if (!live || 4 * e >= nv) continue;
+            const float4 b4 = p.bp ? __ldg(reinterpret_cast<const float4*>(p.bp + n0) + e)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 o;
+            o.x = act_c<A>(v[4 * e + 0] + b4.x + r4[e].x);
+            o.y = act_c<A>(v[4 * e + 1] + b4.y + r4[e].y);
+            o.z = act_c<A>(v[4 * e + 2] + b4.z + r4[e].z);
+            o.w = act_c<A>(v[4 * e + 3] + b4.w + r4[e].w);
+            reinterpret_cast<float4*>(p.y + base)[e] = o;
           }
         });
-        __syncwarp();
       }
       tc_before();
       mb_arrive(&tempty[acc]);
@@ -586,7 +576,7 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
   p.res = res;
   p.y = y;
   p.act_p = q->act_proj;
-  const uint32_t fixed = 1024 + 2 * p.stage_bytes + 4 * kEpiTileBytes + 256;
+  const uint32_t fixed = 1024 + 2 * p.stage_bytes + 256;
   const uint32_t cap = 227 * 1024;
   int hst = 0;
   while (hst < 3 && fixed + (uint32_t)(hst + 1) * p.halo_buf <= cap) ++hst;

@@ -54,3 +54,27 @@ def test_max_over_ranks_gloo_two_ranks():
         out = mgr.dict()
         mp.spawn(_worker, args=(2, port, out), nprocs=2, join=True)
         assert dict(out) == {0: 11.0, 1: 11.0}
+
+
+def test_bench_rank_plumbing_two_gloo_ranks():
+    """bench.py under the driver's torchrun launch line, two ranks, --dry-run:
+    exactly one JSON line (rank 0), the slowest rank's time, the whole-job
+    throughput and the per-GPU batch of the config."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parent.parent
+    port = _free_port()
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                        "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port",
+                        str(port), str(root / "bench.py"), "--gpus", "2", "--dry-run"],
+                       capture_output=True, text=True, timeout=300, cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, r.stdout
+    d = json.loads(lines[0])
+    assert d["n_gpus"] == 2 and d["dry_run"] is True
+    assert d["ms_per_step"] == 2.0                      # max over ranks (1 + rank)
+    assert d["value"] == pytest.approx(2 * 256 / 0.002)
+    assert d["config"]["batch_per_gpu"] == 256 and d["config"]["global_batch"] == 512
