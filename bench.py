@@ -49,14 +49,17 @@ DEFAULT_BATCH = {"mobilenet_v2": 256, "efficientnet_lite0": 64, "resnet50": 256,
 LLAMA_PROMPT, LLAMA_NEW = 32, 20
 
 
-def build_model(name: str, batch: int, graph, seed_rank: int):
-    """(executor, host input) for a config; inputs are this rank's shard."""
+def build_model(name: str, batch: int, graph, seed_rank: int, unfused: bool = False):
+    """(executor, host input) for a config; inputs are this rank's shard.
+    unfused: the CNN step without the fused depthwise->projection kernel and
+    with the CUDA-core stem (the kernels the fused path replaces)."""
     from spirv_inference_b200 import nets, nets_hlo
     from spirv_inference_b200.sharding import shard_seed
     if name in ("mobilenet_v2", "efficientnet_lite0"):
         from spirv_inference_b200.executor import CnnExecutor
         model = nets.MODELS[name](seed=0)
-        ex = CnnExecutor(model, batch=batch, graph=graph)
+        ex = CnnExecutor(model, batch=batch, graph=graph, fuse_dw_project=not unfused,
+                         tc_stem=not unfused)
         return ex, nets.make_input(model, batch, seed=shard_seed(1000, seed_rank))
     from spirv_inference_b200.executor_hlo import HloExecutor
     if name == "resnet50":
@@ -233,7 +236,10 @@ def _config(args, world) -> dict:
     return {"workload": f"{_WORKLOADS.get(args.model, args.model)}, batch {args.batch} per GPU",
             "batch_per_gpu": args.batch, "global_batch": args.batch * world,
             "parallelism": f"dp{world} (batch-sharded replicas, no collective)",
-            "l2": l2, "cuda_graph": True}
+            "l2": l2, "cuda_graph": True,
+            "kernels": ("unfused (depthwise and projection as separate kernels, CUDA-core stem)"
+                        if getattr(args, "unfused", False) else
+                        "fused depthwise->projection, tensor-core stem")}
 
 
 def _ref_config(args, world) -> dict:
@@ -286,7 +292,7 @@ def run_spx(args) -> None:
     stream = torch.cuda.Stream()  # a real stream: the legacy default stream cannot be captured
     torch.cuda.set_stream(stream)
     g = Graph(local, stream=stream.cuda_stream)
-    ex, x = build_model(args.model, B, g, rank)  # x: this rank's shard of the global batch
+    ex, x = build_model(args.model, B, g, rank, unfused=args.unfused)  # this rank's shard
     g.upload(ex.input, x)
     ex.capture()
 
@@ -695,6 +701,8 @@ def main():
     ap.add_argument("--ref-images", type=int, default=2, help="images per reference-arm step")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--unfused", action="store_true",
+                    help="CNN step without the fused depthwise->projection and tensor-core stem")
     ap.add_argument("--dry-run", action="store_true",
                     help="exercise the rank plumbing on CPU (tests); no GPU work, no timing")
     args = ap.parse_args()

@@ -183,6 +183,8 @@ _SIGS = {
     "spx_ar_destroy": ([c_void_p], c_int),
     "spx_op_dw_project_nhwc": ([c_void_p] + [c_void_p] * 8 + [POINTER(DwProjParams)], c_int),
     "spx_dw_project_supported": ([POINTER(DwProjParams)], c_int),
+    "spx_op_stem_conv_nhwc": ([c_void_p] * 6 + [POINTER(ConvParams)], c_int),
+    "spx_stem_conv_supported": ([POINTER(ConvParams)], c_int),
     "spx_op_expand_dw_nhwc": ([c_void_p] + [c_void_p] * 6 + [POINTER(ExpandDwParams)], c_int),
     "spx_op_expand_dw_nhwc_split": ([c_void_p] + [c_void_p] * 8 + [POINTER(ExpandDwParams)],
                                     c_int),

@@ -94,7 +94,11 @@ struct DwpArgs {
   int act_p;
 };
 
-template <int KS, int S, int TH, int TW, int CB, int R>
+// STEM = true: the same pipeline with an im2col builder for a 3x3 stride-2
+// convolution over 3-channel NHWC input (the CNN stems, K = 27 padded to
+// one 32-wide K block): the halo slot is a 3-D box of whole input rows
+// (W * 3 floats), the builders gather each pixel's 27 taps into its A row.
+template <int KS, int S, int TH, int TW, int CB, int R, bool STEM = false>
 __global__ void __launch_bounds__(kThreads, 1)
     dwproj_kernel(const __grid_constant__ CUtensorMap tmX,
                   const __grid_constant__ CUtensorMap tmBhi,
@@ -103,18 +107,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const __grid_constant__ CUtensorMap tmBd, const DwpArgs p) {
   constexpr int IH = (TH - 1) * S + KS, IW = (TW - 1) * S + KS;
   constexpr int CG = CB / 2;  // channel pairs per sub-block
-  constexpr int SUBS = 32 / CB;
+  constexpr int SUBS = STEM ? 1 : 32 / CB;
   constexpr int CW = 2;       // output columns per builder thread
   constexpr int WIN = (CW - 1) * S + KS;  // input columns a thread's window spans
-  constexpr uint32_t kHaloBytes = IH * IW * CB * 4;
+  // Stem rows: IW pixels x 3 channels, plus up to 3 floats of 16-byte alignment
+  // shift, rounded to whole 16-byte units.
+  constexpr int kStemRow = (IW * 3 + 3 + 3) / 4 * 4;
+  constexpr uint32_t kHaloBytes = STEM ? IH * kStemRow * 4 : IH * IW * CB * 4;
   // A halo slot: the input box, then the sub-block's depthwise taps [KS*KS][CB]
   // and its bias [CB] (TMA boxes of the weight tensors; zero past c).
   constexpr uint32_t kWOff = (kHaloBytes + 127) / 128 * 128;
   constexpr uint32_t kWBytes = KS * KS * CB * 4;
   constexpr uint32_t kBOff = kWOff + (kWBytes + 127) / 128 * 128;  // TMA: 128-byte aligned
-  const uint32_t slot_tx = kHaloBytes + kWBytes + (p.bd ? CB * 4 : 0);
-  static_assert(CG * (TW / CW) * (TH / R) == kBuildWarps * 32,
+  const uint32_t slot_tx = STEM ? kHaloBytes : kHaloBytes + kWBytes + (p.bd ? CB * 4 : 0);
+  static_assert(STEM || CG * (TW / CW) * (TH / R) == kBuildWarps * 32,
                 "one builder thread per (rows, column pair, channel pair)");
+  static_assert(!STEM || (TH * TW == 128 && S == 2 && KS == 3), "stem tile");
   static_assert(TH * TW <= 128, "a tile is at most 128 GEMM rows");
   static_assert(TH % R == 0 && 32 % CB == 0, "tile shape");
 
@@ -191,9 +199,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint8_t* slot = halo + (size_t)h * p.halo_buf;
             const int c0 = kb * 32 + sub * CB;
             mb_expect_tx(&hfull[h], slot_tx);
-            tma_4d(slot, &tmX, &hfull[h], c0, x0, y0, img);
-            tma_2d(slot + kWOff, &tmWd, &hfull[h], c0, 0);
-            if (p.bd) tma_2d(slot + kBOff, &tmBd, &hfull[h], c0, 0);
+            if constexpr (STEM) {
+              // whole rows of W * 3 floats; the start rounded down to 16 bytes
+              tma_3d(slot, &tmX, &hfull[h], (x0 * 3) & ~3, y0, img);
+            } else {
+              tma_4d(slot, &tmX, &hfull[h], c0, x0, y0, img);
+              tma_2d(slot + kWOff, &tmWd, &hfull[h], c0, 0);
+              if (p.bd) tma_2d(slot + kBOff, &tmBd, &hfull[h], c0, 0);
+            }
             h_armed |= 1u << h;
             h_par = (h_par & ~(1u << h)) | (hph << h);
             if (++h == p.hst) {
@@ -302,7 +315,62 @@ __global__ void __launch_bounds__(kThreads, 1)
         mb_wait(drain, 0, &never, &g_dwp_status, kDrainNs, 64);
       }
     }
-  } else if (warp < kBuildWarps) {
+  } else if (STEM && warp < kBuildWarps) {
+    // ---------------- builders (stem): im2col -> A tile (raw, lo) ----------------
+    // Thread: GEMM row m (pixel) and half of its 32 K columns; k = (ky*3+kx)*3+c
+    // (OHWI weight order), zero for k >= 27.
+    const int tid = threadIdx.x;
+    const int m = tid & 127, khalf = tid >> 7;
+    const int oy_l = m / TW, ox_l = m % TW;
+    int j = 0, h = 0;
+    uint32_t eph = 0, hph = 0;
+    for (int t = blockIdx.x; t < p.total; t += gridDim.x) {
+      int nt, img, ty, tx;
+      decode(t, nt, img, ty, tx);
+      const int shift = (tx * TW * S - p.pl) * 3 - (((tx * TW * S - p.pl) * 3) & ~3);
+      bool ok = __all_sync(0xffffffffu,
+                           mb_wait(&empty[j], eph ^ 1, abort_flag, &g_dwp_status, kWaitNs, 64));
+      if (!ok) break;
+      ok = __all_sync(0xffffffffu, mb_wait(&hfull[h], hph, abort_flag, &g_dwp_status, kWaitNs, 32));
+      if (!ok) break;
+      const float* in = reinterpret_cast<const float*>(halo + (size_t)h * p.halo_buf);
+      float vals[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int k = khalf * 16 + e;
+        const int ky = k / 9, kx = (k / 3) % 3, c = k % 3;
+        vals[e] = k < 27 ? in[(oy_l * S + ky) * kStemRow + shift + (ox_l * S + kx) * 3 + c] : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mb_arrive(&hempty[h]);
+      }
+      if (++h == p.hst) {
+        h = 0;
+        hph ^= 1;
+      }
+      uint8_t* a_raw = stages + (size_t)j * p.stage_bytes;
+      uint8_t* a_lo = a_raw + kAHalf;
+#pragma unroll
+      for (int qd = 0; qd < 4; ++qd) {
+        const int c16 = khalf * 4 + qd;
+        const uint32_t off = (uint32_t)m * 128u + (uint32_t)((c16 ^ (m & 7)) * 16);
+        const float4 v = make_float4(vals[4 * qd], vals[4 * qd + 1], vals[4 * qd + 2],
+                                     vals[4 * qd + 3]);
+        *reinterpret_cast<float4*>(a_raw + off) = v;
+        *reinterpret_cast<float4*>(a_lo + off) =
+            make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mb_arrive(&afull[j]);
+      if (++j == 2) {
+        j = 0;
+        eph ^= 1;
+      }
+    }
+  } else if (!STEM && warp < kBuildWarps) {
     // ---------------- builders: depthwise conv -> A tile (raw, lo) ----------------
     // Warps run independently; each hands a halo slot back after its lanes'
     // reads (__syncwarp, then one elected proxy fence + arrive: the TMA
@@ -645,6 +713,86 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
 
 bool al16(const void* v) { return ((uintptr_t)v & 15) == 0; }
 
+// The stem instantiation: 8 x 16 output pixels per tile, one 32-wide K block.
+constexpr int kStemTH = 8, kStemTW = 16;
+
+int launch_stem(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
+                const float* w_lo, const float* bias, float* y, const spx_conv_params* q) {
+  constexpr int IH = (kStemTH - 1) * 2 + 3, IW = (kStemTW - 1) * 2 + 3;
+  constexpr int kRow = (IW * 3 + 3 + 3) / 4 * 4;
+  constexpr uint32_t kHalo = IH * kRow * 4;
+  DwpArgs p{};
+  p.n = q->n;
+  p.ih = q->ih;
+  p.iw = q->iw;
+  p.ce = 32;
+  p.oh = q->oh;
+  p.ow = q->ow;
+  p.cout = q->oc;
+  p.n_ntiles = 1;
+  p.np = (int)ceil_div(q->oc, 32) * 32;
+  p.pt = q->pad_top;
+  p.pl = q->pad_left;
+  p.tiles_h = (int)ceil_div(q->oh, kStemTH);
+  p.tiles_w = (int)ceil_div(q->ow, kStemTW);
+  p.kblocks = 1;
+  const int64_t total = (int64_t)q->n * p.tiles_h * p.tiles_w;
+  if (total > INT32_MAX) return fail(SPX_ERR_UNSUPPORTED, "stem: too many tiles");
+  p.total = (int)total;
+  p.halo_buf = (kHalo + 1023) / 1024 * 1024;
+  p.b_bytes = (uint32_t)p.np * 128;
+  p.stage_bytes = 2 * kAHalf + 2 * p.b_bytes;
+  p.cat = p.np <= 128 ? 1 : 0;
+  uint32_t cols = 32;
+  while (cols < (uint32_t)(2 * p.np * (1 + p.cat))) cols <<= 1;
+  p.tmem_cols = cols;
+  p.idesc = idesc_tf32(128, p.np);
+  p.idesc2 = idesc_tf32(128, 2 * p.np);
+  p.bp = bias;
+  p.y = y;
+  p.act_p = q->activation;
+  const uint32_t fixed = 1024 + 2 * p.stage_bytes + 256;
+  const uint32_t cap = 227 * 1024;
+  int hst = 0;
+  while (hst < 4 && fixed + (uint32_t)(hst + 1) * p.halo_buf <= cap) ++hst;
+  p.hst = hst;
+  const uint32_t smem = fixed + (uint32_t)hst * p.halo_buf;
+  EncodeFn fn = encoder();
+  if (!fn) return fail(SPX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  CUtensorMap mx, mh, ml;
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)q->iw * 3, (cuuint64_t)q->ih, (cuuint64_t)q->n};
+    cuuint64_t strides[2] = {(cuuint64_t)q->iw * 12, (cuuint64_t)q->ih * q->iw * 12};
+    cuuint32_t box[3] = {(cuuint32_t)kRow, (cuuint32_t)IH, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = fn(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)x, dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SPX_ERR_CUDA, "stem: input map encode failed (%d)", (int)r);
+  }
+  for (int b = 0; b < 2; ++b) {
+    cuuint64_t dims[2] = {32, (cuuint64_t)q->oc};
+    cuuint64_t strides[1] = {128};
+    cuuint32_t box[2] = {32, (cuuint32_t)p.np};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(b ? &ml : &mh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)(b ? w_lo : w_hi),
+                    dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SPX_ERR_CUDA, "stem: weight map encode failed (%d)", (int)r);
+  }
+  auto kern = dwproj_kernel<3, 2, kStemTH, kStemTW, 32, 4, true>;
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [&] {
+    attr = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+  });
+  if (attr != cudaSuccess) return check_cuda(attr, "stem: smem attribute");
+  const int grid = (int)(p.total < num_sms() ? p.total : num_sms());
+  kern<<<grid, kThreads, smem, s>>>(mx, mh, ml, mx, mx, p);
+  return after_launch(cnt, "stem_tc");
+}
+
 }  // namespace
 
 #ifdef SPX_DWP_TRACE
@@ -664,6 +812,25 @@ int dwp_take_status() {
     cudaMemcpyToSymbol(g_dwp_status, &zero, sizeof(int));
   }
   return v;
+}
+
+// 3x3 stride-2 convolution of 3-channel NHWC input on the tensor cores (the
+// CNN stems).  w_hi / w_lo: [oc][32] tf32 split of the OHWI weights flattened
+// to 27 taps and zero-padded to 32.  SPX_ERR_UNSUPPORTED for other shapes.
+int launch_stem_tc(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
+                   const float* w_lo, const float* bias, float* y, const spx_conv_params* q,
+                   bool dry_run) {
+  if (!q) return fail(SPX_ERR_INVALID_ARGUMENT, "stem: null params");
+  if (q->ic != 3 || q->kh != 3 || q->kw != 3 || q->stride_h != 2 || q->stride_w != 2 ||
+      q->dilation_h != 1 || q->dilation_w != 1 || q->oc <= 0 || q->oc > 128 || q->oc % 4 ||
+      q->iw % 4 || q->n <= 0 || q->oh <= 0 || q->ow <= 0 || q->pad_top < 0 || q->pad_left < 0 ||
+      q->pad_top > 2 || q->pad_left > 2)
+    return fail(SPX_ERR_UNSUPPORTED, "stem: 3x3 stride-2 over 3 channels (iw % 4 == 0, oc <= 128) only");
+  if (dry_run) return SPX_OK;
+  if (!x || !w_hi || !w_lo || !y || !al16(x) || !al16(w_hi) || !al16(w_lo) || !al16(y) ||
+      (bias && !al16(bias)))
+    return fail(SPX_ERR_INVALID_ARGUMENT, "stem: null or unaligned tensor");
+  return launch_stem(s, cnt, x, w_hi, w_lo, bias, y, q);
 }
 
 // Returns SPX_ERR_UNSUPPORTED (without launching) for shapes the fused kernel

@@ -72,6 +72,14 @@ __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, uint64
       "l"(reinterpret_cast<uint64_t>(map)), "r"(sa(bar)), "r"(x), "r"(y)
       : "memory");
 }
+__device__ __forceinline__ void tma_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                       int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(sa(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(sa(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
 __device__ __forceinline__ void tma_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0,
                                        int c1, int c2, int c3) {
   asm volatile(

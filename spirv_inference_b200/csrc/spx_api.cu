@@ -857,6 +857,19 @@ int spx_op_dw_project_nhwc(spx_graph* g, const float* x, const float* w_dw, cons
                            residual, y, p, false);
 }
 
+int spx_op_stem_conv_nhwc(spx_graph* g, const float* x, const float* w_hi, const float* w_lo,
+                          const float* bias, float* y, const spx_conv_params* p) {
+  SPX_G(g);
+  return launch_stem_tc(g->stream, &g->launches, x, w_hi, w_lo, bias, y, p, false);
+}
+
+int spx_stem_conv_supported(const spx_conv_params* p) {
+  return launch_stem_tc(nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, p, true) ==
+                 SPX_OK
+             ? 1
+             : 0;
+}
+
 int spx_dw_project_supported(const spx_dwproj_params* p) {
   return launch_dw_project(nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
                            nullptr, nullptr, nullptr, p, true) == SPX_OK

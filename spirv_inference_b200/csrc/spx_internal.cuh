@@ -242,6 +242,9 @@ int try_bgemm_tc(cudaStream_t s, int64_t* cnt, const float* a, const float* b, c
                  const float* res, float* c, const spx_gemm_params* q);
 // Fused depthwise 3x3 -> 1x1 projection (k_dwproj.cu).  dry_run: eligibility
 // check only (SPX_OK or SPX_ERR_UNSUPPORTED), nothing launched.
+int launch_stem_tc(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
+                   const float* w_lo, const float* bias, float* y, const spx_conv_params* q,
+                   bool dry_run);
 int launch_dw_project(cudaStream_t s, int64_t* cnt, const float* x, const float* wd,
                       const float* bd, const float* w_hi, const float* w_lo, const float* bp,
                       const float* res, float* y, const spx_dwproj_params* q, bool dry_run);

@@ -42,13 +42,15 @@ class _Shape:
 class CnnExecutor:
     def __init__(self, model: Model, batch: int, device: int = 0, graph: Graph | None = None,
                  fuse_residual: bool = True, presplit: bool = True,
-                 fuse_expand_dw: bool = False, fuse_dw_project: bool = True):
+                 fuse_expand_dw: bool = False, fuse_dw_project: bool = True,
+                 tc_stem: bool = True):
         self.model = model
         self.batch = batch
         self.g = graph or Graph(device)
         self.fuse_residual = fuse_residual
         self.fuse_expand_dw = fuse_expand_dw
         self.fuse_dw_project = fuse_dw_project and presplit
+        self.tc_stem = tc_stem and presplit
         self.fused_away: set[str] = set()   # tensors that never reach HBM
         self.presplit = presplit
         self._splits: dict = {}
@@ -218,6 +220,14 @@ class CnnExecutor:
                 pt, pl = same_padding_offsets(a["padding"], ih, iw, oh, ow, kh, kw, *a["stride"])
                 pointwise = (kh, kw) == (1, 1) and tuple(a["stride"]) == (1, 1)
                 split = self._split(op.inputs[1]) if pointwise else None
+                if (self.tc_stem and res is None and (kh, kw) == (3, 3) and x.shape[3] == 3
+                        and self.g.stem_supported(x, y, stride=tuple(a["stride"]), pad=(pt, pl),
+                                                  activation=a.get("activation", 0))):
+                    self._plan.append(("stem", dict(
+                        x=x, w=w, w_split=self.g.stem_weights(m.weights[op.inputs[1]]),
+                        bias=self.w[op.inputs[2]], y=y, stride=tuple(a["stride"]), pad=(pt, pl),
+                        activation=a.get("activation", 0))))
+                    continue
                 self._plan.append(("conv", dict(x=x, w=w, bias=self.w[op.inputs[2]], y=y,
                                                 stride=a["stride"], pad=(pt, pl),
                                                 activation=a.get("activation", 0),
@@ -274,6 +284,9 @@ class CnnExecutor:
                 g.expand_dw_nhwc(p["x"], p["we"], p["be"], p["wd"], p["bd"], p["y"],
                                  stride=p["stride"], pad=p["pad"], act_expand=p["act_e"],
                                  act_dw=p["act_d"], w_split=p["we_split"])
+            elif kind == "stem":
+                g.stem_conv_nhwc(p["x"], p["w_split"], p["bias"], p["y"], stride=p["stride"],
+                                 pad=p["pad"], activation=p["activation"])
             elif kind == "dwproj":
                 g.dw_project_nhwc(p["x"], p["wd"], p["bd"], p["w_split"], p["bp"], p["y"],
                                   stride=p["stride"], pad=p["pad"], act_dw=p["act_dw"],
@@ -302,11 +315,12 @@ class CnnExecutor:
         written once, fp32)."""
         out = []
         for kind, p in self._plan:
-            if kind == "conv":
+            if kind in ("conv", "stem"):
                 x, w, y = p["x"], p["w"], p["y"]
                 k = w.shape[1] * w.shape[2] * w.shape[3]
                 f = 2 * y.size * k
-                b = x.size + w.size + y.shape[-1] + y.size + (y.size if p["residual"] else 0)
+                b = (x.size + w.size + y.shape[-1] + y.size
+                     + (y.size if p.get("residual") is not None else 0))
                 label = f"conv{w.shape[1]}x{w.shape[2]}"
             elif kind == "expand_dw":
                 x, y, we = p["x"], p["y"], p["we"]

@@ -127,3 +127,29 @@ def test_fused_forward_is_deterministic(gpu):
             np.testing.assert_array_equal(ex.forward(x), first)
     finally:
         ex.close()
+
+
+@pytest.mark.parametrize("n,ih,iw,oc,pad", [(2, 224, 224, 32, (0, 0)), (3, 16, 16, 32, (1, 1)),
+                                             (1, 37, 20, 16, (1, 0))])
+def test_stem_conv_matches_float64(g, n, ih, iw, oc, pad):
+    """The tensor-core stem (3x3 stride 2 over 3 channels, im2col on chip,
+    3xTF32) against float64, with ReLU6; pads 0 / 1 exercise the 16-byte
+    rounding of the row box start."""
+    oh, ow = -(-ih // 2), -(-iw // 2)
+    x = _r(n, ih, iw, 3, scale=2.0)
+    w = _r(oc, 3, 3, 3, scale=0.5)
+    b = _r(oc, scale=0.1)
+    dx, dy = g.tensor(x), g.alloc((n, oh, ow, oc))
+    assert g.stem_supported(dx, dy, pad=pad, activation=_lib.ACT_RELU6)
+    g.stem_conv_nhwc(dx, g.stem_weights(w), g.tensor(b), dy, pad=pad,
+                     activation=_lib.ACT_RELU6)
+    ref = np.clip(R.conv_nhwc(x, w.transpose(1, 2, 3, 0), (2, 2), pad, (oh, ow)) + b, 0, 6)
+    got = dy.download()
+    assert np.abs(got - ref).max() / np.abs(ref).max() <= 2.5e-8 * 27 + 1e-6
+
+
+def test_stem_rejects_other_shapes(g):
+    x, y = g.alloc((1, 16, 18, 3)), g.alloc((1, 8, 9, 32))
+    assert not g.stem_supported(x, y)                     # iw % 4
+    x2, y2 = g.alloc((1, 16, 16, 4)), g.alloc((1, 8, 8, 32))
+    assert not g.stem_supported(x2, y2)                   # 4 input channels
