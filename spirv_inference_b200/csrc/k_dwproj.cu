@@ -70,7 +70,9 @@ constexpr int kBuildWarps = 8;
 constexpr int kProdWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kEpiWarp0 = 10;
-constexpr int kThreads = 14 * 32;
+constexpr int kEpiGroups = 2;  // epilogue groups of 4 warps, draining alternate tiles
+constexpr int kThreads = (kEpiWarp0 + 4 * kEpiGroups) * 32;
+constexpr uint32_t kEStage = 128 * 128;  // 128 rows x 32 fp32
 constexpr uint32_t kAHalf = 128 * 32 * 4;        // one 128 x 32 fp32 A tile: 16 KB
 constexpr unsigned long long kWaitNs = 2000000000ull;
 constexpr unsigned long long kDrainNs = 200000000ull;
@@ -98,13 +100,35 @@ struct DwpArgs {
 // convolution over 3-channel NHWC input (the CNN stems, K = 27 padded to
 // one 32-wide K block): the halo slot is a 3-D box of whole input rows
 // (W * 3 floats), the builders gather each pixel's 27 taps into its A row.
+// Named barrier over one epilogue group (4 warps); ids 1 and 2.
+__device__ __forceinline__ void group_sync(int grp) {
+  asm volatile("bar.sync %0, 128;" ::"r"(1 + grp) : "memory");
+}
+// AND of `p` over one epilogue group (the same named barrier): every exit
+// from the group's loop is taken by all 128 threads together, so none is
+// left waiting at a barrier the others never reach.
+__device__ __forceinline__ bool group_all(int grp, bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred a, b;\n\t"
+      "setp.ne.u32 a, %1, 0;\n\t"
+      "barrier.red.and.pred b, %2, 128, a;\n\t"
+      "selp.u32 %0, 1, 0, b;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)p), "r"(1 + grp)
+      : "memory");
+  return r != 0;
+}
+
 template <int KS, int S, int TH, int TW, int CB, int R, bool STEM = false>
 __global__ void __launch_bounds__(kThreads, 1)
     dwproj_kernel(const __grid_constant__ CUtensorMap tmX,
                   const __grid_constant__ CUtensorMap tmBhi,
                   const __grid_constant__ CUtensorMap tmBlo,
                   const __grid_constant__ CUtensorMap tmWd,
-                  const __grid_constant__ CUtensorMap tmBd, const DwpArgs p) {
+                  const __grid_constant__ CUtensorMap tmBd,
+                  const __grid_constant__ CUtensorMap tmY,
+                  const __grid_constant__ CUtensorMap tmR, const DwpArgs p) {
   constexpr int IH = (TH - 1) * S + KS, IW = (TW - 1) * S + KS;
   constexpr int CG = CB / 2;  // channel pairs per sub-block
   constexpr int SUBS = STEM ? 1 : 32 / CB;
@@ -130,7 +154,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* halo = smem;
   uint8_t* stages = halo + (size_t)p.hst * p.halo_buf;
-  uint64_t* hfull = (uint64_t*)(stages + 2 * (size_t)p.stage_bytes);
+  // Epilogue staging: one 128-row x 32-channel tile per group, 128-byte
+  // swizzled (the TMA store / residual load box layout).
+  uint8_t* estage = stages + 2 * (size_t)p.stage_bytes;
+  uint64_t* hfull = (uint64_t*)(estage + kEpiGroups * (size_t)kEStage);
   uint64_t* hempty = hfull + kMaxHalo;
   uint64_t* afull = hempty + kMaxHalo;
   uint64_t* bfull = afull + 2;
@@ -138,7 +165,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull = empty + 2;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+  uint64_t* rfull = drain + 1;  // [kEpiGroups]: residual box landed
+  uint32_t* tmem_slot = (uint32_t*)(rfull + kEpiGroups);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -155,6 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mb_init(&tempty[j], 4 * 32);
     }
     mb_init(drain, 1);
+    for (int g2 = 0; g2 < kEpiGroups; ++g2) mb_init(&rfull[g2], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -331,8 +360,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = __all_sync(0xffffffffu,
                            mb_wait(&empty[j], eph ^ 1, abort_flag, &g_dwp_status, kWaitNs, 64));
       if (!ok) break;
+      const int st_i = (t - (int)blockIdx.x) / (int)gridDim.x;
+      if (tid == 0) DWP_TRACE(1, st_i);
       ok = __all_sync(0xffffffffu, mb_wait(&hfull[h], hph, abort_flag, &g_dwp_status, kWaitNs, 32));
       if (!ok) break;
+      if (tid == 0) DWP_TRACE(2, st_i);
       const float* in = reinterpret_cast<const float*>(halo + (size_t)h * p.halo_buf);
       float vals[16];
 #pragma unroll
@@ -365,6 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mb_arrive(&afull[j]);
+      if (tid == 0) DWP_TRACE(4, st_i);
       if (++j == 2) {
         j = 0;
         eph ^= 1;
@@ -496,26 +529,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     // A lane owns one GEMM row (one output pixel): tcgen05.ld gives it 32
     // consecutive output channels, which it writes (with bias, residual and
     // activation) as one contiguous 128-byte run of the NHWC output.
+    // Group g (warps 10+4g .. 13+4g) drains the CTA's tiles of parity g, which
+    // the MMA issuer puts in accumulator g: two tiles drain at once.
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    int acc = 0;
-    uint32_t aph = 0;
-    for (int t = blockIdx.x; t < p.total; t += gridDim.x) {
+    const int grp = (warp - kEpiWarp0) / 4;
+    const int acc = grp;
+    const bool issuer = warp == kEpiWarp0 + 4 * grp && lane == 0;  // the group's TMA thread
+    uint8_t* stg = estage + (size_t)grp * kEStage;
+    uint32_t aph = 0, rph = 0;
+    bool ok_all = true;
+    for (int t = blockIdx.x + grp * gridDim.x; t < p.total; t += kEpiGroups * gridDim.x) {
       int nt, img, ty, tx;
       decode(t, nt, img, ty, tx);
-      const bool ok = mb_wait(&tfull[acc], aph, abort_flag, &g_dwp_status, kWaitNs, 128);
-      if (__any_sync(0xffffffffu, !ok)) break;
+      const bool ok = group_all(grp, mb_wait(&tfull[acc], aph, abort_flag, &g_dwp_status,
+                                             kWaitNs, 128));
+      if (!ok) break;
       tc_after();
       if (warp == kEpiWarp0 + 2 && lane == 0) DWP_TRACE(6, (t - (int)blockIdx.x) / (int)gridDim.x);
       const uint32_t tbase =
           tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * p.np * (1 + p.cat));
-      const int m = q * 32 + lane;
-      const int oy = ty * TH + m / TW, ox = tx * TW + m % TW;
-      const bool live = m < TH * TW && oy < p.oh && ox < p.ow;
-      const int64_t pix = live ? ((int64_t)img * p.oh + oy) * p.ow + ox : 0;
+      const int m = q * 32 + lane;  // this lane's GEMM row (pixel of the tile)
       for (int c0 = 0; c0 < p.np; c0 += 32) {
         const int n0 = nt * p.np + c0;
-        if (n0 >= p.cout) break;  // uniform across the warp
-        const int nv = min(32, p.cout - n0);  // live channels of this chunk (a multiple of 4)
+        if (n0 >= p.cout) break;  // uniform across the group
+        // Accumulator chunk into registers first; meanwhile the issuer makes
+        // sure its previous store has read the staging tile and loads the
+        // residual box (if any) into it.
         float v[32];
         tmem_ld_32x32(tbase + (uint32_t)c0, v);
         if (p.cat) {
@@ -524,37 +563,58 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] += v2[e];
         }
-        const int64_t base = pix * p.cout + n0;
-        float4 r4[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          r4[e] = (live && p.res && 4 * e < nv)
-                      ? __ldg(reinterpret_cast<const float4*>(p.res + base) + e)
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (issuer) {
+          bulk_wait_read0();
+          if (p.res) {
+            mb_expect_tx(&rfull[grp], (uint32_t)(TH * TW * 128));
+            tma_4d(stg, &tmR, &rfull[grp], n0, tx * TW, ty * TH, img);
+          }
+        }
+        group_sync(grp);
+        if (warp == kEpiWarp0 + 2 && lane == 0 && c0 == 0)
+          DWP_TRACE(11, (t - (int)blockIdx.x) / (int)gridDim.x);
+        if (p.res) {
+          const bool rok = group_all(
+              grp, mb_wait(&rfull[grp], rph, abort_flag, &g_dwp_status, kWaitNs, 64));
+          rph ^= 1;
+          if (!rok) {
+            ok_all = false;
+            break;
+          }
+        }
+        float4* row = reinterpret_cast<float4*>(stg + m * 128);
         with_act(p.act_p, [&](auto tag) {
           constexpr int A = decltype(tag)::value;
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            if (!live || 4 * e >= nv) continue;
-            const float4 b4 = p.bp ? __ldg(reinterpret_cast<const float4*>(p.bp + n0) + e)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            const int ch = n0 + 4 * e;
+            const float4 b4 = (p.bp && ch < p.cout)
+                                  ? __ldg(reinterpret_cast<const float4*>(p.bp + ch))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 r4 = p.res ? row[e ^ (m & 7)] : make_float4(0.f, 0.f, 0.f, 0.f);
             float4 o;
-            o.x = act_c<A>(v[4 * e + 0] + b4.x + r4[e].x);
-            o.y = act_c<A>(v[4 * e + 1] + b4.y + r4[e].y);
-            o.z = act_c<A>(v[4 * e + 2] + b4.z + r4[e].z);
-            o.w = act_c<A>(v[4 * e + 3] + b4.w + r4[e].w);
-            reinterpret_cast<float4*>(p.y + base)[e] = o;
+            o.x = act_c<A>(v[4 * e + 0] + b4.x + r4.x);
+            o.y = act_c<A>(v[4 * e + 1] + b4.y + r4.y);
+            o.z = act_c<A>(v[4 * e + 2] + b4.z + r4.z);
+            o.w = act_c<A>(v[4 * e + 3] + b4.w + r4.w);
+            row[e ^ (m & 7)] = o;
           }
         });
+        // Generic-proxy writes of the tile become visible to the TMA store.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        group_sync(grp);
+        if (issuer) {
+          tma_store_4d(&tmY, stg, n0, tx * TW, ty * TH, img);  // clips rows / columns off the map
+          bulk_commit();
+        }
       }
+      if (!ok_all) break;
       tc_before();
       mb_arrive(&tempty[acc]);
       if (warp == kEpiWarp0 + 2 && lane == 0) DWP_TRACE(7, (t - (int)blockIdx.x) / (int)gridDim.x);
-      if (++acc == 2) {
-        acc = 0;
-        aph ^= 1;
-      }
+      aph ^= 1;
     }
+    if (issuer) bulk_wait_all();  // this group's stores have completed
   }
 
   tc_before();
@@ -583,6 +643,22 @@ EncodeFn encoder() {
       fn = (EncodeFn)q;
   });
   return fn;
+}
+
+// Output (and residual) NHWC [n][oh][ow][cout]: 32-channel x TW x TH boxes,
+// 128-byte swizzle (the epilogue staging layout).  Boxes past the map or past
+// cout are clipped on store and zero-filled on load.
+int out_map(EncodeFn fn, CUtensorMap* m, const float* t, int n, int oh, int ow, int cout, int th,
+            int tw) {
+  cuuint64_t dims[4] = {(cuuint64_t)cout, (cuuint64_t)ow, (cuuint64_t)oh, (cuuint64_t)n};
+  cuuint64_t strides[3] = {(cuuint64_t)cout * 4, (cuuint64_t)ow * cout * 4,
+                           (cuuint64_t)oh * ow * cout * 4};
+  cuuint32_t box[4] = {32, (cuuint32_t)tw, (cuuint32_t)th, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)t, dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SPX_OK : fail(SPX_ERR_CUDA, "output map encode failed (%d)", (int)r);
 }
 
 int num_sms() {
@@ -644,7 +720,7 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
   p.res = res;
   p.y = y;
   p.act_p = q->act_proj;
-  const uint32_t fixed = 1024 + 2 * p.stage_bytes + 256;
+  const uint32_t fixed = 1024 + 2 * p.stage_bytes + kEpiGroups * kEStage + 256;
   const uint32_t cap = 227 * 1024;
   int hst = 0;
   while (hst < 3 && fixed + (uint32_t)(hst + 1) * p.halo_buf <= cap) ++hst;
@@ -657,7 +733,12 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
 
   EncodeFn fn = encoder();
   if (!fn) return fail(SPX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  CUtensorMap mx, mh, ml, mw, mb;
+  CUtensorMap mx, mh, ml, mw, mb, my, mr;
+  if (int rc = out_map(fn, &my, y, q->n, q->oh, q->ow, q->cout, TH, TW)) return rc;
+  mr = my;
+  if (res) {
+    if (int rc = out_map(fn, &mr, res, q->n, q->oh, q->ow, q->cout, TH, TW)) return rc;
+  }
   {
     cuuint64_t dims[4] = {(cuuint64_t)q->c, (cuuint64_t)q->iw, (cuuint64_t)q->ih,
                           (cuuint64_t)q->n};
@@ -707,11 +788,12 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
   });
   if (attr != cudaSuccess) return check_cuda(attr, "dw_project: smem attribute");
   const int grid = (int)(p.total < num_sms() ? p.total : num_sms());
-  kern<<<grid, kThreads, smem, s>>>(mx, mh, ml, mw, mb, p);
+  kern<<<grid, kThreads, smem, s>>>(mx, mh, ml, mw, mb, my, mr, p);
   return after_launch(cnt, "dw_project");
 }
 
 bool al16(const void* v) { return ((uintptr_t)v & 15) == 0; }
+
 
 // The stem instantiation: 8 x 16 output pixels per tile, one 32-wide K block.
 constexpr int kStemTH = 8, kStemTW = 16;
@@ -751,7 +833,7 @@ int launch_stem(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
   p.bp = bias;
   p.y = y;
   p.act_p = q->activation;
-  const uint32_t fixed = 1024 + 2 * p.stage_bytes + 256;
+  const uint32_t fixed = 1024 + 2 * p.stage_bytes + kEpiGroups * kEStage + 256;
   const uint32_t cap = 227 * 1024;
   int hst = 0;
   while (hst < 4 && fixed + (uint32_t)(hst + 1) * p.halo_buf <= cap) ++hst;
@@ -759,7 +841,8 @@ int launch_stem(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
   const uint32_t smem = fixed + (uint32_t)hst * p.halo_buf;
   EncodeFn fn = encoder();
   if (!fn) return fail(SPX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  CUtensorMap mx, mh, ml;
+  CUtensorMap mx, mh, ml, my;
+  if (int rc = out_map(fn, &my, y, q->n, q->oh, q->ow, q->oc, kStemTH, kStemTW)) return rc;
   {
     cuuint64_t dims[3] = {(cuuint64_t)q->iw * 3, (cuuint64_t)q->ih, (cuuint64_t)q->n};
     cuuint64_t strides[2] = {(cuuint64_t)q->iw * 12, (cuuint64_t)q->ih * q->iw * 12};
@@ -789,7 +872,7 @@ int launch_stem(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
   });
   if (attr != cudaSuccess) return check_cuda(attr, "stem: smem attribute");
   const int grid = (int)(p.total < num_sms() ? p.total : num_sms());
-  kern<<<grid, kThreads, smem, s>>>(mx, mh, ml, mx, mx, p);
+  kern<<<grid, kThreads, smem, s>>>(mx, mh, ml, mx, mx, my, my, p);
   return after_launch(cnt, "stem_tc");
 }
 
