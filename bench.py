@@ -358,6 +358,14 @@ def run_spx(args) -> None:
                         "achieved_gbs": round(d["bytes"] / (d["ms"] / 1e3) / 1e9, 1),
                         "achieved_tflops": round(d["flops"] / (d["ms"] / 1e3) / 1e12, 2),
                         "hbm_roof_frac": round(t_mem / d["ms"], 4)}
+    if args.per_op:
+        # one line per recorded kernel on stderr: label, output shape, us, GB/s
+        plan = getattr(ex, "_plan", None) or [(c["kind"], {}) for c in costs]
+        for (kind, pl), c, t in zip(plan, costs, times):
+            y = pl.get("y")
+            shape = tuple(y.shape) if y is not None else ()
+            print(f"per_op {c['label']:12s} {str(shape):24s} {t * 1000:9.1f} us "
+                  f"{c['bytes'] / (t / 1e3) / 1e9:8.0f} GB/s", file=sys.stderr)
     top = max(classes, key=lambda k: classes[k]["ms"])
     d = classes[top]
     per_launch_bytes = d["bytes"] / d["launches"]
@@ -701,6 +709,8 @@ def main():
     ap.add_argument("--ref-images", type=int, default=2, help="images per reference-arm step")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--per-op", action="store_true",
+                    help="print each kernel's eager-pass time to stderr")
     ap.add_argument("--unfused", action="store_true",
                     help="CNN step without the fused depthwise->projection and tensor-core stem")
     ap.add_argument("--dry-run", action="store_true",
