@@ -120,7 +120,7 @@ __device__ __forceinline__ bool group_all(int grp, bool p) {
   return r != 0;
 }
 
-template <int KS, int S, int TH, int TW, int CB, int R, bool STEM = false>
+template <int KS, int S, int TH, int TW, int CB, int R, bool STEM = false, int TN = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     dwproj_kernel(const __grid_constant__ CUtensorMap tmX,
                   const __grid_constant__ CUtensorMap tmBhi,
@@ -137,17 +137,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Stem rows: IW pixels x 3 channels, plus up to 3 floats of 16-byte alignment
   // shift, rounded to whole 16-byte units.
   constexpr int kStemRow = (IW * 3 + 3 + 3) / 4 * 4;
-  constexpr uint32_t kHaloBytes = STEM ? IH * kStemRow * 4 : IH * IW * CB * 4;
+  constexpr uint32_t kHaloBytes = STEM ? IH * kStemRow * 4 : TN * IH * IW * CB * 4;
+  constexpr int kTilePx = TN * TH * TW;  // GEMM rows of a tile (TN images of TH x TW)
   // A halo slot: the input box, then the sub-block's depthwise taps [KS*KS][CB]
   // and its bias [CB] (TMA boxes of the weight tensors; zero past c).
   constexpr uint32_t kWOff = (kHaloBytes + 127) / 128 * 128;
   constexpr uint32_t kWBytes = KS * KS * CB * 4;
   constexpr uint32_t kBOff = kWOff + (kWBytes + 127) / 128 * 128;  // TMA: 128-byte aligned
   const uint32_t slot_tx = STEM ? kHaloBytes : kHaloBytes + kWBytes + (p.bd ? CB * 4 : 0);
-  static_assert(STEM || CG * (TW / CW) * (TH / R) == kBuildWarps * 32,
-                "one builder thread per (rows, column pair, channel pair)");
+  static_assert(STEM || TN * CG * (TW / CW) * (TH / R) == kBuildWarps * 32,
+                "one builder thread per (image, rows, column pair, channel pair)");
   static_assert(!STEM || (TH * TW == 128 && S == 2 && KS == 3), "stem tile");
-  static_assert(TH * TW <= 128, "a tile is at most 128 GEMM rows");
+  static_assert(TN * TH * TW <= 128, "a tile is at most 128 GEMM rows");
+  static_assert(!STEM || TN == 1, "stem tiles hold one image");
   static_assert(TH % R == 0 && 32 % CB == 0, "tile shape");
 
   extern __shared__ uint8_t smem_raw[];
@@ -204,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tx = r % p.tiles_w;
     r /= p.tiles_w;
     ty = r % p.tiles_h;
-    img = r / p.tiles_h;
+    img = (r / p.tiles_h) * TN;  // first image of the tile
   };
 
   if (warp == kProdWarp) {
@@ -413,7 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tid = threadIdx.x;
     const int cg = tid % CG;
     const int ox_l = ((tid / CG) % (TW / CW)) * CW;  // first of this thread's columns
-    const int rg = tid / (CG * (TW / CW));
+    const int rg = (tid / (CG * (TW / CW))) % (TH / R);
+    const int im = tid / (CG * (TW / CW) * (TH / R));  // image of the tile
     int j = 0, h = 0;
     uint32_t eph = 0, hph = 0;
     int step = 0;
@@ -434,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
           if (tid == 0 && sub == 0) DWP_TRACE(2, step);
           const uint8_t* slot = halo + (size_t)h * p.halo_buf;
-          const float* in = reinterpret_cast<const float*>(slot);
+          const float* in = reinterpret_cast<const float*>(slot) + im * (IH * IW * CB);
           const float* wsm = reinterpret_cast<const float*>(slot + kWOff);
           float2 wr[KS][KS];
 #pragma unroll
@@ -485,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // 128-byte swizzle phase m & 7 = (ox_l + c) & 7 does not depend on r.
           const uint32_t c16s = (uint32_t)(cl >> 2) << 4;  // 16-byte chunk, in bytes
           const uint32_t in16 = (uint32_t)(cl & 3) * 4;    // byte offset inside the chunk
-          const uint32_t row0 = (uint32_t)((rg * R * TW + ox_l) * 128) + in16;
+          const uint32_t row0 = (uint32_t)((im * TH * TW + rg * R * TW + ox_l) * 128) + in16;
           with_act(p.act_d, [&](auto tag) {
             constexpr int A = decltype(tag)::value;
             // Clamped activations cannot produce inf: the lo term needs no
@@ -566,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (issuer) {
           bulk_wait_read0();
           if (p.res) {
-            mb_expect_tx(&rfull[grp], (uint32_t)(TH * TW * 128));
+            mb_expect_tx(&rfull[grp], (uint32_t)(kTilePx * 128));
             tma_4d(stg, &tmR, &rfull[grp], n0, tx * TW, ty * TH, img);
           }
         }
@@ -649,11 +652,11 @@ EncodeFn encoder() {
 // 128-byte swizzle (the epilogue staging layout).  Boxes past the map or past
 // cout are clipped on store and zero-filled on load.
 int out_map(EncodeFn fn, CUtensorMap* m, const float* t, int n, int oh, int ow, int cout, int th,
-            int tw) {
+            int tw, int tn = 1) {
   cuuint64_t dims[4] = {(cuuint64_t)cout, (cuuint64_t)ow, (cuuint64_t)oh, (cuuint64_t)n};
   cuuint64_t strides[3] = {(cuuint64_t)cout * 4, (cuuint64_t)ow * cout * 4,
                            (cuuint64_t)oh * ow * cout * 4};
-  cuuint32_t box[4] = {32, (cuuint32_t)tw, (cuuint32_t)th, 1};
+  cuuint32_t box[4] = {32, (cuuint32_t)tw, (cuuint32_t)th, (cuuint32_t)tn};
   cuuint32_t es[4] = {1, 1, 1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)t, dims, strides, box, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -677,12 +680,12 @@ struct DwpCfg {
   int th, tw, cb;
 };
 
-template <int KS, int S, int TH, int TW, int CB, int R>
+template <int KS, int S, int TH, int TW, int CB, int R, int TN = 1>
 int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, const float* bd,
                const float* w_hi, const float* w_lo, const float* bp, const float* res, float* y,
                const spx_dwproj_params* q, bool dry_run, uint32_t* smem_out) {
   constexpr int IH = (TH - 1) * S + KS, IW = (TW - 1) * S + KS;
-  constexpr uint32_t kHaloBytes = IH * IW * CB * 4;
+  constexpr uint32_t kHaloBytes = TN * IH * IW * CB * 4;
   DwpArgs p{};
   p.n = q->n;
   p.ih = q->ih;
@@ -699,7 +702,7 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
   p.tiles_h = (int)ceil_div(q->oh, TH);
   p.tiles_w = (int)ceil_div(q->ow, TW);
   p.kblocks = (int)ceil_div(q->c, 32);
-  const int64_t total = (int64_t)p.n_ntiles * q->n * p.tiles_h * p.tiles_w;
+  const int64_t total = (int64_t)p.n_ntiles * ceil_div(q->n, TN) * p.tiles_h * p.tiles_w;
   if (total > INT32_MAX) return fail(SPX_ERR_UNSUPPORTED, "dw_project: too many tiles");
   p.total = (int)total;
   constexpr uint32_t kSlotBytes =
@@ -734,17 +737,17 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
   EncodeFn fn = encoder();
   if (!fn) return fail(SPX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   CUtensorMap mx, mh, ml, mw, mb, my, mr;
-  if (int rc = out_map(fn, &my, y, q->n, q->oh, q->ow, q->cout, TH, TW)) return rc;
+  if (int rc = out_map(fn, &my, y, q->n, q->oh, q->ow, q->cout, TH, TW, TN)) return rc;
   mr = my;
   if (res) {
-    if (int rc = out_map(fn, &mr, res, q->n, q->oh, q->ow, q->cout, TH, TW)) return rc;
+    if (int rc = out_map(fn, &mr, res, q->n, q->oh, q->ow, q->cout, TH, TW, TN)) return rc;
   }
   {
     cuuint64_t dims[4] = {(cuuint64_t)q->c, (cuuint64_t)q->iw, (cuuint64_t)q->ih,
                           (cuuint64_t)q->n};
     cuuint64_t strides[3] = {(cuuint64_t)q->c * 4, (cuuint64_t)q->iw * q->c * 4,
                              (cuuint64_t)q->ih * q->iw * q->c * 4};
-    cuuint32_t box[4] = {(cuuint32_t)CB, (cuuint32_t)IW, (cuuint32_t)IH, 1};
+    cuuint32_t box[4] = {(cuuint32_t)CB, (cuuint32_t)IW, (cuuint32_t)IH, (cuuint32_t)TN};
     cuuint32_t es[4] = {1, 1, 1, 1};
     CUresult r = fn(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)x, dims, strides, box, es,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -780,7 +783,7 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
     if (r != CUDA_SUCCESS)
       return fail(SPX_ERR_CUDA, "dw_project: depthwise weight map encode failed (%d)", (int)r);
   }
-  auto kern = dwproj_kernel<KS, S, TH, TW, CB, R>;
+  auto kern = dwproj_kernel<KS, S, TH, TW, CB, R, false, TN>;
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [&] {
@@ -945,7 +948,7 @@ int launch_dw_project(cudaStream_t s, int64_t* cnt, const float* x, const float*
   }
   if (q->stride == 1) {
     if (q->ow <= 8)
-      return launch_cfg<3, 1, 8, 8, 32, 2>(s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run,
+      return launch_cfg<3, 1, 8, 8, 16, 2, 2>(s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run,
                                            nullptr);
     return launch_cfg<3, 1, 8, 16, 32, 4>(s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run,
                                           nullptr);

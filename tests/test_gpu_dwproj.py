@@ -43,6 +43,8 @@ CASES = [
     (2, 14, 576, 2, 160, False),   # 7x7 output: the narrow-map tile
     (3, 7, 960, 1, 160, True),
     (2, 7, 960, 1, 320, False),    # two n tiles of 160
+    (1, 7, 64, 1, 32, True),       # a two-image 7x7 tile with its second image absent
+    (5, 6, 48, 1, 40, True),       # 6x6 maps, odd image count
     (1, 9, 40, 1, 52, False),      # c and cout not multiples of 32
 ]
 
