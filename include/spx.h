@@ -101,6 +101,10 @@ int spx_device_status(void);
  * alternate tiles; 0 = never.
  * "tc_conv_groups": 2 (default) = tensor-core GEMMs with several k-blocks per
  * tile split two stages at once (two converter groups), 1 = one at a time.
+ * "pw_gemm": 1 = pointwise convolutions with pre-split weights, a reduction of
+ * at most 160 and at least 128 outputs keep each 128-row activation tile
+ * resident (split once for every n tile); 0 (default) = the row-tiled
+ * tensor-core GEMM, measured faster on every MobileNetV2 expand layer.
  * "ar_wait_limit_us": bound of the peer all-reduce's wait for the other ranks
  * (default 2,000,000; 1,000 .. 60,000,000).
  * "tc_lo_tmem": 1 = with pre-split weights and several k-blocks the

@@ -51,7 +51,7 @@ __device__ int g_dwp_status = 0;
 
 #ifdef SPX_DWP_TRACE
 // Development-only timeline of CTA 0 (not compiled into the library).
-__device__ unsigned long long g_dwp_trace[12][256];
+__device__ unsigned long long g_dwp_trace[16][256];
 #define DWP_TRACE(ev, i)                                                         \
   do {                                                                           \
     if (blockIdx.x == 0 && (i) < 256) g_dwp_trace[ev][i] = sm100::gtime();      \
@@ -72,7 +72,8 @@ constexpr int kMmaWarp = 9;
 constexpr int kEpiWarp0 = 10;
 constexpr int kEpiGroups = 2;  // epilogue groups of 4 warps, draining alternate tiles
 constexpr int kThreads = (kEpiWarp0 + 4 * kEpiGroups) * 32;
-constexpr uint32_t kEStage = 128 * 128;  // 128 rows x 32 fp32
+constexpr uint32_t kEWarp = 32 * 128;                     // one warp's 32 rows x 32 fp32
+constexpr uint32_t kEStage = 4 * kEWarp;                   // a group's staging (16 KB)
 constexpr uint32_t kAHalf = 128 * 32 * 4;        // one 128 x 32 fp32 A tile: 16 KB
 constexpr unsigned long long kWaitNs = 2000000000ull;
 constexpr unsigned long long kDrainNs = 200000000ull;
@@ -100,26 +101,6 @@ struct DwpArgs {
 // convolution over 3-channel NHWC input (the CNN stems, K = 27 padded to
 // one 32-wide K block): the halo slot is a 3-D box of whole input rows
 // (W * 3 floats), the builders gather each pixel's 27 taps into its A row.
-// Named barrier over one epilogue group (4 warps); ids 1 and 2.
-__device__ __forceinline__ void group_sync(int grp) {
-  asm volatile("bar.sync %0, 128;" ::"r"(1 + grp) : "memory");
-}
-// AND of `p` over one epilogue group (the same named barrier): every exit
-// from the group's loop is taken by all 128 threads together, so none is
-// left waiting at a barrier the others never reach.
-__device__ __forceinline__ bool group_all(int grp, bool p) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred a, b;\n\t"
-      "setp.ne.u32 a, %1, 0;\n\t"
-      "barrier.red.and.pred b, %2, 128, a;\n\t"
-      "selp.u32 %0, 1, 0, b;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)p), "r"(1 + grp)
-      : "memory");
-  return r != 0;
-}
-
 template <int KS, int S, int TH, int TW, int CB, int R, bool STEM = false, int TN = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     dwproj_kernel(const __grid_constant__ CUtensorMap tmX,
@@ -167,8 +148,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull = empty + 2;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* rfull = drain + 1;  // [kEpiGroups]: residual box landed
-  uint32_t* tmem_slot = (uint32_t*)(rfull + kEpiGroups);
+  uint64_t* rfull = drain + 1;  // [4 * kEpiGroups]: a warp's residual box landed
+  uint32_t* tmem_slot = (uint32_t*)(rfull + 4 * kEpiGroups);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -185,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mb_init(&tempty[j], 4 * 32);
     }
     mb_init(drain, 1);
-    for (int g2 = 0; g2 < kEpiGroups; ++g2) mb_init(&rfull[g2], 1);
+    for (int w2 = 0; w2 < 4 * kEpiGroups; ++w2) mb_init(&rfull[w2], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -533,81 +514,94 @@ __global__ void __launch_bounds__(kThreads, 1)
     // consecutive output channels, which it writes (with bias, residual and
     // activation) as one contiguous 128-byte run of the NHWC output.
     // Group g (warps 10+4g .. 13+4g) drains the CTA's tiles of parity g, which
-    // the MMA issuer puts in accumulator g: two tiles drain at once.
+    // the MMA issuer puts in accumulator g: two tiles drain at once.  Each
+    // warp owns its 32 rows end to end: its own 4 KB staging tile, its own
+    // residual box and TMA store (32 channels x TW x 32/TW rows), so warps
+    // never wait on one another.
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int grp = (warp - kEpiWarp0) / 4;
     const int acc = grp;
-    const bool issuer = warp == kEpiWarp0 + 4 * grp && lane == 0;  // the group's TMA thread
-    uint8_t* stg = estage + (size_t)grp * kEStage;
+    uint8_t* stg = estage + (size_t)(warp - kEpiWarp0) * kEWarp;
+    uint64_t* rbar = &rfull[warp - kEpiWarp0];
+    const int row0 = q * 32;                     // first GEMM row of this warp
+    const int w_im = row0 / (TH * TW);           // image of the tile these rows are in
+    const int w_oy = (row0 % (TH * TW)) / TW;    // their first output row in the tile
+    const bool w_live = row0 < kTilePx;          // rows past a 64-row tile are padding
     uint32_t aph = 0, rph = 0;
     bool ok_all = true;
     for (int t = blockIdx.x + grp * gridDim.x; t < p.total; t += kEpiGroups * gridDim.x) {
       int nt, img, ty, tx;
       decode(t, nt, img, ty, tx);
-      const bool ok = group_all(grp, mb_wait(&tfull[acc], aph, abort_flag, &g_dwp_status,
-                                             kWaitNs, 128));
+      const bool ok = __all_sync(0xffffffffu, mb_wait(&tfull[acc], aph, abort_flag,
+                                                      &g_dwp_status, kWaitNs, 128));
       if (!ok) break;
       tc_after();
       if (warp == kEpiWarp0 + 2 && lane == 0) DWP_TRACE(6, (t - (int)blockIdx.x) / (int)gridDim.x);
       const uint32_t tbase =
           tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * p.np * (1 + p.cat));
-      const int m = q * 32 + lane;  // this lane's GEMM row (pixel of the tile)
+      const int ox0 = tx * TW, oy0 = ty * TH + w_oy, im = img + w_im;
       for (int c0 = 0; c0 < p.np; c0 += 32) {
         const int n0 = nt * p.np + c0;
-        if (n0 >= p.cout) break;  // uniform across the group
-        // Accumulator chunk into registers first; meanwhile the issuer makes
-        // sure its previous store has read the staging tile and loads the
-        // residual box (if any) into it.
+        if (n0 >= p.cout) break;  // uniform
         float v[32];
         tmem_ld_32x32(tbase + (uint32_t)c0, v);
+        if (warp == kEpiWarp0 + 2 && lane == 0 && c0 == 0)
+          DWP_TRACE(12, (t - (int)blockIdx.x) / (int)gridDim.x);
         if (p.cat) {
           float v2[32];
           tmem_ld_32x32(tbase + (uint32_t)(p.np + c0), v2);
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] += v2[e];
         }
-        if (issuer) {
-          bulk_wait_read0();
+        if (warp == kEpiWarp0 + 2 && lane == 0 && c0 == 0)
+          DWP_TRACE(13, (t - (int)blockIdx.x) / (int)gridDim.x);
+        if (lane == 0 && w_live) {
+          bulk_wait_read0();  // this warp's previous store has read the staging tile
           if (p.res) {
-            mb_expect_tx(&rfull[grp], (uint32_t)(kTilePx * 128));
-            tma_4d(stg, &tmR, &rfull[grp], n0, tx * TW, ty * TH, img);
+            mb_expect_tx(rbar, kEWarp);
+            tma_4d(stg, &tmR, rbar, n0, ox0, oy0, im);
           }
         }
-        group_sync(grp);
+        __syncwarp();
         if (warp == kEpiWarp0 + 2 && lane == 0 && c0 == 0)
           DWP_TRACE(11, (t - (int)blockIdx.x) / (int)gridDim.x);
-        if (p.res) {
-          const bool rok = group_all(
-              grp, mb_wait(&rfull[grp], rph, abort_flag, &g_dwp_status, kWaitNs, 64));
+        if (p.res && w_live) {
+          const bool rok = __all_sync(0xffffffffu, mb_wait(rbar, rph, abort_flag, &g_dwp_status,
+                                                           kWaitNs, 64));
           rph ^= 1;
           if (!rok) {
             ok_all = false;
             break;
           }
         }
-        float4* row = reinterpret_cast<float4*>(stg + m * 128);
+        float4* row = reinterpret_cast<float4*>(stg + lane * 128);
+        // Bias first, all eight loads in flight before any staging store.
+        float4 b4[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          b4[e] = (p.bp && n0 + 4 * e < p.cout)
+                      ? __ldg(reinterpret_cast<const float4*>(p.bp + n0) + e)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
         with_act(p.act_p, [&](auto tag) {
           constexpr int A = decltype(tag)::value;
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const int ch = n0 + 4 * e;
-            const float4 b4 = (p.bp && ch < p.cout)
-                                  ? __ldg(reinterpret_cast<const float4*>(p.bp + ch))
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float4 r4 = p.res ? row[e ^ (m & 7)] : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 r4 = p.res ? row[e ^ (lane & 7)] : make_float4(0.f, 0.f, 0.f, 0.f);
             float4 o;
-            o.x = act_c<A>(v[4 * e + 0] + b4.x + r4.x);
-            o.y = act_c<A>(v[4 * e + 1] + b4.y + r4.y);
-            o.z = act_c<A>(v[4 * e + 2] + b4.z + r4.z);
-            o.w = act_c<A>(v[4 * e + 3] + b4.w + r4.w);
-            row[e ^ (m & 7)] = o;
+            o.x = act_c<A>(v[4 * e + 0] + b4[e].x + r4.x);
+            o.y = act_c<A>(v[4 * e + 1] + b4[e].y + r4.y);
+            o.z = act_c<A>(v[4 * e + 2] + b4[e].z + r4.z);
+            o.w = act_c<A>(v[4 * e + 3] + b4[e].w + r4.w);
+            row[e ^ (lane & 7)] = o;
           }
         });
+        if (warp == kEpiWarp0 + 2 && lane == 0 && c0 == 0)
+          DWP_TRACE(14, (t - (int)blockIdx.x) / (int)gridDim.x);
         // Generic-proxy writes of the tile become visible to the TMA store.
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        group_sync(grp);
-        if (issuer) {
-          tma_store_4d(&tmY, stg, n0, tx * TW, ty * TH, img);  // clips rows / columns off the map
+        __syncwarp();
+        if (lane == 0 && w_live) {
+          tma_store_4d(&tmY, stg, n0, ox0, oy0, im);  // clipped at the map edges and cout
           bulk_commit();
         }
       }
@@ -617,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (warp == kEpiWarp0 + 2 && lane == 0) DWP_TRACE(7, (t - (int)blockIdx.x) / (int)gridDim.x);
       aph ^= 1;
     }
-    if (issuer) bulk_wait_all();  // this group's stores have completed
+    if (lane == 0) bulk_wait_all();  // this warp's stores have completed
   }
 
   tc_before();
@@ -648,15 +642,18 @@ EncodeFn encoder() {
   return fn;
 }
 
-// Output (and residual) NHWC [n][oh][ow][cout]: 32-channel x TW x TH boxes,
-// 128-byte swizzle (the epilogue staging layout).  Boxes past the map or past
+// Output (and residual) NHWC [n][oh][ow][cout]: 32-channel x TW x 32/TW-row
+// boxes (one epilogue warp's rows), 128-byte swizzle (its staging layout).  Boxes past the map or past
 // cout are clipped on store and zero-filled on load.
 int out_map(EncodeFn fn, CUtensorMap* m, const float* t, int n, int oh, int ow, int cout, int th,
             int tw, int tn = 1) {
   cuuint64_t dims[4] = {(cuuint64_t)cout, (cuuint64_t)ow, (cuuint64_t)oh, (cuuint64_t)n};
   cuuint64_t strides[3] = {(cuuint64_t)cout * 4, (cuuint64_t)ow * cout * 4,
                            (cuuint64_t)oh * ow * cout * 4};
-  cuuint32_t box[4] = {32, (cuuint32_t)tw, (cuuint32_t)th, (cuuint32_t)tn};
+  // one epilogue warp's 32 rows: TW columns x 32 / TW rows of one image
+  (void)th;
+  (void)tn;
+  cuuint32_t box[4] = {32, (cuuint32_t)tw, (cuuint32_t)(32 / tw), 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)t, dims, strides, box, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

@@ -89,6 +89,14 @@ __device__ __forceinline__ void tma_4d(void* dst, const CUtensorMap* map, uint64
       : "memory");
 }
 
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0,
+                                             int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(sa(src))
+      : "memory");
+}
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0,
                                              int c1, int c2, int c3) {
   asm volatile(

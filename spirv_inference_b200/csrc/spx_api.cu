@@ -44,6 +44,7 @@ int g_gemm_path = 0;
 int64_t g_ar_wait_limit_us = 2000000;
 int g_dw_path = 0;
 int g_pw_path = 0;
+int g_pw_gemm = 0;
 
 // ---- algorithm selection for dense contractions ---------------------------
 int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
@@ -75,6 +76,13 @@ int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* 
     // GEMM on every MobileNetV2 layer, so off by default.
     if (g_gemm_path == 0 && g_pw_path == 1 && pw_simt_eligible(x, y, res, M, p->ic, p->oc))
       return launch_pw_simt(s, cnt, x, w, bias, res, y, M, p->ic, p->oc, p->activation);
+    // Wide outputs over short reductions: the activation tile stays resident
+    // and is split once for all n tiles.
+    if (g_pw_gemm && split) {
+      const int rc = try_pwgemm(s, cnt, x, w_hi, w_lo, bias, res, y, M, p->oc, p->ic,
+                                p->activation);
+      if (rc != -1) return rc;
+    }
     if (gemm_tc_eligible(x, p->ic, wb, p->ic, M, p->oc, p->ic, y, p->oc) &&
         (!split || ((uintptr_t)w_lo & 15) == 0))
       return launch_gemm_tc(s, cnt, x, p->ic, wb, split ? w_lo : nullptr, p->ic, M, p->oc, p->ic,
@@ -492,6 +500,11 @@ int spx_set_option(const char* name, int64_t value) {
     g_pw_path = (int)value;
     return SPX_OK;
   }
+  if (n == "pw_gemm") {
+    if (value < 0 || value > 1) return fail(SPX_ERR_INVALID_ARGUMENT, "pw_gemm must be 0..1");
+    g_pw_gemm = (int)value;
+    return SPX_OK;
+  }
   if (n == "ar_wait_limit_us") {
     if (value < 1000 || value > 60000000)
       return fail(SPX_ERR_INVALID_ARGUMENT, "ar_wait_limit_us must be 1000..60000000");
@@ -515,12 +528,15 @@ int64_t spx_get_option(const char* name) {
   if (n == "tc_conv_groups") return g_tc_conv2 ? 2 : 1;
   if (n == "tc_lo_tmem") return g_tc_lo_tmem;
   if (n == "ar_wait_limit_us") return g_ar_wait_limit_us;
+  if (n == "pw_gemm") return g_pw_gemm;
   return -1;
 }
 
 static int device_status(const char* what) {
   if (dw_take_status())
     return fail(SPX_ERR_CUDA, "%s: a depthwise tile load wait timed out", what);
+  if (pw_take_status())
+    return fail(SPX_ERR_CUDA, "%s: a resident-tile pointwise GEMM wait timed out", what);
   if (bg_take_status())
     return fail(SPX_ERR_CUDA, "%s: a batched tensor-core GEMM wait timed out", what);
   if (dwp_take_status())

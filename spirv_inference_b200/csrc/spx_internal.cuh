@@ -236,6 +236,13 @@ int launch_weights_split(cudaStream_t s, int64_t* cnt, const float* w, float* hi
 int tc_take_status();
 int dwp_take_status();
 int bg_take_status();
+int pw_take_status();
+// 1x1 conv / GEMM with a resident activation tile (k_pwgemm.cu): K <= 160,
+// N >= 128, pre-split weights, no residual.  -1 when not eligible.
+int try_pwgemm(cudaStream_t s, int64_t* cnt, const float* a, const float* w_hi, const float* w_lo,
+               const float* bias, const float* res, float* c, int M, int N, int K, int act);
+// 1: pointwise convolutions that try_pwgemm takes run there (default 0).
+extern int g_pw_gemm;
 // Batched 3xTF32 tensor-core GEMM for K <= 128 (k_bgemm.cu): -1 when the
 // operands are not eligible (caller falls back), else SPX_OK or an error.
 int try_bgemm_tc(cudaStream_t s, int64_t* cnt, const float* a, const float* b, const float* bias,
