@@ -575,23 +575,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         float4* row = reinterpret_cast<float4*>(stg + lane * 128);
-        // Bias first, all eight loads in flight before any staging store.
-        float4 b4[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          b4[e] = (p.bp && n0 + 4 * e < p.cout)
-                      ? __ldg(reinterpret_cast<const float4*>(p.bp + n0) + e)
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
         with_act(p.act_p, [&](auto tag) {
           constexpr int A = decltype(tag)::value;
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
+            const float4 b4 = (p.bp && n0 + 4 * e < p.cout)
+                                  ? __ldg(reinterpret_cast<const float4*>(p.bp + n0) + e)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
             const float4 r4 = p.res ? row[e ^ (lane & 7)] : make_float4(0.f, 0.f, 0.f, 0.f);
             float4 o;
-            o.x = act_c<A>(v[4 * e + 0] + b4[e].x + r4.x);
-            o.y = act_c<A>(v[4 * e + 1] + b4[e].y + r4.y);
-            o.z = act_c<A>(v[4 * e + 2] + b4[e].z + r4.z);
-            o.w = act_c<A>(v[4 * e + 3] + b4[e].w + r4.w);
+            o.x = act_c<A>(v[4 * e + 0] + b4.x + r4.x);
+            o.y = act_c<A>(v[4 * e + 1] + b4.y + r4.y);
+            o.z = act_c<A>(v[4 * e + 2] + b4.z + r4.z);
+            o.w = act_c<A>(v[4 * e + 3] + b4.w + r4.w);
             row[e ^ (lane & 7)] = o;
           }
         });
