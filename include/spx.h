@@ -105,6 +105,14 @@ int spx_device_status(void);
  * at most 160 and at least 128 outputs keep each 128-row activation tile
  * resident (split once for every n tile); 0 (default) = the row-tiled
  * tensor-core GEMM, measured faster on every MobileNetV2 expand layer.
+ * "dwp_groups": bit mask over the fused depthwise -> projection kernel's
+ * tile classes (bit 0: stride 1, output width <= 8; bit 1: stride 1, wider,
+ * more than 32 channels; bit 4: stride 1, wider, at most 32 channels (one K
+ * block); bit 2: stride 2, width <= 8; bit 3: stride 2, wider); a set bit
+ * builds the class's depthwise tiles with two builder groups taking
+ * alternate K blocks, a clear bit with one group over each K block.  Results
+ * are identical either way; default 15 (measured on the MobileNetV2 layers at
+ * batch 256: two groups faster everywhere but on the single-K-block layer).
  * "ar_wait_limit_us": bound of the peer all-reduce's wait for the other ranks
  * (default 2,000,000; 1,000 .. 60,000,000).
  * "tc_lo_tmem": 1 = with pre-split weights and several k-blocks the

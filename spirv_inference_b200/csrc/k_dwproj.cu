@@ -101,7 +101,7 @@ struct DwpArgs {
 // convolution over 3-channel NHWC input (the CNN stems, K = 27 padded to
 // one 32-wide K block): the halo slot is a 3-D box of whole input rows
 // (W * 3 floats), the builders gather each pixel's 27 taps into its A row.
-template <int KS, int S, int TH, int TW, int CB, int R, bool STEM = false, int TN = 1>
+template <int KS, int S, int TH, int TW, int CB, int R, bool STEM = false, int TN = 1, int NG = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     dwproj_kernel(const __grid_constant__ CUtensorMap tmX,
                   const __grid_constant__ CUtensorMap tmBhi,
@@ -126,7 +126,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kWBytes = KS * KS * CB * 4;
   constexpr uint32_t kBOff = kWOff + (kWBytes + 127) / 128 * 128;  // TMA: 128-byte aligned
   const uint32_t slot_tx = STEM ? kHaloBytes : kHaloBytes + kWBytes + (p.bd ? CB * 4 : 0);
-  static_assert(STEM || TN * CG * (TW / CW) * (TH / R) == kBuildWarps * 32,
+  // NG builder groups: with NG = 2 the two groups of four warps take
+  // alternate K-block steps (a group's stage is the step parity), so two K
+  // blocks are built at once; each group covers the whole tile.
+  constexpr int kGroupThreads = kBuildWarps * 32 / NG;
+  constexpr int kArrive = kBuildWarps / NG;  // warp arrivals per stage / halo phase
+  static_assert(NG == 1 || NG == 2, "one or two builder groups");
+  static_assert(!STEM || NG == 1, "the stem builder is one group");
+  static_assert(STEM || TN * CG * (TW / CW) * (TH / R) == kGroupThreads,
                 "one builder thread per (image, rows, column pair, channel pair)");
   static_assert(!STEM || (TH * TW == 128 && S == 2 && KS == 3), "stem tile");
   static_assert(TN * TH * TW <= 128, "a tile is at most 128 GEMM rows");
@@ -156,10 +163,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int h = 0; h < p.hst; ++h) {
       mb_init(&hfull[h], 1);
-      mb_init(&hempty[h], kBuildWarps);
+      mb_init(&hempty[h], kArrive);
     }
     for (int j = 0; j < 2; ++j) {
-      mb_init(&afull[j], kBuildWarps);
+      mb_init(&afull[j], kArrive);
       mb_init(&bfull[j], 1);
       mb_init(&empty[j], 1);
       mb_init(&tfull[j], 1);
@@ -394,27 +401,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     // written the same way.  Wait results are voted per warp, so a wait that
     // gave up makes the whole warp leave together.
     const int tid = threadIdx.x;
-    const int cg = tid % CG;
-    const int ox_l = ((tid / CG) % (TW / CW)) * CW;  // first of this thread's columns
-    const int rg = (tid / (CG * (TW / CW))) % (TH / R);
-    const int im = tid / (CG * (TW / CW) * (TH / R));  // image of the tile
-    int j = 0, h = 0;
-    uint32_t eph = 0, hph = 0;
+    const int bgrp = tid / kGroupThreads;  // builder group: steps with step % NG == bgrp
+    const int gtid = tid % kGroupThreads;
+    const int cg = gtid % CG;
+    const int ox_l = ((gtid / CG) % (TW / CW)) * CW;  // first of this thread's columns
+    const int rg = (gtid / (CG * (TW / CW))) % (TH / R);
+    const int im = gtid / (CG * (TW / CW) * (TH / R));  // image of the tile
     int step = 0;
     for (int t = blockIdx.x; t < p.total; t += gridDim.x) {
       bool ok = true;
       for (int kb = 0; kb < p.kblocks && ok; ++kb, ++step) {
-        // The stage's previous MMAs are done before its A tile is rewritten.
-        ok = __all_sync(0xffffffffu,
-                        mb_wait(&empty[j], eph ^ 1, abort_flag, &g_dwp_status, kWaitNs, 64));
+        if (NG == 2 && (step & 1) != bgrp) continue;
+        // The stage's previous MMAs are done before its A tile is rewritten
+        // (stage j = step parity; this is its (step / 2)-th use).
+        const int j = step & 1;
+        ok = __all_sync(0xffffffffu, mb_wait(&empty[j], ((uint32_t)(step >> 1) & 1u) ^ 1u,
+                                             abort_flag, &g_dwp_status, kWaitNs, 64));
         if (!ok) break;
         uint8_t* a_raw = stages + (size_t)j * p.stage_bytes;
         uint8_t* a_lo = a_raw + kAHalf;
         for (int sub = 0; sub < SUBS; ++sub) {
           const int cl = sub * CB + cg * 2;  // channel within the 32-channel K block
+          // Halo slots are filled in sub-block order over all steps.
+          const int seq = step * SUBS + sub;
+          const int h = seq % p.hst;
+          const uint32_t hph = (uint32_t)(seq / p.hst) & 1u;
           if (tid == 0 && sub == 0) DWP_TRACE(1, step);
-          ok = __all_sync(0xffffffffu,
-                          mb_wait(&hfull[h], hph, abort_flag, &g_dwp_status, kWaitNs, 32));
+          // With two groups the slot's previous fill (sequence seq - hst) may
+          // belong to the other group, which can lag a step behind; until it
+          // has released that fill, this fill's parity would also match the
+          // phase before (the fill two back).  So first wait for that release
+          // on the slot's empty barrier (its phase count is unambiguous here:
+          // this group has not released seq yet), then for this fill.
+          bool wok = true;
+          if (NG == 2 && seq >= p.hst)
+            wok = mb_wait(&hempty[h], hph ^ 1u, abort_flag, &g_dwp_status, kWaitNs, 32);
+          if (wok) wok = mb_wait(&hfull[h], hph, abort_flag, &g_dwp_status, kWaitNs, 32);
+          ok = __all_sync(0xffffffffu, wok);
           if (!ok) break;
           if (tid == 0 && sub == 0) DWP_TRACE(2, step);
           const uint8_t* slot = halo + (size_t)h * p.halo_buf;
@@ -461,10 +484,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mb_arrive(&hempty[h]);
           }
-          if (++h == p.hst) {
-            h = 0;
-            hph ^= 1;
-          }
           // GEMM row m = (rg*R + r)*TW + ox_l + c; TW is a multiple of 8, so the
           // 128-byte swizzle phase m & 7 = (ox_l + c) & 7 does not depend on r.
           const uint32_t c16s = (uint32_t)(cl >> 2) << 4;  // 16-byte chunk, in bytes
@@ -501,10 +520,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mb_arrive(&afull[j]);
         if (tid == 0) DWP_TRACE(4, step);
-        if (++j == 2) {
-          j = 0;
-          eph ^= 1;
-        }
       }
       if (!ok) break;
     }
@@ -673,7 +688,7 @@ struct DwpCfg {
   int th, tw, cb;
 };
 
-template <int KS, int S, int TH, int TW, int CB, int R, int TN = 1>
+template <int KS, int S, int TH, int TW, int CB, int R, int TN = 1, int NG = 1>
 int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, const float* bd,
                const float* w_hi, const float* w_lo, const float* bp, const float* res, float* y,
                const spx_dwproj_params* q, bool dry_run, uint32_t* smem_out) {
@@ -776,7 +791,7 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
     if (r != CUDA_SUCCESS)
       return fail(SPX_ERR_CUDA, "dw_project: depthwise weight map encode failed (%d)", (int)r);
   }
-  auto kern = dwproj_kernel<KS, S, TH, TW, CB, R, false, TN>;
+  auto kern = dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG>;
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [&] {
@@ -939,18 +954,23 @@ int launch_dw_project(cudaStream_t s, int64_t* cnt, const float* x, const float*
         (bp && !al16(bp)) || (res && !al16(res)))
       return fail(SPX_ERR_INVALID_ARGUMENT, "dw_project: tensors must be 16-byte aligned");
   }
+  // Builder groups per tile class (bit set: two groups, each with twice the
+  // rows per thread), from the "dwp_groups" option.
+  const int g = g_dwp_groups;
+#define SPX_DWP_CFG(bit, S_, TW_, CB_, R_, TN_)                                               \
+  return (g >> bit) & 1                                                                     \
+             ? launch_cfg<3, S_, 8, TW_, CB_, 2 * R_, TN_, 2>(s, cnt, x, wd, bd, w_hi, w_lo, bp, \
+                                                             res, y, q, dry_run, nullptr)   \
+             : launch_cfg<3, S_, 8, TW_, CB_, R_, TN_, 1>(s, cnt, x, wd, bd, w_hi, w_lo, bp,     \
+                                                         res, y, q, dry_run, nullptr)
   if (q->stride == 1) {
-    if (q->ow <= 8)
-      return launch_cfg<3, 1, 8, 8, 16, 2, 2>(s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run,
-                                           nullptr);
-    return launch_cfg<3, 1, 8, 16, 32, 4>(s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run,
-                                          nullptr);
+    if (q->ow <= 8) SPX_DWP_CFG(0, 1, 8, 16, 2, 2);
+    if (q->c <= 32) SPX_DWP_CFG(4, 1, 16, 32, 4, 1);
+    SPX_DWP_CFG(1, 1, 16, 32, 4, 1);
   }
-  if (q->ow <= 8)
-    return launch_cfg<3, 2, 8, 8, 16, 1>(s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run,
-                                         nullptr);
-  return launch_cfg<3, 2, 8, 16, 16, 2>(s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run,
-                                        nullptr);
+  if (q->ow <= 8) SPX_DWP_CFG(2, 2, 8, 16, 1, 1);
+  SPX_DWP_CFG(3, 2, 16, 16, 2, 1);
+#undef SPX_DWP_CFG
 }
 
 }  // namespace spx

@@ -45,6 +45,7 @@ int64_t g_ar_wait_limit_us = 2000000;
 int g_dw_path = 0;
 int g_pw_path = 0;
 int g_pw_gemm = 0;
+int g_dwp_groups = 15;
 
 // ---- algorithm selection for dense contractions ---------------------------
 int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
@@ -505,6 +506,11 @@ int spx_set_option(const char* name, int64_t value) {
     g_pw_gemm = (int)value;
     return SPX_OK;
   }
+  if (n == "dwp_groups") {
+    if (value < 0 || value > 31) return fail(SPX_ERR_INVALID_ARGUMENT, "dwp_groups must be 0..31");
+    g_dwp_groups = (int)value;
+    return SPX_OK;
+  }
   if (n == "ar_wait_limit_us") {
     if (value < 1000 || value > 60000000)
       return fail(SPX_ERR_INVALID_ARGUMENT, "ar_wait_limit_us must be 1000..60000000");
@@ -529,6 +535,7 @@ int64_t spx_get_option(const char* name) {
   if (n == "tc_lo_tmem") return g_tc_lo_tmem;
   if (n == "ar_wait_limit_us") return g_ar_wait_limit_us;
   if (n == "pw_gemm") return g_pw_gemm;
+  if (n == "dwp_groups") return g_dwp_groups;
   return -1;
 }
 

@@ -84,6 +84,33 @@ def test_dw_project_matches_float64(g, n, ih, c, s, cout, residual):
     assert np.abs(got - dz.download()).max() / np.abs(ref).max() <= 2 * (2.5e-8 * c + 1e-6)
 
 
+@pytest.mark.parametrize("n,ih,c,s,cout,residual", [CASES[1], CASES[3], CASES[8], CASES[10],
+                                                   CASES[11], CASES[13]])
+def test_builder_groups_give_identical_results(g, n, ih, c, s, cout, residual):
+    """One builder group per K block or two taking alternate K blocks: every
+    depthwise value is accumulated by one thread in the same order either
+    way, so the outputs are bit-identical."""
+    oh = -(-ih // s)
+    pt = max((oh - 1) * s + 3 - ih, 0) // 2
+    x = g.tensor(_r(n, ih, ih, c, scale=2.0))
+    wd, bd = g.tensor(_r(3, 3, c)), g.tensor(_r(c, scale=0.1))
+    split = g.weights_split(g.tensor(_r(cout, c, scale=np.sqrt(3.0 / c))))
+    bp = g.tensor(_r(cout, scale=0.1))
+    res = g.tensor(_r(n, oh, oh, cout)) if residual else None
+    outs = []
+    default = _lib.get_option("dwp_groups")
+    try:
+        for mask in (0, 31):
+            _lib.set_option("dwp_groups", mask)
+            dy = g.alloc((n, oh, oh, cout))
+            g.dw_project_nhwc(x, wd, bd, split, bp, dy, stride=s, pad=(pt, pt),
+                              act_dw=_lib.ACT_RELU6, residual=res)
+            outs.append(dy.download())
+    finally:
+        _lib.set_option("dwp_groups", default)
+    np.testing.assert_array_equal(outs[0], outs[1])
+
+
 def test_dw_project_rejects_unsupported(g):
     x, y = g.alloc((1, 8, 8, 30)), g.alloc((1, 8, 8, 16))
     assert not g.dw_project_supported(x, y, stride=1, pad=(1, 1))     # c % 4
