@@ -113,6 +113,10 @@ int spx_device_status(void);
  * alternate K blocks, a clear bit with one group over each K block.  Results
  * are identical either way; default 15 (measured on the MobileNetV2 layers at
  * batch 256: two groups faster everywhere but on the single-K-block layer).
+ * "dwp_stages": most A/B operand stages the fused depthwise -> projection
+ * kernel uses (2..4, default 4; fewer where shared memory is short).  More
+ * stages let the depthwise builders run ahead of the tensor core.  Results
+ * are identical for every value.
  * "ar_wait_limit_us": bound of the peer all-reduce's wait for the other ranks
  * (default 2,000,000; 1,000 .. 60,000,000).
  * "tc_lo_tmem": 1 = with pre-split weights and several k-blocks the

@@ -78,10 +78,15 @@ constexpr uint32_t kAHalf = 128 * 32 * 4;        // one 128 x 32 fp32 A tile: 16
 constexpr unsigned long long kWaitNs = 2000000000ull;
 constexpr unsigned long long kDrainNs = 200000000ull;
 constexpr int kMaxHalo = 4;
+constexpr int kMaxStages = 4;        // A/B stages (runtime count nst, 2..4)
+constexpr uint32_t kBarBytes = 512;  // mbarriers, TMEM slot, abort flag
+constexpr int kMaxBias = 512;        // projection bias staged in shared memory
+constexpr uint32_t kBiasBytes = kMaxBias * 4;
 
 struct DwpArgs {
   int n, ih, iw, ce, oh, ow, cout, np, n_ntiles, pt, pl, tiles_h, tiles_w, kblocks, total;
   int hst;                 // halo ring depth
+  int nst;                 // A/B stages
   uint32_t halo_buf;       // bytes per halo slot (1024-aligned)
   uint32_t stage_bytes;    // A raw | A lo | B hi | B lo
   uint32_t b_bytes;        // NP x 128
@@ -146,18 +151,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* stages = halo + (size_t)p.hst * p.halo_buf;
   // Epilogue staging: one 128-row x 32-channel tile per group, 128-byte
   // swizzled (the TMA store / residual load box layout).
-  uint8_t* estage = stages + 2 * (size_t)p.stage_bytes;
+  uint8_t* estage = stages + (size_t)p.nst * p.stage_bytes;
   uint64_t* hfull = (uint64_t*)(estage + kEpiGroups * (size_t)kEStage);
   uint64_t* hempty = hfull + kMaxHalo;
   uint64_t* afull = hempty + kMaxHalo;
-  uint64_t* bfull = afull + 2;
-  uint64_t* empty = bfull + 2;
-  uint64_t* tfull = empty + 2;
+  uint64_t* bfull = afull + kMaxStages;
+  uint64_t* empty = bfull + kMaxStages;
+  uint64_t* tfull = empty + kMaxStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint64_t* rfull = drain + 1;  // [4 * kEpiGroups]: a warp's residual box landed
   uint32_t* tmem_slot = (uint32_t*)(rfull + 4 * kEpiGroups);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  // Projection bias of every n tile, zero past cout (or without a bias): the
+  // epilogue reads it as shared-memory broadcasts instead of global loads.
+  float* bias_s = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(hfull) + kBarBytes);
+  for (int i = threadIdx.x; i < p.n_ntiles * p.np && i < kMaxBias; i += kThreads)
+    bias_s[i] = (p.bp && i < p.cout) ? __ldg(p.bp + i) : 0.f;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -165,10 +175,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mb_init(&hfull[h], 1);
       mb_init(&hempty[h], kArrive);
     }
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < p.nst; ++j) {
       mb_init(&afull[j], kArrive);
       mb_init(&bfull[j], 1);
       mb_init(&empty[j], 1);
+    }
+    for (int j = 0; j < 2; ++j) {
       mb_init(&tfull[j], 1);
       mb_init(&tempty[j], 4 * 32);
     }
@@ -256,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_2d(st + 2 * kAHalf + p.b_bytes, &tmBlo, &bfull[j], kb * 32, nt * p.np);
           b_armed |= 1u << j;
           b_par = (b_par & ~(1u << j)) | (eph << j);
-          if (++j == 2) {
+          if (++j == p.nst) {
             j = 0;
             eph ^= 1;
           }
@@ -265,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     b_done:
       if (*abort_flag) {
         volatile int never = 0;
-        for (int q = 0; q < 2; ++q)
+        for (int q = 0; q < p.nst; ++q)
           if (b_armed & (1u << q))
             mb_wait(&bfull[q], (b_par >> q) & 1, &never, &g_dwp_status, kDrainNs, 64);
       }
@@ -316,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           issued = true;
           mma_commit(&empty[j]);
-          if (++j == 2) {
+          if (++j == p.nst) {
             j = 0;
             ph ^= 1;
           }
@@ -388,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mb_arrive(&afull[j]);
       if (tid == 0) DWP_TRACE(4, st_i);
-      if (++j == 2) {
+      if (++j == p.nst) {
         j = 0;
         eph ^= 1;
       }
@@ -413,9 +425,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < p.kblocks && ok; ++kb, ++step) {
         if (NG == 2 && (step & 1) != bgrp) continue;
         // The stage's previous MMAs are done before its A tile is rewritten
-        // (stage j = step parity; this is its (step / 2)-th use).
-        const int j = step & 1;
-        ok = __all_sync(0xffffffffu, mb_wait(&empty[j], ((uint32_t)(step >> 1) & 1u) ^ 1u,
+        // (stage j = step mod nst; this is its (step / nst)-th use).  With two
+        // groups and three stages a stage's uses alternate between the
+        // groups, but a group at step s has built s - 2, which needed the MMA
+        // of s - 5 (so of s - 6) done: the stage is never two phases behind.
+        const int j = step % p.nst;
+        ok = __all_sync(0xffffffffu, mb_wait(&empty[j], ((uint32_t)(step / p.nst) & 1u) ^ 1u,
                                              abort_flag, &g_dwp_status, kWaitNs, 64));
         if (!ok) break;
         uint8_t* a_raw = stages + (size_t)j * p.stage_bytes;
@@ -426,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int seq = step * SUBS + sub;
           const int h = seq % p.hst;
           const uint32_t hph = (uint32_t)(seq / p.hst) & 1u;
-          if (tid == 0 && sub == 0) DWP_TRACE(1, step);
+          if (gtid == 0 && sub == 0) DWP_TRACE(1, step);
           // With two groups the slot's previous fill (sequence seq - hst) may
           // belong to the other group, which can lag a step behind; until it
           // has released that fill, this fill's parity would also match the
@@ -439,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (wok) wok = mb_wait(&hfull[h], hph, abort_flag, &g_dwp_status, kWaitNs, 32);
           ok = __all_sync(0xffffffffu, wok);
           if (!ok) break;
-          if (tid == 0 && sub == 0) DWP_TRACE(2, step);
+          if (gtid == 0 && sub == 0) DWP_TRACE(2, step);
           const uint8_t* slot = halo + (size_t)h * p.halo_buf;
           const float* in = reinterpret_cast<const float*>(slot) + im * (IH * IW * CB);
           const float* wsm = reinterpret_cast<const float*>(slot + kWOff);
@@ -477,9 +492,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
           }
-          if (tid == 0 && sub == 0) DWP_TRACE(3, step);
+          if (gtid == 0 && sub == 0) DWP_TRACE(3, step);
           __syncwarp();
-          if (tid == 0 && sub == 0) DWP_TRACE(10, step);
+          if (gtid == 0 && sub == 0) DWP_TRACE(10, step);
           if (lane == 0) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mb_arrive(&hempty[h]);
@@ -513,13 +528,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           });
         }
         if (!ok) break;
-        if (tid == 0) DWP_TRACE(8, step);
+        if (gtid == 0) DWP_TRACE(8, step);
         // Generic-proxy writes of the A tile become visible to the tensor core.
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        if (tid == 0) DWP_TRACE(9, step);
+        if (gtid == 0) DWP_TRACE(9, step);
         __syncwarp();
         if (lane == 0) mb_arrive(&afull[j]);
-        if (tid == 0) DWP_TRACE(4, step);
+        if (gtid == 0) DWP_TRACE(4, step);
       }
       if (!ok) break;
     }
@@ -594,9 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           constexpr int A = decltype(tag)::value;
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const float4 b4 = (p.bp && n0 + 4 * e < p.cout)
-                                  ? __ldg(reinterpret_cast<const float4*>(p.bp + n0) + e)
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 b4 = reinterpret_cast<const float4*>(bias_s + n0)[e];
             const float4 r4 = p.res ? row[e ^ (lane & 7)] : make_float4(0.f, 0.f, 0.f, 0.f);
             float4 o;
             o.x = act_c<A>(v[4 * e + 0] + b4.x + r4.x);
@@ -731,14 +744,23 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
   p.res = res;
   p.y = y;
   p.act_p = q->act_proj;
-  const uint32_t fixed = 1024 + 2 * p.stage_bytes + kEpiGroups * kEStage + 256;
   const uint32_t cap = 227 * 1024;
-  int hst = 0;
-  while (hst < 3 && fixed + (uint32_t)(hst + 1) * p.halo_buf <= cap) ++hst;
-  if (hst < 2)
-    return fail(SPX_ERR_UNSUPPORTED, "dw_project: tile buffers exceed shared memory");
-  p.hst = hst;
-  const uint32_t smem = fixed + (uint32_t)hst * p.halo_buf;
+  // Shared memory: as many A/B stages as fit (up to the "dwp_stages"
+  // option) with at least two halo slots, then a third halo slot if it fits.
+  auto need = [&](int nst, int hst) {
+    return 1024 + (uint32_t)nst * p.stage_bytes + kEpiGroups * kEStage + kBarBytes + kBiasBytes +
+           (uint32_t)hst * p.halo_buf;
+  };
+  p.nst = 0;
+  for (int nst = g_dwp_stages; nst >= 2 && !p.nst; --nst)
+    for (int hst = 3; hst >= 2; --hst)
+      if (need(nst, hst) <= cap) {
+        p.nst = nst;
+        p.hst = hst;
+        break;
+      }
+  if (!p.nst) return fail(SPX_ERR_UNSUPPORTED, "dw_project: tile buffers exceed shared memory");
+  const uint32_t smem = need(p.nst, p.hst);
   if (smem_out) *smem_out = smem;
   if (dry_run) return SPX_OK;
 
@@ -844,7 +866,9 @@ int launch_stem(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
   p.bp = bias;
   p.y = y;
   p.act_p = q->activation;
-  const uint32_t fixed = 1024 + 2 * p.stage_bytes + kEpiGroups * kEStage + 256;
+  p.nst = 2;
+  const uint32_t fixed =
+      1024 + 2 * p.stage_bytes + kEpiGroups * kEStage + kBarBytes + kBiasBytes;
   const uint32_t cap = 227 * 1024;
   int hst = 0;
   while (hst < 4 && fixed + (uint32_t)(hst + 1) * p.halo_buf <= cap) ++hst;

@@ -46,6 +46,7 @@ int g_dw_path = 0;
 int g_pw_path = 0;
 int g_pw_gemm = 0;
 int g_dwp_groups = 15;
+int g_dwp_stages = 4;
 
 // ---- algorithm selection for dense contractions ---------------------------
 int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
@@ -506,6 +507,11 @@ int spx_set_option(const char* name, int64_t value) {
     g_pw_gemm = (int)value;
     return SPX_OK;
   }
+  if (n == "dwp_stages") {
+    if (value < 2 || value > 4) return fail(SPX_ERR_INVALID_ARGUMENT, "dwp_stages must be 2..4");
+    g_dwp_stages = (int)value;
+    return SPX_OK;
+  }
   if (n == "dwp_groups") {
     if (value < 0 || value > 31) return fail(SPX_ERR_INVALID_ARGUMENT, "dwp_groups must be 0..31");
     g_dwp_groups = (int)value;
@@ -536,6 +542,7 @@ int64_t spx_get_option(const char* name) {
   if (n == "ar_wait_limit_us") return g_ar_wait_limit_us;
   if (n == "pw_gemm") return g_pw_gemm;
   if (n == "dwp_groups") return g_dwp_groups;
+  if (n == "dwp_stages") return g_dwp_stages;
   return -1;
 }
 

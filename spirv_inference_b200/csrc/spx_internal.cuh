@@ -263,7 +263,8 @@ extern int g_gemm_path;
 // Bound of the peer all-reduce's wait for the other ranks, microseconds.
 extern int64_t g_ar_wait_limit_us;
 extern int g_tc_epi12;
-extern int g_dwp_groups;  // dw_project builder groups per tile class (bit mask)
+extern int g_dwp_groups;
+extern int g_dwp_stages;  // dw_project A/B stage count cap (2..4)  // dw_project builder groups per tile class (bit mask)
 extern int g_tc_conv2;
 extern int g_tc_lo_tmem;
 // Depthwise path: 0 automatic (TMA tiles where the shape allows), 1 register

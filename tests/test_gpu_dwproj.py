@@ -86,10 +86,11 @@ def test_dw_project_matches_float64(g, n, ih, c, s, cout, residual):
 
 @pytest.mark.parametrize("n,ih,c,s,cout,residual", [CASES[1], CASES[3], CASES[8], CASES[10],
                                                    CASES[11], CASES[13]])
-def test_builder_groups_give_identical_results(g, n, ih, c, s, cout, residual):
-    """One builder group per K block or two taking alternate K blocks: every
-    depthwise value is accumulated by one thread in the same order either
-    way, so the outputs are bit-identical."""
+def test_builder_groups_and_stages_give_identical_results(g, n, ih, c, s, cout, residual):
+    """One builder group per K block or two taking alternate K blocks, two to
+    four A/B stages: every depthwise value is accumulated by one thread in
+    the same order and every GEMM in the same k order either way, so the
+    outputs are bit-identical."""
     oh = -(-ih // s)
     pt = max((oh - 1) * s + 3 - ih, 0) // 2
     x = g.tensor(_r(n, ih, ih, c, scale=2.0))
@@ -98,17 +99,20 @@ def test_builder_groups_give_identical_results(g, n, ih, c, s, cout, residual):
     bp = g.tensor(_r(cout, scale=0.1))
     res = g.tensor(_r(n, oh, oh, cout)) if residual else None
     outs = []
-    default = _lib.get_option("dwp_groups")
+    defaults = _lib.get_option("dwp_groups"), _lib.get_option("dwp_stages")
     try:
-        for mask in (0, 31):
+        for mask, stages in ((0, 2), (31, 2), (0, 4), (31, 4), (31, 3)):
             _lib.set_option("dwp_groups", mask)
+            _lib.set_option("dwp_stages", stages)
             dy = g.alloc((n, oh, oh, cout))
             g.dw_project_nhwc(x, wd, bd, split, bp, dy, stride=s, pad=(pt, pt),
                               act_dw=_lib.ACT_RELU6, residual=res)
             outs.append(dy.download())
     finally:
-        _lib.set_option("dwp_groups", default)
-    np.testing.assert_array_equal(outs[0], outs[1])
+        _lib.set_option("dwp_groups", defaults[0])
+        _lib.set_option("dwp_stages", defaults[1])
+    for o in outs[1:]:
+        np.testing.assert_array_equal(o, outs[0])
 
 
 def test_dw_project_rejects_unsupported(g):
