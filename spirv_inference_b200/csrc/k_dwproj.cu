@@ -486,10 +486,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int c = 0; c < CW; ++c)
 #pragma unroll
-                for (int kx = 0; kx < KS; ++kx) {
-                  acc[r][c].x = fmaf(row[c * S + kx].x, wr[ky][kx].x, acc[r][c].x);
-                  acc[r][c].y = fmaf(row[c * S + kx].y, wr[ky][kx].y, acc[r][c].y);
-                }
+                for (int kx = 0; kx < KS; ++kx)
+                  acc[r][c] = ffma2(row[c * S + kx], wr[ky][kx], acc[r][c]);
             }
           }
           if (gtid == 0 && sub == 0) DWP_TRACE(3, step);

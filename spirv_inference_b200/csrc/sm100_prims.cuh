@@ -202,6 +202,18 @@ __device__ __forceinline__ float tf32_lo(float x) {
   return __uint_as_float((__float_as_uint(r) + 0x1000u) & 0xFFFFE000u);
 }
 
+// Two independent fp32 fused multiply-adds in one instruction (sm_100
+// packed fp32): each lane is rounded exactly as fmaf rounds it.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<const unsigned long long*>(&a)),
+        "l"(*reinterpret_cast<const unsigned long long*>(&b)),
+        "l"(*reinterpret_cast<const unsigned long long*>(&c)));
+  return *reinterpret_cast<const float2*>(&d);
+}
+
 // The same for a finite x (no special-value check).
 __device__ __forceinline__ float tf32_lo_finite(float x) {
   const float r = x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
