@@ -111,6 +111,7 @@ struct TcArgs {
   int lo_tmem;      // activation lo terms in two TMEM slots (A operand from TMEM)
   int lo_col;       // first TMEM column of the two 32-column lo slots
   uint32_t smem_bytes;  // dynamic shared memory of the launch
+  int bias_n;           // bias entries staged in shared memory (n_tiles * BN), 0 = read from global
   int epi_warps;  // epilogue warps in use (4, 8 or 12): long k-loops trade them for stages,
                   // 1-block k-loops take 12 (warps 8-11 leave the converters)
 };
@@ -409,6 +410,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   // live in TMEM, the A lo tile.
   const uint32_t b_off = p.lo_tmem ? kATileBytes : 2 * kATileBytes;
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  // Bias of every n tile (zero past N, or without a bias) where shared memory
+  // has room: the TMA epilogue then reads it as broadcasts, not global loads.
+  float* bias_s = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 512);
+  for (int i = threadIdx.x; i < p.bias_n; i += kThreads)
+    bias_s[i] = (p.bias && i < p.N) ? __ldg(p.bias + i) : 0.f;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Converters: warps conv_lo .. kEpiWarps + kConvWarps - 1.
@@ -688,7 +694,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int q = 0; q < 8; ++q) {
             const int nq = n0 + 4 * q;
             float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (p.bias && nq < p.N) b4 = __ldg(reinterpret_cast<const float4*>(p.bias + nq));
+            if (p.bias_n) b4 = reinterpret_cast<const float4*>(bias_s + n0)[q];
+            else if (p.bias && nq < p.N) b4 = __ldg(reinterpret_cast<const float4*>(p.bias + nq));
             const float4 r4 = p.res ? srow[q ^ sw] : make_float4(0.f, 0.f, 0.f, 0.f);
             float4 o;
             o.x = act_c<A>(v[4 * q + 0] * p.alpha + b4.x + r4.x);
@@ -1590,13 +1597,14 @@ int plan_gemm_tc(TcArgs& p, int M, int N, int K, bool presplit, bool conv, int m
     const int half_budget = 227 * 1024 - 1024 - 4 * (int)kEpiSlot - 512;
     if (kb_total >= 8 && full_budget / bn_stage < 3 && half_budget / bn_stage >= 3)
       p.epi_warps = 4;
-    // One k-block per tile (K <= 32, the expand layers): the converters are
-    // mostly idle and the epilogue's per-chunk latency sets the tile period,
-    // so four converter warps become a third epilogue warp per lane quarter
-    // when that saves a round of chunks.
+    // One or two k-blocks per tile (K <= 64, the expand layers): the
+    // converters are mostly idle and the epilogue's per-chunk latency sets
+    // the tile period, so four converter warps become a third epilogue warp
+    // per lane quarter when that saves a round of chunks (measured: 64 ->
+    // 384 at 14x14, b256, 36.8 -> 34.6 us; no gain from three k-blocks).
     const int chunks = (p.BN + 31) / 32;
     const int wide_budget = 227 * 1024 - 1024 - kMaxEpiWarps * (int)kEpiSlot - 512;
-    if (g_tc_epi12 && kb_total == 1 && (chunks + 2) / 3 < (chunks + 1) / 2 &&
+    if (g_tc_epi12 && kb_total <= 2 && (chunks + 2) / 3 < (chunks + 1) / 2 &&
         wide_budget / bn_stage >= 2)
       p.epi_warps = kMaxEpiWarps;
   }
@@ -1640,6 +1648,12 @@ int plan_gemm_tc(TcArgs& p, int M, int N, int K, bool presplit, bool conv, int m
             | ((uint32_t)(kBM >> 4) << 24);    // M
   p.smem_bytes = 1024 + (uint32_t)p.stages * p.stage_bytes +
                  (p.b_resident ? 2 * p.b_bytes : 0u) + (uint32_t)p.epi_warps * kEpiSlot + 512;
+  // The bias goes to shared memory only where the plan leaves room for it.
+  const int bias_n = p.n_tiles * p.BN;
+  if (p.tma_store && bias_n <= 4096 && p.smem_bytes + (uint32_t)bias_n * 4 <= 227u * 1024u) {
+    p.bias_n = bias_n;
+    p.smem_bytes += (uint32_t)bias_n * 4;
+  }
   return SPX_OK;
 }
 
