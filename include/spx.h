@@ -108,10 +108,11 @@ int spx_device_status(void);
  * "dwp_groups": bit mask over the fused depthwise -> projection kernel's
  * tile classes (bit 0: stride 1, output width <= 8; bit 1: stride 1, wider,
  * more than 32 channels; bit 4: stride 1, wider, at most 32 channels (one K
- * block); bit 2: stride 2, width <= 8; bit 3: stride 2, wider); a set bit
+ * block); bit 2: stride 2, width <= 8; bit 3: stride 2, wider, at most 160
+ * channels; bit 5: stride 2, wider, more than 160 channels); a set bit
  * builds the class's depthwise tiles with two builder groups taking
  * alternate K blocks, a clear bit with one group over each K block.  Results
- * are identical either way; default 15 (measured on the MobileNetV2 layers at
+ * are identical either way; default 47 (measured on the MobileNetV2 layers at
  * batch 256: two groups faster everywhere but on the single-K-block layer).
  * "dwp_stages": most A/B operand stages the fused depthwise -> projection
  * kernel uses (2..4, default 4; fewer where shared memory is short).  More

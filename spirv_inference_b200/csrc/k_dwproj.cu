@@ -979,19 +979,26 @@ int launch_dw_project(cudaStream_t s, int64_t* cnt, const float* x, const float*
   // Builder groups per tile class (bit set: two groups, each with twice the
   // rows per thread), from the "dwp_groups" option.
   const int g = g_dwp_groups;
-#define SPX_DWP_CFG(bit, S_, TW_, CB_, R_, TN_)                                               \
-  return (g >> bit) & 1                                                                     \
-             ? launch_cfg<3, S_, 8, TW_, CB_, 2 * R_, TN_, 2>(s, cnt, x, wd, bd, w_hi, w_lo, bp, \
-                                                             res, y, q, dry_run, nullptr)   \
-             : launch_cfg<3, S_, 8, TW_, CB_, R_, TN_, 1>(s, cnt, x, wd, bd, w_hi, w_lo, bp,     \
-                                                         res, y, q, dry_run, nullptr)
+#define SPX_DWP_CFG(bit, S_, TH_, TW_, CB_, R_, TN_)                                           \
+  return (g >> bit) & 1                                                                        \
+             ? launch_cfg<3, S_, TH_, TW_, CB_, 2 * R_, TN_, 2>(s, cnt, x, wd, bd, w_hi, w_lo, bp, \
+                                                               res, y, q, dry_run, nullptr)   \
+             : launch_cfg<3, S_, TH_, TW_, CB_, R_, TN_, 1>(s, cnt, x, wd, bd, w_hi, w_lo, bp,     \
+                                                           res, y, q, dry_run, nullptr)
   if (q->stride == 1) {
-    if (q->ow <= 8) SPX_DWP_CFG(0, 1, 8, 16, 2, 2);
-    if (q->c <= 32) SPX_DWP_CFG(4, 1, 16, 32, 4, 1);
-    SPX_DWP_CFG(1, 1, 16, 32, 4, 1);
+    if (q->ow <= 8) SPX_DWP_CFG(0, 1, 8, 8, 16, 2, 2);
+    if (q->c <= 32) SPX_DWP_CFG(4, 1, 8, 16, 32, 4, 1);
+    SPX_DWP_CFG(1, 1, 8, 16, 32, 4, 1);
   }
-  if (q->ow <= 8) SPX_DWP_CFG(2, 2, 8, 16, 1, 1);
-  SPX_DWP_CFG(3, 2, 16, 16, 2, 1);
+  if (q->ow <= 8) SPX_DWP_CFG(2, 2, 8, 8, 16, 1, 1);
+  // Stride 2 with long reductions: 32-channel halo blocks on 64-pixel tiles.
+  // A warp's lanes then read two whole 128-byte pixels (the 16-channel
+  // blocks put the four pixels a warp reads on the same 16 banks, a 4-way
+  // conflict); the smaller tiles cost per-tile work, which only the longer
+  // K loops repay (measured: 192 -> 64 at 28x28 69.7 -> 60.8 us, 96 -> 24
+  // at 112x112 285.9 -> 312.9 us, b256).
+  if (q->c > 160) SPX_DWP_CFG(5, 2, 4, 16, 32, 2, 1);
+  SPX_DWP_CFG(3, 2, 8, 16, 16, 2, 1);
 #undef SPX_DWP_CFG
 }
 

@@ -45,7 +45,7 @@ int64_t g_ar_wait_limit_us = 2000000;
 int g_dw_path = 0;
 int g_pw_path = 0;
 int g_pw_gemm = 0;
-int g_dwp_groups = 15;
+int g_dwp_groups = 47;
 int g_dwp_stages = 4;
 
 // ---- algorithm selection for dense contractions ---------------------------
@@ -513,7 +513,7 @@ int spx_set_option(const char* name, int64_t value) {
     return SPX_OK;
   }
   if (n == "dwp_groups") {
-    if (value < 0 || value > 31) return fail(SPX_ERR_INVALID_ARGUMENT, "dwp_groups must be 0..31");
+    if (value < 0 || value > 63) return fail(SPX_ERR_INVALID_ARGUMENT, "dwp_groups must be 0..63");
     g_dwp_groups = (int)value;
     return SPX_OK;
   }

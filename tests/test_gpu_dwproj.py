@@ -46,6 +46,8 @@ CASES = [
     (1, 7, 64, 1, 32, True),       # a two-image 7x7 tile with its second image absent
     (5, 6, 48, 1, 40, True),       # 6x6 maps, odd image count
     (1, 9, 40, 1, 52, False),      # c and cout not multiples of 32
+    (2, 28, 192, 2, 64, False),    # stride 2, c > 160: 32-channel halo blocks, 64-pixel tiles
+    (1, 30, 200, 2, 40, True),     # the same class, ragged: c = 200, 15x15 output
 ]
 
 
@@ -101,7 +103,7 @@ def test_builder_groups_and_stages_give_identical_results(g, n, ih, c, s, cout, 
     outs = []
     defaults = _lib.get_option("dwp_groups"), _lib.get_option("dwp_stages")
     try:
-        for mask, stages in ((0, 2), (31, 2), (0, 4), (31, 4), (31, 3)):
+        for mask, stages in ((0, 2), (63, 2), (0, 4), (63, 4), (63, 3)):
             _lib.set_option("dwp_groups", mask)
             _lib.set_option("dwp_stages", stages)
             dy = g.alloc((n, oh, oh, cout))
