@@ -106,7 +106,8 @@ struct DwpArgs {
 // convolution over 3-channel NHWC input (the CNN stems, K = 27 padded to
 // one 32-wide K block): the halo slot is a 3-D box of whole input rows
 // (W * 3 floats), the builders gather each pixel's 27 taps into its A row.
-template <int KS, int S, int TH, int TW, int CB, int R, bool STEM = false, int TN = 1, int NG = 1>
+template <int KS, int S, int TH, int TW, int CB, int R, bool STEM = false, int TN = 1, int NG = 1,
+          int CW = 2>
 __global__ void __launch_bounds__(kThreads, 1)
     dwproj_kernel(const __grid_constant__ CUtensorMap tmX,
                   const __grid_constant__ CUtensorMap tmBhi,
@@ -118,7 +119,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int IH = (TH - 1) * S + KS, IW = (TW - 1) * S + KS;
   constexpr int CG = CB / 2;  // channel pairs per sub-block
   constexpr int SUBS = STEM ? 1 : 32 / CB;
-  constexpr int CW = 2;       // output columns per builder thread
+  // CW: output columns per builder thread (adjacent; 1 or 2)
   constexpr int WIN = (CW - 1) * S + KS;  // input columns a thread's window spans
   // Stem rows: IW pixels x 3 channels, plus up to 3 floats of 16-byte alignment
   // shift, rounded to whole 16-byte units.
@@ -416,7 +417,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int bgrp = tid / kGroupThreads;  // builder group: steps with step % NG == bgrp
     const int gtid = tid % kGroupThreads;
     const int cg = gtid % CG;
-    const int ox_l = ((gtid / CG) % (TW / CW)) * CW;  // first of this thread's columns
+    // First of this thread's columns.  With one column per thread and
+    // 16-channel blocks (64 bytes a pixel), a warp's four lane groups take
+    // columns {0, 1, 4, 5} or {2, 3, 6, 7}: their halo pixels then alternate
+    // between the two 64-byte bank halves, and so do their A-tile rows
+    // after the 128-byte swizzle (adjacent even columns would put all four
+    // on the same 16 banks).
+    const int colg = (gtid / CG) % (TW / CW);
+    const int ox_l = CW == 1 ? ((colg & 1) | ((colg & 2) << 1) | ((colg & 4) >> 1) | (colg & ~7))
+                             : colg * CW;
     const int rg = (gtid / (CG * (TW / CW))) % (TH / R);
     const int im = gtid / (CG * (TW / CW) * (TH / R));  // image of the tile
     int step = 0;
@@ -699,7 +708,7 @@ struct DwpCfg {
   int th, tw, cb;
 };
 
-template <int KS, int S, int TH, int TW, int CB, int R, int TN = 1, int NG = 1>
+template <int KS, int S, int TH, int TW, int CB, int R, int TN = 1, int NG = 1, int CW = 2>
 int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, const float* bd,
                const float* w_hi, const float* w_lo, const float* bp, const float* res, float* y,
                const spx_dwproj_params* q, bool dry_run, uint32_t* smem_out) {
@@ -811,7 +820,7 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
     if (r != CUDA_SUCCESS)
       return fail(SPX_ERR_CUDA, "dw_project: depthwise weight map encode failed (%d)", (int)r);
   }
-  auto kern = dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG>;
+  auto kern = dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG, CW>;
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [&] {
@@ -979,26 +988,26 @@ int launch_dw_project(cudaStream_t s, int64_t* cnt, const float* x, const float*
   // Builder groups per tile class (bit set: two groups, each with twice the
   // rows per thread), from the "dwp_groups" option.
   const int g = g_dwp_groups;
-#define SPX_DWP_CFG(bit, S_, TH_, TW_, CB_, R_, TN_)                                           \
+#define SPX_DWP_CFG(bit, S_, TH_, TW_, CB_, R_, TN_, CW_)                                      \
   return (g >> bit) & 1                                                                        \
-             ? launch_cfg<3, S_, TH_, TW_, CB_, 2 * R_, TN_, 2>(s, cnt, x, wd, bd, w_hi, w_lo, bp, \
-                                                               res, y, q, dry_run, nullptr)   \
-             : launch_cfg<3, S_, TH_, TW_, CB_, R_, TN_, 1>(s, cnt, x, wd, bd, w_hi, w_lo, bp,     \
-                                                           res, y, q, dry_run, nullptr)
+             ? launch_cfg<3, S_, TH_, TW_, CB_, 2 * R_, TN_, 2, CW_>(                          \
+                   s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run, nullptr)             \
+             : launch_cfg<3, S_, TH_, TW_, CB_, R_, TN_, 1, CW_>(s, cnt, x, wd, bd, w_hi, w_lo, \
+                                                                 bp, res, y, q, dry_run, nullptr)
   if (q->stride == 1) {
-    if (q->ow <= 8) SPX_DWP_CFG(0, 1, 8, 8, 16, 2, 2);
-    if (q->c <= 32) SPX_DWP_CFG(4, 1, 8, 16, 32, 4, 1);
-    SPX_DWP_CFG(1, 1, 8, 16, 32, 4, 1);
+    if (q->ow <= 8) SPX_DWP_CFG(0, 1, 8, 8, 16, 4, 2, 1);
+    if (q->c <= 32) SPX_DWP_CFG(4, 1, 8, 16, 32, 4, 1, 2);
+    SPX_DWP_CFG(1, 1, 8, 16, 32, 4, 1, 2);
   }
-  if (q->ow <= 8) SPX_DWP_CFG(2, 2, 8, 8, 16, 1, 1);
+  if (q->ow <= 8) SPX_DWP_CFG(2, 2, 8, 8, 16, 1, 1, 2);
   // Stride 2 with long reductions: 32-channel halo blocks on 64-pixel tiles.
   // A warp's lanes then read two whole 128-byte pixels (the 16-channel
   // blocks put the four pixels a warp reads on the same 16 banks, a 4-way
   // conflict); the smaller tiles cost per-tile work, which only the longer
   // K loops repay (measured: 192 -> 64 at 28x28 69.7 -> 60.8 us, 96 -> 24
   // at 112x112 285.9 -> 312.9 us, b256).
-  if (q->c > 160) SPX_DWP_CFG(5, 2, 4, 16, 32, 2, 1);
-  SPX_DWP_CFG(3, 2, 8, 16, 16, 2, 1);
+  if (q->c > 160) SPX_DWP_CFG(5, 2, 4, 16, 32, 2, 1, 2);
+  SPX_DWP_CFG(3, 2, 8, 16, 16, 2, 1, 2);
 #undef SPX_DWP_CFG
 }
 
