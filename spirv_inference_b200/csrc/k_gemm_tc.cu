@@ -1584,18 +1584,24 @@ int plan_gemm_tc(TcArgs& p, int M, int N, int K, bool presplit, bool conv, int m
       p.BN = best_bn;
     }
   }
-  // At least two pipeline stages must fit next to the epilogue tiles.
+  // At least two pipeline stages must fit next to the epilogue tiles; long
+  // k-loops count with four epilogue warps (below), so a 256-wide tile keeps
+  // its width (wide tiles read A once per 256 columns: measured 120 -> 169
+  // fp32 TFLOP/s at 4096 x 3072 x 768, 141 -> 203 at 50176 x 1024 x 512).
   const int full_budget = 227 * 1024 - 1024 - kEpiWarps * (int)kEpiSlot - 512;
-  while (p.BN > 32 && full_budget / (int)(2 * kATileBytes + 2 * (uint32_t)p.BN * kBK * 4) < 2)
+  const int fit_budget = kb_total >= 8 ? 227 * 1024 - 1024 - 4 * (int)kEpiSlot - 512 : full_budget;
+  while (p.BN > 32 && fit_budget / (int)(2 * kATileBytes + 2 * (uint32_t)p.BN * kBK * 4) < 2)
     p.BN = (p.BN / 2 + 31) / 32 * 32;
   // Long k-loops keep the tensor pipe busy only with several stages in
-  // flight; their epilogue is rare, so when that buys a third stage they
-  // give up half the epilogue warps (and their staging tiles).
+  // flight; their epilogue is rare, so when that buys a third stage, or the
+  // second one, they give up half the epilogue warps (and their staging
+  // tiles).
   p.epi_warps = kEpiWarps;
   {
     const int bn_stage = (int)(2 * kATileBytes + 2 * (uint32_t)p.BN * kBK * 4);
     const int half_budget = 227 * 1024 - 1024 - 4 * (int)kEpiSlot - 512;
-    if (kb_total >= 8 && full_budget / bn_stage < 3 && half_budget / bn_stage >= 3)
+    if (kb_total >= 8 && full_budget / bn_stage < 3 &&
+        (half_budget / bn_stage >= 3 || full_budget / bn_stage < 2))
       p.epi_warps = 4;
     // One or two k-blocks per tile (K <= 64, the expand layers): the
     // converters are mostly idle and the epilogue's per-chunk latency sets
