@@ -281,15 +281,17 @@ typedef struct spx_dwproj_params {
 int spx_op_dw_project_nhwc(spx_graph* g, const float* x, const float* w_dw, const float* b_dw,
                            const float* w_proj_hi, const float* w_proj_lo, const float* b_proj,
                            const float* residual, float* y, const spx_dwproj_params* p);
-/* 3x3 stride-2 convolution over 3-channel NHWC input (the MobileNetV2 /
- * EfficientNet-Lite0 stems, conv2d.comp through the Conv2d lowering of
- * scheduler.rs:321-427) on the tensor cores: each output pixel's 27 taps are
- * gathered into a GEMM row on chip and multiplied with the weights in
- * 3xTF32.  w_hi / w_lo: [oc][32] tf32 hi / lo of the OHWI weights flattened
- * to 27 taps and zero-padded to 32 (spx_weights_split of the padded copy).
- * p->ic must be 3, the kernel 3x3 with stride 2, oc <= 128 and a multiple of
- * 4, iw a multiple of 4; bias and activation are fused.  Other shapes:
- * SPX_ERR_UNSUPPORTED. */
+/* 3x3 or 7x7 stride-2 convolution over 3-channel NHWC input (the MobileNetV2
+ * / EfficientNet-Lite0 stems, conv2d.comp through the Conv2d lowering of
+ * scheduler.rs:321-427; ResNet-50's 7x7 stem, hlo_conv_nhwc_hwio through
+ * compiler.rs) on the tensor cores: each output pixel's k*k*3 taps are
+ * gathered into a GEMM row on chip, 32 taps per K block, and multiplied with
+ * the weights in 3xTF32.  w_hi / w_lo: [oc][kpad] tf32 hi / lo of the OHWI
+ * weights flattened to k*k*3 taps and zero-padded to kpad = 32 (3x3) or 160
+ * (7x7) (spx_weights_split of the padded copy).  p->ic must be 3, the kernel
+ * square 3x3 or 7x7 with stride 2 and pads below the kernel size, oc <= 128
+ * and a multiple of 4, iw a multiple of 4; bias and activation are fused.
+ * Other shapes: SPX_ERR_UNSUPPORTED. */
 int spx_op_stem_conv_nhwc(spx_graph* g, const float* x, const float* w_hi, const float* w_lo,
                           const float* bias, float* y, const spx_conv_params* p);
 int spx_stem_conv_supported(const spx_conv_params* p);

@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(!STEM || NG == 1, "the stem builder is one group");
   static_assert(STEM || TN * CG * (TW / CW) * (TH / R) == kGroupThreads,
                 "one builder thread per (image, rows, column pair, channel pair)");
-  static_assert(!STEM || (TH * TW == 128 && S == 2 && KS == 3), "stem tile");
+  static_assert(!STEM || (TH * TW == 128 && S == 2 && (KS == 3 || KS == 7)), "stem tile");
   static_assert(TN * TH * TW <= 128, "a tile is at most 128 GEMM rows");
   static_assert(!STEM || TN == 1, "stem tiles hold one image");
   static_assert(TH % R == 0 && 32 % CB == 0, "tile shape");
@@ -349,61 +349,68 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (STEM && warp < kBuildWarps) {
     // ---------------- builders (stem): im2col -> A tile (raw, lo) ----------------
-    // Thread: GEMM row m (pixel) and half of its 32 K columns; k = (ky*3+kx)*3+c
-    // (OHWI weight order), zero for k >= 27.
+    // Thread: GEMM row m (pixel) and half of the 32 K columns of each K block;
+    // k = (ky*KS+kx)*3+c (OHWI weight order), zero for k >= KS*KS*3.  The
+    // producer streams the tile's input box once per K block.
+    constexpr int kTaps = KS * KS * 3;
     const int tid = threadIdx.x;
     const int m = tid & 127, khalf = tid >> 7;
     const int oy_l = m / TW, ox_l = m % TW;
     int j = 0, h = 0;
     uint32_t eph = 0, hph = 0;
-    for (int t = blockIdx.x; t < p.total; t += gridDim.x) {
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
       int nt, img, ty, tx;
       decode(t, nt, img, ty, tx);
       const int shift = (tx * TW * S - p.pl) * 3 - (((tx * TW * S - p.pl) * 3) & ~3);
-      bool ok = __all_sync(0xffffffffu,
-                           mb_wait(&empty[j], eph ^ 1, abort_flag, &g_dwp_status, kWaitNs, 64));
-      if (!ok) break;
       const int st_i = (t - (int)blockIdx.x) / (int)gridDim.x;
-      if (tid == 0) DWP_TRACE(1, st_i);
-      ok = __all_sync(0xffffffffu, mb_wait(&hfull[h], hph, abort_flag, &g_dwp_status, kWaitNs, 32));
-      if (!ok) break;
-      if (tid == 0) DWP_TRACE(2, st_i);
-      const float* in = reinterpret_cast<const float*>(halo + (size_t)h * p.halo_buf);
-      float vals[16];
+      for (int kb = 0; kb < p.kblocks; ++kb) {
+        ok = __all_sync(0xffffffffu,
+                        mb_wait(&empty[j], eph ^ 1, abort_flag, &g_dwp_status, kWaitNs, 64));
+        if (!ok) break;
+        if (tid == 0 && kb == 0) DWP_TRACE(1, st_i);
+        ok = __all_sync(0xffffffffu,
+                        mb_wait(&hfull[h], hph, abort_flag, &g_dwp_status, kWaitNs, 32));
+        if (!ok) break;
+        if (tid == 0 && kb == 0) DWP_TRACE(2, st_i);
+        const float* in = reinterpret_cast<const float*>(halo + (size_t)h * p.halo_buf);
+        float vals[16];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const int k = khalf * 16 + e;
-        const int ky = k / 9, kx = (k / 3) % 3, c = k % 3;
-        vals[e] = k < 27 ? in[(oy_l * S + ky) * kStemRow + shift + (ox_l * S + kx) * 3 + c] : 0.f;
-      }
-      __syncwarp();
-      if (lane == 0) {
+        for (int e = 0; e < 16; ++e) {
+          const int k = kb * 32 + khalf * 16 + e;
+          const int ky = k / (KS * 3), kx = (k / 3) % KS, c = k % 3;
+          vals[e] =
+              k < kTaps ? in[(oy_l * S + ky) * kStemRow + shift + (ox_l * S + kx) * 3 + c] : 0.f;
+        }
+        __syncwarp();
+        if (lane == 0) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          mb_arrive(&hempty[h]);
+        }
+        if (++h == p.hst) {
+          h = 0;
+          hph ^= 1;
+        }
+        uint8_t* a_raw = stages + (size_t)j * p.stage_bytes;
+        uint8_t* a_lo = a_raw + kAHalf;
+#pragma unroll
+        for (int qd = 0; qd < 4; ++qd) {
+          const int c16 = khalf * 4 + qd;
+          const uint32_t off = (uint32_t)m * 128u + (uint32_t)((c16 ^ (m & 7)) * 16);
+          const float4 v = make_float4(vals[4 * qd], vals[4 * qd + 1], vals[4 * qd + 2],
+                                       vals[4 * qd + 3]);
+          *reinterpret_cast<float4*>(a_raw + off) = v;
+          *reinterpret_cast<float4*>(a_lo + off) =
+              make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+        }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mb_arrive(&hempty[h]);
-      }
-      if (++h == p.hst) {
-        h = 0;
-        hph ^= 1;
-      }
-      uint8_t* a_raw = stages + (size_t)j * p.stage_bytes;
-      uint8_t* a_lo = a_raw + kAHalf;
-#pragma unroll
-      for (int qd = 0; qd < 4; ++qd) {
-        const int c16 = khalf * 4 + qd;
-        const uint32_t off = (uint32_t)m * 128u + (uint32_t)((c16 ^ (m & 7)) * 16);
-        const float4 v = make_float4(vals[4 * qd], vals[4 * qd + 1], vals[4 * qd + 2],
-                                     vals[4 * qd + 3]);
-        *reinterpret_cast<float4*>(a_raw + off) = v;
-        *reinterpret_cast<float4*>(a_lo + off) =
-            make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mb_arrive(&afull[j]);
-      if (tid == 0) DWP_TRACE(4, st_i);
-      if (++j == p.nst) {
-        j = 0;
-        eph ^= 1;
+        __syncwarp();
+        if (lane == 0) mb_arrive(&afull[j]);
+        if (tid == 0 && kb == 0) DWP_TRACE(4, st_i);
+        if (++j == p.nst) {
+          j = 0;
+          eph ^= 1;
+        }
       }
     }
   } else if (!STEM && warp < kBuildWarps) {
@@ -838,16 +845,18 @@ bool al16(const void* v) { return ((uintptr_t)v & 15) == 0; }
 // The stem instantiation: 8 x 16 output pixels per tile, one 32-wide K block.
 constexpr int kStemTH = 8, kStemTW = 16;
 
+template <int KS>
 int launch_stem(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
                 const float* w_lo, const float* bias, float* y, const spx_conv_params* q) {
-  constexpr int IH = (kStemTH - 1) * 2 + 3, IW = (kStemTW - 1) * 2 + 3;
+  constexpr int IH = (kStemTH - 1) * 2 + KS, IW = (kStemTW - 1) * 2 + KS;
+  constexpr int kKPad = (KS * KS * 3 + 31) / 32 * 32;  // weights [oc][kKPad], zero past the taps
   constexpr int kRow = (IW * 3 + 3 + 3) / 4 * 4;
   constexpr uint32_t kHalo = IH * kRow * 4;
   DwpArgs p{};
   p.n = q->n;
   p.ih = q->ih;
   p.iw = q->iw;
-  p.ce = 32;
+  p.ce = kKPad;
   p.oh = q->oh;
   p.ow = q->ow;
   p.cout = q->oc;
@@ -857,7 +866,7 @@ int launch_stem(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
   p.pl = q->pad_left;
   p.tiles_h = (int)ceil_div(q->oh, kStemTH);
   p.tiles_w = (int)ceil_div(q->ow, kStemTW);
-  p.kblocks = 1;
+  p.kblocks = kKPad / 32;
   const int64_t total = (int64_t)q->n * p.tiles_h * p.tiles_w;
   if (total > INT32_MAX) return fail(SPX_ERR_UNSUPPORTED, "stem: too many tiles");
   p.total = (int)total;
@@ -896,8 +905,8 @@ int launch_stem(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
     if (r != CUDA_SUCCESS) return fail(SPX_ERR_CUDA, "stem: input map encode failed (%d)", (int)r);
   }
   for (int b = 0; b < 2; ++b) {
-    cuuint64_t dims[2] = {32, (cuuint64_t)q->oc};
-    cuuint64_t strides[1] = {128};
+    cuuint64_t dims[2] = {(cuuint64_t)kKPad, (cuuint64_t)q->oc};
+    cuuint64_t strides[1] = {(cuuint64_t)kKPad * 4};
     cuuint32_t box[2] = {32, (cuuint32_t)p.np};
     cuuint32_t es[2] = {1, 1};
     CUresult r = fn(b ? &ml : &mh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)(b ? w_lo : w_hi),
@@ -906,7 +915,7 @@ int launch_stem(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(SPX_ERR_CUDA, "stem: weight map encode failed (%d)", (int)r);
   }
-  auto kern = dwproj_kernel<3, 2, kStemTH, kStemTW, 32, 4, true>;
+  auto kern = dwproj_kernel<KS, 2, kStemTH, kStemTW, 32, 4, true>;
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [&] {
@@ -946,16 +955,18 @@ int launch_stem_tc(cudaStream_t s, int64_t* cnt, const float* x, const float* w_
                    const float* w_lo, const float* bias, float* y, const spx_conv_params* q,
                    bool dry_run) {
   if (!q) return fail(SPX_ERR_INVALID_ARGUMENT, "stem: null params");
-  if (q->ic != 3 || q->kh != 3 || q->kw != 3 || q->stride_h != 2 || q->stride_w != 2 ||
-      q->dilation_h != 1 || q->dilation_w != 1 || q->oc <= 0 || q->oc > 128 || q->oc % 4 ||
-      q->iw % 4 || q->n <= 0 || q->oh <= 0 || q->ow <= 0 || q->pad_top < 0 || q->pad_left < 0 ||
-      q->pad_top > 2 || q->pad_left > 2)
-    return fail(SPX_ERR_UNSUPPORTED, "stem: 3x3 stride-2 over 3 channels (iw % 4 == 0, oc <= 128) only");
+  if (q->ic != 3 || (q->kh != 3 && q->kh != 7) || q->kw != q->kh || q->stride_h != 2 ||
+      q->stride_w != 2 || q->dilation_h != 1 || q->dilation_w != 1 || q->oc <= 0 ||
+      q->oc > 128 || q->oc % 4 || q->iw % 4 || q->n <= 0 || q->oh <= 0 || q->ow <= 0 ||
+      q->pad_top < 0 || q->pad_left < 0 || q->pad_top >= q->kh || q->pad_left >= q->kw)
+    return fail(SPX_ERR_UNSUPPORTED,
+                "stem: 3x3 or 7x7 stride-2 over 3 channels (iw % 4 == 0, oc <= 128) only");
   if (dry_run) return SPX_OK;
   if (!x || !w_hi || !w_lo || !y || !al16(x) || !al16(w_hi) || !al16(w_lo) || !al16(y) ||
       (bias && !al16(bias)))
     return fail(SPX_ERR_INVALID_ARGUMENT, "stem: null or unaligned tensor");
-  return launch_stem(s, cnt, x, w_hi, w_lo, bias, y, q);
+  return q->kh == 7 ? launch_stem<7>(s, cnt, x, w_hi, w_lo, bias, y, q)
+                    : launch_stem<3>(s, cnt, x, w_hi, w_lo, bias, y, q);
 }
 
 // Returns SPX_ERR_UNSUPPORTED (without launching) for shapes the fused kernel

@@ -411,6 +411,23 @@ class HloExecutor:
             self.done.update(consumed)
         out = self._new(op.shape)
         pointwise = kh == 1 and kw == 1 and tuple(st) == (1, 1)
+        # A 3x3 / 7x7 stride-2 stem over 3 channels (ResNet-50's first conv):
+        # the tensor-core stem, im2col on chip, weights padded and split once.
+        if (self.presplit and ic == 3 and kh == kw and kh in (3, 7) and tuple(st) == (2, 2)
+                and res is None and pd[0][0] < kh and pd[1][0] < kw
+                and self.g.stem_supported(x.t, out.t, pad=(pd[0][0], pd[1][0]), kernel=kh)):
+            wt = self._weight_buf(wname)
+            split = self.g.stem_weights(np.ascontiguousarray(w.transpose(3, 0, 1, 2)))
+            self.plan.append(("conv", dict(x=x.t, w=wt, bias=bias, y=out.t, stride=tuple(st),
+                                           pad=(pd[0][0], pd[1][0]), weight_layout=_lib.WEIGHT_HWIO,
+                                           activation=_lib.ACT_RELU if relu else _lib.ACT_NONE,
+                                           residual=None, w_split=split, stem=kh)))
+            self._set(last, out)
+            if relu:
+                self.nonneg.add(last)
+            if last != op.name:
+                self._set(op.name, out)
+            return
         # Tensor-core convs (pointwise GEMM, or the implicit GEMM of KxK /
         # strided convs over 32-channel blocks) take an OHWI copy, pre-split once.
         if pointwise or w.shape[2] % 32 == 0:
@@ -663,6 +680,10 @@ class HloExecutor:
             elif k == "select":
                 _, tp, ta, tb, ty, d, sp, sa, sb = step
                 g.select(tp, ta, tb, ty, d, sp, sa, sb)
+            elif k == "conv" and step[1].get("stem"):
+                p = step[1]
+                g.stem_conv_nhwc(p["x"], p["w_split"], p["bias"], p["y"], stride=p["stride"],
+                                 pad=p["pad"], activation=p["activation"], kernel=p["stem"])
             elif k == "conv":
                 p = step[1]
                 g.conv2d_nhwc(p["x"], p["w"], p["bias"], p["y"], stride=p["stride"], pad=p["pad"],

@@ -290,28 +290,30 @@ class Graph:
                                             self._p(y), ctypes.byref(p)))
 
     @staticmethod
-    def _stem_params(x, y, stride, pad, activation):
+    def _stem_params(x, y, stride, pad, activation, kernel=3):
         n, ih, iw, ic = x.shape
         _, oh, ow, oc = y.shape
-        return _lib.ConvParams(n, ih, iw, ic, oc, oh, ow, 3, 3, stride[0], stride[1], pad[0],
-                               pad[1], 1, 1, _lib.WEIGHT_OHWI, activation)
+        return _lib.ConvParams(n, ih, iw, ic, oc, oh, ow, kernel, kernel, stride[0], stride[1],
+                               pad[0], pad[1], 1, 1, _lib.WEIGHT_OHWI, activation)
 
     def stem_supported(self, x, y, *, stride=(2, 2), pad=(0, 0),
-                       activation=_lib.ACT_NONE) -> bool:
-        p = self._stem_params(x, y, stride, pad, activation)
+                       activation=_lib.ACT_NONE, kernel=3) -> bool:
+        p = self._stem_params(x, y, stride, pad, activation, kernel)
         return bool(self._l.spx_stem_conv_supported(ctypes.byref(p)))
 
     def stem_weights(self, w_ohwi: np.ndarray) -> tuple:
-        """[oc][3][3][3] OHWI weights -> tensor-core (hi, lo) of the [oc][32]
-        copy (27 taps, zero-padded to 32) for stem_conv_nhwc."""
-        oc = w_ohwi.shape[0]
-        pad = np.zeros((oc, 32), np.float32)
-        pad[:, :27] = np.asarray(w_ohwi, np.float32).reshape(oc, 27)
+        """[oc][k][k][3] OHWI weights (k = 3 or 7) -> tensor-core (hi, lo) of
+        the [oc][kpad] copy (k*k*3 taps, zero-padded to a multiple of 32) for
+        stem_conv_nhwc."""
+        w = np.asarray(w_ohwi, np.float32)
+        oc, taps = w.shape[0], int(np.prod(w.shape[1:]))
+        pad = np.zeros((oc, -(-taps // 32) * 32), np.float32)
+        pad[:, :taps] = w.reshape(oc, taps)
         return self.weights_split(self.tensor(pad))
 
     def stem_conv_nhwc(self, x, w_split, bias, y, *, stride=(2, 2), pad=(0, 0),
-                       activation=_lib.ACT_NONE):
-        p = self._stem_params(x, y, stride, pad, activation)
+                       activation=_lib.ACT_NONE, kernel=3):
+        p = self._stem_params(x, y, stride, pad, activation, kernel)
         check(self._l.spx_op_stem_conv_nhwc(self.h, self._p(x), self._p(w_split[0]),
                                             self._p(w_split[1]), self._p(bias), self._p(y),
                                             ctypes.byref(p)))

@@ -183,6 +183,26 @@ def test_stem_conv_matches_float64(g, n, ih, iw, oc, pad):
     assert np.abs(got - ref).max() / np.abs(ref).max() <= 2.5e-8 * 27 + 1e-6
 
 
+@pytest.mark.parametrize("n,ih,iw,oc,pad", [(2, 224, 224, 64, (3, 3)), (3, 20, 24, 32, (2, 2)),
+                                         (1, 17, 16, 12, (3, 1))])
+def test_stem_7x7_matches_float64(g, n, ih, iw, oc, pad):
+    """The 7x7 stride-2 tensor-core stem (ResNet-50's first conv: 147 taps in
+    five 32-wide K blocks) against float64, with ReLU; pad 3 exercises row box
+    starts that round down below the map and past its left edge."""
+    oh = (ih + 2 * pad[0] - 7) // 2 + 1
+    ow = (iw + 2 * pad[1] - 7) // 2 + 1
+    x = _r(n, ih, iw, 3, scale=2.0)
+    w = _r(oc, 7, 7, 3, scale=0.2)
+    b = _r(oc, scale=0.1)
+    dx, dy = g.tensor(x), g.alloc((n, oh, ow, oc))
+    assert g.stem_supported(dx, dy, pad=pad, activation=_lib.ACT_RELU, kernel=7)
+    g.stem_conv_nhwc(dx, g.stem_weights(w), g.tensor(b), dy, pad=pad,
+                     activation=_lib.ACT_RELU, kernel=7)
+    ref = np.maximum(R.conv_nhwc(x, w.transpose(1, 2, 3, 0), (2, 2), pad, (oh, ow)) + b, 0)
+    got = dy.download()
+    assert np.abs(got - ref).max() / np.abs(ref).max() <= 2.5e-8 * 147 + 1e-6
+
+
 def test_stem_rejects_other_shapes(g):
     x, y = g.alloc((1, 16, 18, 3)), g.alloc((1, 8, 9, 32))
     assert not g.stem_supported(x, y)                     # iw % 4
