@@ -353,6 +353,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // k = (ky*KS+kx)*3+c (OHWI weight order), zero for k >= KS*KS*3.  The
     // producer streams the tile's input box once per K block.
     constexpr int kTaps = KS * KS * 3;
+    constexpr int kKB = (kTaps + 31) / 32;  // K blocks (p.kblocks); unrolled so every tap's
+                                            // halo offset is a compile-time constant
     const int tid = threadIdx.x;
     const int m = tid & 127, khalf = tid >> 7;
     const int oy_l = m / TW, ox_l = m % TW;
@@ -364,7 +366,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       decode(t, nt, img, ty, tx);
       const int shift = (tx * TW * S - p.pl) * 3 - (((tx * TW * S - p.pl) * 3) & ~3);
       const int st_i = (t - (int)blockIdx.x) / (int)gridDim.x;
-      for (int kb = 0; kb < p.kblocks; ++kb) {
+      const float* const base = reinterpret_cast<const float*>(halo) + oy_l * S * kStemRow +
+                                shift + ox_l * S * 3;
+#pragma unroll
+      for (int kb = 0; kb < kKB; ++kb) {
         ok = __all_sync(0xffffffffu,
                         mb_wait(&empty[j], eph ^ 1, abort_flag, &g_dwp_status, kWaitNs, 64));
         if (!ok) break;
@@ -373,15 +378,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                         mb_wait(&hfull[h], hph, abort_flag, &g_dwp_status, kWaitNs, 32));
         if (!ok) break;
         if (tid == 0 && kb == 0) DWP_TRACE(2, st_i);
-        const float* in = reinterpret_cast<const float*>(halo + (size_t)h * p.halo_buf);
+        const float* in = base + (size_t)h * (p.halo_buf / 4);
         float vals[16];
+        // khalf is warp-uniform: each branch's 16 offsets are constants.
+        auto gather = [&](auto half) {
+          constexpr int kh = decltype(half)::value;
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int k = kb * 32 + khalf * 16 + e;
-          const int ky = k / (KS * 3), kx = (k / 3) % KS, c = k % 3;
-          vals[e] =
-              k < kTaps ? in[(oy_l * S + ky) * kStemRow + shift + (ox_l * S + kx) * 3 + c] : 0.f;
-        }
+          for (int e = 0; e < 16; ++e) {
+            const int k = kb * 32 + kh * 16 + e;
+            const int ky = k / (KS * 3), kx = (k / 3) % KS, c = k % 3;
+            vals[e] = k < kTaps ? in[ky * kStemRow + kx * 3 + c] : 0.f;
+          }
+        };
+        if (khalf) gather(std::integral_constant<int, 1>{});
+        else gather(std::integral_constant<int, 0>{});
         __syncwarp();
         if (lane == 0) {
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -882,14 +892,18 @@ int launch_stem(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
   p.bp = bias;
   p.y = y;
   p.act_p = q->activation;
-  p.nst = 2;
-  const uint32_t fixed =
-      1024 + 2 * p.stage_bytes + kEpiGroups * kEStage + kBarBytes + kBiasBytes;
+  // As many A/B stages as fit next to two halo slots (up to "dwp_stages"),
+  // then up to four halo slots.
   const uint32_t cap = 227 * 1024;
-  int hst = 0;
-  while (hst < 4 && fixed + (uint32_t)(hst + 1) * p.halo_buf <= cap) ++hst;
-  p.hst = hst;
-  const uint32_t smem = fixed + (uint32_t)hst * p.halo_buf;
+  auto need = [&](int nst, int hst) {
+    return 1024 + (uint32_t)nst * p.stage_bytes + kEpiGroups * kEStage + kBarBytes + kBiasBytes +
+           (uint32_t)hst * p.halo_buf;
+  };
+  p.nst = 2;
+  while (p.nst < g_dwp_stages && need(p.nst + 1, 2) <= cap) ++p.nst;
+  p.hst = 2;
+  while (p.hst < 4 && need(p.nst, p.hst + 1) <= cap) ++p.hst;
+  const uint32_t smem = need(p.nst, p.hst);
   EncodeFn fn = encoder();
   if (!fn) return fail(SPX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   CUtensorMap mx, mh, ml, my;
