@@ -120,6 +120,10 @@ int spx_device_status(void);
  * are identical for every value.
  * "ar_wait_limit_us": bound of the peer all-reduce's wait for the other ranks
  * (default 2,000,000; 1,000 .. 60,000,000).
+ * "tc_cat": 1 (default) = tensor-core GEMM tiles up to 128 columns wide issue
+ * raw A x [B hi; B lo] as one product of twice the width plus lo A x hi B
+ * (two wide MMAs instead of three narrow ones per k-step; the epilogue adds
+ * the accumulator's two halves); 0 = three products into one accumulator.
  * "tc_lo_tmem": 1 = with pre-split weights and several k-blocks the
  * activations' tf32 lo terms are written to tensor memory and the lo*hi MMA
  * reads its A operand from there; 0 (default) = lo terms in shared memory. */

@@ -49,6 +49,7 @@ __device__ int g_tc_status = 0;
 int g_tc_epi12 = 1;
 int g_tc_conv2 = 1;
 int g_tc_lo_tmem = 0;
+int g_tc_cat = 1;
 
 #ifdef SPX_TC_TRACE
 // Development-only pipeline trace of CTA 0 (not compiled into the library).
@@ -111,6 +112,9 @@ struct TcArgs {
   int lo_tmem;      // activation lo terms in two TMEM slots (A operand from TMEM)
   int lo_col;       // first TMEM column of the two 32-column lo slots
   uint32_t smem_bytes;  // dynamic shared memory of the launch
+  int cat;              // raw A x [B hi; B lo] as one N = 2 BN product (+ lo x hi): an
+                        // accumulator spans 2 BN columns, the epilogue adds the halves
+  uint32_t idesc2;      // instruction descriptor with N = 2 BN
   int bias_n;           // bias entries staged in shared memory (n_tiles * BN), 0 = read from global
   int epi_warps;  // epilogue warps in use (4, 8 or 12): long k-loops trade them for stages,
                   // 1-block k-loops take 12 (warps 8-11 leave the converters)
@@ -384,6 +388,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// v += the 32 columns at taddr (two 16-column loads, fewer live registers).
+__device__ __forceinline__ void add_tmem32(uint32_t taddr, float (&v)[32]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr + (uint32_t)(h * 16)));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[16 * h + i] += __uint_as_float(r[i]);
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB,
@@ -518,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!bar_wait(&tempty[acc], aph ^ 1, abort_flag, kTimeoutNs, 64)) goto mma_done;
         TC_TRACE(2, (t - blockIdx.x) / gridDim.x);
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(acc * p.BN);
+        const uint32_t d = tmem + (uint32_t)(acc * p.BN * (1 + p.cat));
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!bar_wait(&conv[s], ph, abort_flag, kTimeoutNs, 64)) goto mma_done;
           if (kb == 0) TC_TRACE(3, (t - blockIdx.x) / gridDim.x);
@@ -536,6 +558,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t off = k * 32;  // 8 tf32 = 32 bytes along K
             const uint64_t dah = sdesc(a_hi + off), dal = sdesc(a_lo + off);
             const uint64_t dbh = sdesc(b_hi + off), dbl = sdesc(b_lo + off);
+            if (p.cat) {
+              // B hi and lo are adjacent 128-byte rows: one N = 2 BN operand.
+              umma_tf32(d, dah, dbh, p.idesc2, (kb | k) ? 1u : 0u);
+              umma_tf32(d, dal, dbh, p.idesc, 1u);
+              continue;
+            }
             if (p.lo_tmem)
               umma_tf32_ta(d, lo_t + (uint32_t)(k * 8), dbh, p.idesc, (kb | k) ? 1u : 0u);
             else
@@ -661,7 +689,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (__any_sync(0xffffffffu, !ok)) break;
       tc_fence_after();
       const int quarter = warp & 3;
-      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.BN);
+      const uint32_t tbase =
+          tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.BN * (1 + p.cat));
       const int row0 = mt * kBM + quarter * 32;
       for (int c0 = ((warp % wpg) >> 2) * 32; c0 < p.BN; c0 += 32 * (wpg / 4)) {
         const int n0 = nt * p.BN + c0;
@@ -683,6 +712,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (trc) TC_TRACE(9, (t - blockIdx.x) / gridDim.x);
         float v[32];
         tmem_ld32(tbase + (uint32_t)c0, v);
+        if (p.cat) add_tmem32(tbase + (uint32_t)(p.BN + c0), v);
         if (trc) TC_TRACE(10, (t - blockIdx.x) / gridDim.x);
         if (p.res) {
           ok = bar_wait(&rfull[warp], rph, abort_flag) && ok;
@@ -746,11 +776,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (__any_sync(0xffffffffu, !ok)) break;
       tc_fence_after();
       const int quarter = warp & 3;
-      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.BN);
+      const uint32_t tbase =
+          tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.BN * (1 + p.cat));
       const int64_t row0 = (int64_t)mt * kBM + quarter * 32;
       for (int c0 = (warp >> 2) * 32; c0 < p.BN; c0 += 32 * (p.epi_warps / 4)) {
         float v[32];
         tmem_ld32(tbase + (uint32_t)c0, v);  // lane = row, 32 consecutive columns
+        if (p.cat) add_tmem32(tbase + (uint32_t)(p.BN + c0), v);
         float4* trow = reinterpret_cast<float4*>(tile + lane * kEpiStride);
 #pragma unroll
         for (int q = 0; q < 8; ++q)
@@ -1630,6 +1662,7 @@ int plan_gemm_tc(TcArgs& p, int M, int N, int K, bool presplit, bool conv, int m
   // lo*hi MMA reads A from TMEM), so a stage holds only the raw A tile and B.
   p.lo_tmem = g_tc_lo_tmem && p.presplit && p.k_blocks >= 2 && p.epi_warps <= kEpiWarps &&
               p.nacc * p.BN + 2 * kBK <= 512;
+  p.cat = g_tc_cat && p.BN <= 128 && !p.lo_tmem;
   p.lo_col = p.nacc * p.BN;
   const int budget = 227 * 1024 - 1024 - p.epi_warps * (int)kEpiSlot - 512 -
                      (p.b_resident ? 2 * (int)p.b_bytes : 0);
@@ -1646,12 +1679,13 @@ int plan_gemm_tc(TcArgs& p, int M, int N, int K, bool presplit, bool conv, int m
   p.conv_groups =
       (g_tc_conv2 && p.epi_warps <= kEpiWarps && p.k_blocks > 1 && p.stages % 2 == 0) ? 2 : 1;
   uint32_t cols = 32;
-  while (cols < (uint32_t)(p.nacc * p.BN + (p.lo_tmem ? 2 * kBK : 0))) cols <<= 1;
+  while (cols < (uint32_t)(p.nacc * p.BN * (1 + p.cat) + (p.lo_tmem ? 2 * kBK : 0))) cols <<= 1;
   p.tmem_cols = cols;
   p.idesc = (1u << 4)                          // accumulator F32
             | (2u << 7) | (2u << 10)           // A, B: TF32
             | ((uint32_t)(p.BN >> 3) << 17)    // N
             | ((uint32_t)(kBM >> 4) << 24);    // M
+  p.idesc2 = (p.idesc & ~(0x3Fu << 17)) | ((uint32_t)((2 * p.BN) >> 3) << 17);
   p.smem_bytes = 1024 + (uint32_t)p.stages * p.stage_bytes +
                  (p.b_resident ? 2 * p.b_bytes : 0u) + (uint32_t)p.epi_warps * kEpiSlot + 512;
   // The bias goes to shared memory only where the plan leaves room for it.

@@ -487,6 +487,11 @@ int spx_set_option(const char* name, int64_t value) {
     g_tc_epi12 = (int)value;
     return SPX_OK;
   }
+  if (n == "tc_cat") {
+    if (value < 0 || value > 1) return fail(SPX_ERR_INVALID_ARGUMENT, "tc_cat must be 0..1");
+    g_tc_cat = (int)value;
+    return SPX_OK;
+  }
   if (n == "tc_lo_tmem") {
     if (value < 0 || value > 1) return fail(SPX_ERR_INVALID_ARGUMENT, "tc_lo_tmem must be 0..1");
     g_tc_lo_tmem = (int)value;
@@ -539,6 +544,7 @@ int64_t spx_get_option(const char* name) {
   if (n == "tc_wide_epilogue") return g_tc_epi12;
   if (n == "tc_conv_groups") return g_tc_conv2 ? 2 : 1;
   if (n == "tc_lo_tmem") return g_tc_lo_tmem;
+  if (n == "tc_cat") return g_tc_cat;
   if (n == "ar_wait_limit_us") return g_ar_wait_limit_us;
   if (n == "pw_gemm") return g_pw_gemm;
   if (n == "dwp_groups") return g_dwp_groups;

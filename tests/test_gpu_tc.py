@@ -155,15 +155,19 @@ def test_tc_lo_terms_in_tmem_match_shared_memory(g, M, N, K):
     da, dw, db = g.tensor(a), g.tensor(w), g.tensor(bias)
     split = g.weights_split(dw)
     outs = []
-    for lo_tmem in (0, 1):
-        _lib.set_option("tc_lo_tmem", lo_tmem)
-        try:
-            dc = g.alloc((M, N))
-            g.gemm(da, dw, dc, m=M, n=N, k=K, a_strides=(0, K, 1), b_strides=(0, 1, K),
-                   c_strides=(0, N), bias=db, activation=_lib.ACT_RELU6, b_split=split)
-            outs.append(dc.download())
-        finally:
-            _lib.set_option("tc_lo_tmem", 0)
+    _lib.set_option("tc_cat", 0)  # the three-product form, the one lo_tmem issues
+    try:
+        for lo_tmem in (0, 1):
+            _lib.set_option("tc_lo_tmem", lo_tmem)
+            try:
+                dc = g.alloc((M, N))
+                g.gemm(da, dw, dc, m=M, n=N, k=K, a_strides=(0, K, 1), b_strides=(0, 1, K),
+                       c_strides=(0, N), bias=db, activation=_lib.ACT_RELU6, b_split=split)
+                outs.append(dc.download())
+            finally:
+                _lib.set_option("tc_lo_tmem", 0)
+    finally:
+        _lib.set_option("tc_cat", 1)
     np.testing.assert_array_equal(outs[0], outs[1])
     ref = np.clip(a[:4096].astype(np.float64) @ w.T.astype(np.float64) + bias, 0, 6)
     err = np.abs(outs[1][:4096] - ref).max() / max(np.abs(ref).max(), 1e-30)
@@ -179,13 +183,63 @@ def test_conv_tc_lo_terms_in_tmem(g):
     dx, dw, db = g.tensor(x), g.tensor(w), g.tensor(b)
     split = g.weights_split(dw)
     outs = []
-    for lo_tmem in (0, 1):
-        _lib.set_option("tc_lo_tmem", lo_tmem)
-        try:
-            dy = g.alloc((n, oh, oh, oc))
-            g.conv2d_nhwc(dx, dw, db, dy, stride=(s, s), pad=(pad, pad),
-                          activation=_lib.ACT_RELU, w_split=split)
-            outs.append(dy.download())
-        finally:
-            _lib.set_option("tc_lo_tmem", 0)
+    _lib.set_option("tc_cat", 0)  # the three-product form, the one lo_tmem issues
+    try:
+        for lo_tmem in (0, 1):
+            _lib.set_option("tc_lo_tmem", lo_tmem)
+            try:
+                dy = g.alloc((n, oh, oh, oc))
+                g.conv2d_nhwc(dx, dw, db, dy, stride=(s, s), pad=(pad, pad),
+                              activation=_lib.ACT_RELU, w_split=split)
+                outs.append(dy.download())
+            finally:
+                _lib.set_option("tc_lo_tmem", 0)
+    finally:
+        _lib.set_option("tc_cat", 1)
     np.testing.assert_array_equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("M,N,K,conv", [(802816, 24, 144, 0), (50176, 64, 384, 0), (517, 144, 96, 0),
+                                        (4096, 32, 200, 0), (2, 64, 576, 1)])
+def test_tc_concatenated_product_matches_three_products(g, M, N, K, conv):
+    """Option tc_cat: raw A x [hi; lo] as one product of twice the tile width
+    plus lo x hi, against the three separate products and float64 (same
+    terms, another summation order: equal within the 3xTF32 bound).  conv = 1
+    runs a 3x3 implicit-GEMM convolution (n = M images of 16 x 16 x 64)."""
+    outs = []
+    if conv:
+        x = _r(M, 16, 16, 64)
+        w = _r(N, 3, 3, 64, scale=1.0 / np.sqrt(K))
+        b = _r(N)
+        dx, dw, db = g.tensor(x), g.tensor(w), g.tensor(b)
+        split = g.weights_split(dw)
+        for cat in (0, 1):
+            _lib.set_option("tc_cat", cat)
+            try:
+                dy = g.alloc((M, 16, 16, N))
+                g.conv2d_nhwc(dx, dw, db, dy, pad=(1, 1), w_split=split)
+                outs.append(dy.download())
+            finally:
+                _lib.set_option("tc_cat", 1)
+        ref = R.conv_nhwc(x, w.transpose(1, 2, 3, 0), (1, 1), (1, 1), (16, 16)) + b
+    else:
+        a = _r(M, K)
+        w = _r(N, K, scale=1.0 / np.sqrt(K))
+        bias = _r(N)
+        da, dw, db = g.tensor(a), g.tensor(w), g.tensor(bias)
+        split = g.weights_split(dw)
+        for cat in (0, 1):
+            _lib.set_option("tc_cat", cat)
+            try:
+                dc = g.alloc((M, N))
+                g.gemm(da, dw, dc, m=M, n=N, k=K, a_strides=(0, K, 1), b_strides=(0, 1, K),
+                       c_strides=(0, N), bias=db, b_split=split)
+                outs.append(dc.download())
+            finally:
+                _lib.set_option("tc_cat", 1)
+        ref = a[:4096].astype(np.float64) @ w.T.astype(np.float64) + bias
+        outs = [o[:4096] for o in outs]
+    scale = np.abs(ref).max()
+    for o in outs:
+        assert np.abs(o - ref).max() / scale <= 2.5e-8 * K + 1e-6
+    assert np.abs(outs[0] - outs[1]).max() / scale <= 2 * (2.5e-8 * K + 1e-6)
