@@ -66,6 +66,14 @@ namespace {
 
 using namespace sm100;
 
+// AG = 0: both activations in group 0 (none / clamps), only those epilogues
+// are instantiated; AG = 1: any activation.
+template <int AG, class F>
+__device__ __forceinline__ void with_act_sel(int act, F&& f) {
+  if constexpr (AG == 0) with_act_group<0>(act, static_cast<F&&>(f));
+  else with_act(act, static_cast<F&&>(f));
+}
+
 constexpr int kBuildWarps = 8;
 constexpr int kProdWarp = 8;
 constexpr int kMmaWarp = 9;
@@ -107,7 +115,7 @@ struct DwpArgs {
 // one 32-wide K block): the halo slot is a 3-D box of whole input rows
 // (W * 3 floats), the builders gather each pixel's 27 taps into its A row.
 template <int KS, int S, int TH, int TW, int CB, int R, bool STEM = false, int TN = 1, int NG = 1,
-          int CW = 2>
+          int CW = 2, int AG = 0>
 __global__ void __launch_bounds__(kThreads, 1)
     dwproj_kernel(const __grid_constant__ CUtensorMap tmX,
                   const __grid_constant__ CUtensorMap tmBhi,
@@ -528,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t c16s = (uint32_t)(cl >> 2) << 4;  // 16-byte chunk, in bytes
           const uint32_t in16 = (uint32_t)(cl & 3) * 4;    // byte offset inside the chunk
           const uint32_t row0 = (uint32_t)((im * TH * TW + rg * R * TW + ox_l) * 128) + in16;
-          with_act(p.act_d, [&](auto tag) {
+          with_act_sel<AG>(p.act_d, [&](auto tag) {
             constexpr int A = decltype(tag)::value;
             // Clamped activations cannot produce inf: the lo term needs no
             // special-value check there.
@@ -629,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         float4* row = reinterpret_cast<float4*>(stg + lane * 128);
-        with_act(p.act_p, [&](auto tag) {
+        with_act_sel<AG>(p.act_p, [&](auto tag) {
           constexpr int A = decltype(tag)::value;
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
@@ -837,11 +845,17 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
     if (r != CUDA_SUCCESS)
       return fail(SPX_ERR_CUDA, "dw_project: depthwise weight map encode failed (%d)", (int)r);
   }
-  auto kern = dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG, CW>;
+  const bool heavy = act_group(p.act_d) || act_group(p.act_p);
+  auto kern = heavy ? dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG, CW, 1>
+                    : dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG, CW, 0>;
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [&] {
-    attr = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+    attr = cudaFuncSetAttribute(dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG, CW, 0>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+    if (attr == cudaSuccess)
+      attr = cudaFuncSetAttribute(dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG, CW, 1>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
   });
   if (attr != cudaSuccess) return check_cuda(attr, "dw_project: smem attribute");
   const int grid = (int)(p.total < num_sms() ? p.total : num_sms());
@@ -929,11 +943,16 @@ int launch_stem(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(SPX_ERR_CUDA, "stem: weight map encode failed (%d)", (int)r);
   }
-  auto kern = dwproj_kernel<KS, 2, kStemTH, kStemTW, 32, 4, true>;
+  auto kern = act_group(p.act_p) ? dwproj_kernel<KS, 2, kStemTH, kStemTW, 32, 4, true, 1, 1, 2, 1>
+                                 : dwproj_kernel<KS, 2, kStemTH, kStemTW, 32, 4, true, 1, 1, 2, 0>;
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [&] {
-    attr = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+    attr = cudaFuncSetAttribute(dwproj_kernel<KS, 2, kStemTH, kStemTW, 32, 4, true, 1, 1, 2, 0>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+    if (attr == cudaSuccess)
+      attr = cudaFuncSetAttribute(dwproj_kernel<KS, 2, kStemTH, kStemTW, 32, 4, true, 1, 1, 2, 1>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
   });
   if (attr != cudaSuccess) return check_cuda(attr, "stem: smem attribute");
   const int grid = (int)(p.total < num_sms() ? p.total : num_sms());

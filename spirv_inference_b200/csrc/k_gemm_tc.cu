@@ -406,6 +406,7 @@ __device__ __forceinline__ void add_tmem32(uint32_t taddr, float (&v)[32]) {
   }
 }
 
+template <int AG>  // activation group (act_group of p.act)
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB,
@@ -718,7 +719,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = bar_wait(&rfull[warp], rph, abort_flag) && ok;
           rph ^= 1;
         }
-        with_act(p.act, [&](auto tag) {
+        with_act_group<AG>(p.act, [&](auto tag) {
           constexpr int A = decltype(tag)::value;
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
@@ -806,7 +807,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float* op = &o.x;
           const float* bp = &b4.x;
           float* crow = p.c + m * p.ldc;
-          with_act(p.act, [&](auto tag) {
+          with_act_group<AG>(p.act, [&](auto tag) {
             constexpr int A = decltype(tag)::value;
             if (p.vec4 && n + 3 < p.N) {
               float4 r4 = p.res ? *reinterpret_cast<const float4*>(p.res + m * p.ldc + n)
@@ -1748,13 +1749,17 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    227 * 1024);
+    attr_err = cudaFuncSetAttribute(gemm_tc_kernel<0>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(gemm_tc_kernel<1>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
   if (attr_err != cudaSuccess) return check_cuda(attr_err, "gemm_tc: smem attribute");
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  gemm_tc_kernel<<<grid, kThreads, smem, s>>>(ma, mb, mblo, mc, mr, p);
+  (act_group(p.act) ? gemm_tc_kernel<1> : gemm_tc_kernel<0>)<<<grid, kThreads, smem, s>>>(
+      ma, mb, mblo, mc, mr, p);
   return after_launch(cnt, "gemm_tc");
 }
 

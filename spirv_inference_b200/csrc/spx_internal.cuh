@@ -92,6 +92,34 @@ __device__ __forceinline__ void with_act(int act, F&& f) {
     default: f(ActTag<SPX_ACT_NONE>{}); break;
   }
 }
+// Activation groups: a kernel instantiated once per group holds only its
+// group's specialised epilogues (less code in the instruction cache).  Group
+// 0: none and the clamps (ReLU, ReLU6, ReLU(-1, 1)); group 1: the
+// transcendental ones (tanh, GELU, SiLU).
+__host__ __device__ constexpr int act_group(int act) {
+  return (act == SPX_ACT_TANH || act == SPX_ACT_GELU_ERF || act == SPX_ACT_GELU_TANH ||
+          act == SPX_ACT_SILU)
+             ? 1
+             : 0;
+}
+template <int G, class F>
+__device__ __forceinline__ void with_act_group(int act, F&& f) {
+  if constexpr (G == 0) {
+    switch (act) {
+      case SPX_ACT_RELU: f(ActTag<SPX_ACT_RELU>{}); break;
+      case SPX_ACT_RELU6: f(ActTag<SPX_ACT_RELU6>{}); break;
+      case SPX_ACT_RELU_N1_TO_1: f(ActTag<SPX_ACT_RELU_N1_TO_1>{}); break;
+      default: f(ActTag<SPX_ACT_NONE>{}); break;
+    }
+  } else {
+    switch (act) {
+      case SPX_ACT_TANH: f(ActTag<SPX_ACT_TANH>{}); break;
+      case SPX_ACT_GELU_ERF: f(ActTag<SPX_ACT_GELU_ERF>{}); break;
+      case SPX_ACT_GELU_TANH: f(ActTag<SPX_ACT_GELU_TANH>{}); break;
+      default: f(ActTag<SPX_ACT_SILU>{}); break;
+    }
+  }
+}
 // Host-side twin: picks the kernel instantiation for a runtime code.
 template <class F>
 inline void host_with_act(int act, F&& f) {

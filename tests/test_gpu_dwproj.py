@@ -117,6 +117,28 @@ def test_builder_groups_and_stages_give_identical_results(g, n, ih, c, s, cout, 
         np.testing.assert_array_equal(o, outs[0])
 
 
+@pytest.mark.parametrize("act_dw,act_proj", [(_lib.ACT_NONE, _lib.ACT_RELU), (_lib.ACT_RELU6, _lib.ACT_TANH),
+                                             (_lib.ACT_SILU, _lib.ACT_NONE)])
+def test_dw_project_other_activations(g, act_dw, act_proj):
+    """Activations outside ReLU6 / none on either side (the kernel's second
+    activation-group instantiation) against float64."""
+    n, ih, c, s, cout = 2, 14, 96, 1, 40
+    x = _r(n, ih, ih, c, scale=2.0)
+    wd, bd = _r(3, 3, c), _r(c, scale=0.1)
+    wp = _r(cout, c, scale=np.sqrt(3.0 / c))
+    bp = _r(cout, scale=0.1)
+    dy = g.alloc((n, ih, ih, cout))
+    g.dw_project_nhwc(g.tensor(x), g.tensor(wd), g.tensor(bd), g.weights_split(g.tensor(wp)),
+                      g.tensor(bp), dy, stride=s, pad=(1, 1), act_dw=act_dw, act_proj=act_proj)
+    acts = {_lib.ACT_NONE: lambda v: v, _lib.ACT_RELU: lambda v: np.maximum(v, 0),
+            _lib.ACT_RELU6: lambda v: np.clip(v, 0, 6), _lib.ACT_TANH: np.tanh,
+            _lib.ACT_SILU: lambda v: v / (1 + np.exp(-v))}
+    d = acts[act_dw](R.depthwise_nhwc(x, wd, bd, (s, s), (1, 1), (ih, ih)))
+    ref = acts[act_proj](d @ wp.T.astype(np.float64) + bp)
+    got = dy.download()
+    assert np.abs(got - ref).max() / np.abs(ref).max() <= 2.5e-8 * c + 2e-6
+
+
 def test_dw_project_rejects_unsupported(g):
     x, y = g.alloc((1, 8, 8, 30)), g.alloc((1, 8, 8, 16))
     assert not g.dw_project_supported(x, y, stride=1, pad=(1, 1))     # c % 4
