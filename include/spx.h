@@ -118,6 +118,11 @@ int spx_device_status(void);
  * kernel uses (2..4, default 4; fewer where shared memory is short).  More
  * stages let the depthwise builders run ahead of the tensor core.  Results
  * are identical for every value.
+ * "pdl": 1 (default) = the tensor-core GEMM and fused depthwise kernels are
+ * launched with programmatic stream serialisation: a launch may start its
+ * set-up (barriers, tensor memory, staged bias) on SMs the previous kernel
+ * has left and waits for that kernel's completion before touching any
+ * activation; 0 = plain launches.  Results are identical either way.
  * "ar_wait_limit_us": bound of the peer all-reduce's wait for the other ranks
  * (default 2,000,000; 1,000 .. 60,000,000).
  * "tc_cat": 1 (default) = tensor-core GEMM tiles up to 128 columns wide issue

@@ -208,6 +208,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_after();
   const uint32_t tmem = *tmem_slot;
+  // Set-up above touched only this launch's constants: from here on the
+  // previous kernel's output is read and buffers it may still read are written.
+  pdl_trigger();
+  pdl_wait();
 
   auto decode = [&](int t, int& nt, int& img, int& ty, int& tx) {
     nt = t % p.n_ntiles;
@@ -859,7 +863,9 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
   });
   if (attr != cudaSuccess) return check_cuda(attr, "dw_project: smem attribute");
   const int grid = (int)(p.total < num_sms() ? p.total : num_sms());
-  kern<<<grid, kThreads, smem, s>>>(mx, mh, ml, mw, mb, my, mr, p);
+  const cudaError_t le = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, mx, mh, ml, mw, mb,
+                                    my, mr, p);
+  if (le != cudaSuccess) return check_cuda(le, "dw_project launch");
   return after_launch(cnt, "dw_project");
 }
 
@@ -956,7 +962,9 @@ int launch_stem(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
   });
   if (attr != cudaSuccess) return check_cuda(attr, "stem: smem attribute");
   const int grid = (int)(p.total < num_sms() ? p.total : num_sms());
-  kern<<<grid, kThreads, smem, s>>>(mx, mh, ml, mx, mx, my, my, p);
+  const cudaError_t le = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, mx, mh, ml, mx, mx,
+                                    my, my, p);
+  if (le != cudaSuccess) return check_cuda(le, "stem launch");
   return after_launch(cnt, "stem_tc");
 }
 

@@ -472,6 +472,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int total = p.m_tiles * p.n_tiles;
+  // Set-up above touched only this launch's constants (the bias): from here
+  // on the previous kernel's output is read and buffers it may read are written.
+  pdl_trigger();
+  pdl_wait();
 
   if (warp == kProducerWarp) {
     // ---------------- TMA producer ----------------
@@ -1758,8 +1762,9 @@ int launch_gemm_tc(cudaStream_t s, int64_t* cnt, const float* a, int64_t lda, co
   if (attr_err != cudaSuccess) return check_cuda(attr_err, "gemm_tc: smem attribute");
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  (act_group(p.act) ? gemm_tc_kernel<1> : gemm_tc_kernel<0>)<<<grid, kThreads, smem, s>>>(
-      ma, mb, mblo, mc, mr, p);
+  const cudaError_t le = launch_pdl(act_group(p.act) ? gemm_tc_kernel<1> : gemm_tc_kernel<0>,
+                                    dim3(grid), dim3(kThreads), smem, s, ma, mb, mblo, mc, mr, p);
+  if (le != cudaSuccess) return check_cuda(le, "gemm_tc launch");
   return after_launch(cnt, "gemm_tc");
 }
 

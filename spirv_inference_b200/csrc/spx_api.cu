@@ -47,6 +47,7 @@ int g_pw_path = 0;
 int g_pw_gemm = 0;
 int g_dwp_groups = 47;
 int g_dwp_stages = 4;
+int g_pdl = 1;
 
 // ---- algorithm selection for dense contractions ---------------------------
 int launch_conv_nhwc(cudaStream_t s, int64_t* cnt, const float* x, const float* w,
@@ -512,6 +513,11 @@ int spx_set_option(const char* name, int64_t value) {
     g_pw_gemm = (int)value;
     return SPX_OK;
   }
+  if (n == "pdl") {
+    if (value < 0 || value > 1) return fail(SPX_ERR_INVALID_ARGUMENT, "pdl must be 0..1");
+    g_pdl = (int)value;
+    return SPX_OK;
+  }
   if (n == "dwp_stages") {
     if (value < 2 || value > 4) return fail(SPX_ERR_INVALID_ARGUMENT, "dwp_stages must be 2..4");
     g_dwp_stages = (int)value;
@@ -549,6 +555,7 @@ int64_t spx_get_option(const char* name) {
   if (n == "pw_gemm") return g_pw_gemm;
   if (n == "dwp_groups") return g_dwp_groups;
   if (n == "dwp_stages") return g_dwp_stages;
+  if (n == "pdl") return g_pdl;
   return -1;
 }
 

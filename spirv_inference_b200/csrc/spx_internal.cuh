@@ -33,6 +33,34 @@ int check_cuda(cudaError_t e, const char* what);
 // Checks the launch that was just issued and bumps the launch counter.
 int after_launch(int64_t* counter, const char* what);
 
+// Programmatic dependent launch.  A kernel launched with launch_pdl may start
+// while the previous kernel on the stream is still running (on SMs that
+// kernel has left); it must call pdl_wait() before its first access to global
+// memory that an earlier kernel writes or reads (the wait returns once every
+// earlier kernel has completed and its writes are visible).  pdl_trigger()
+// lets the next PDL launch begin as soon as every CTA of this grid has
+// called it.  Option "pdl" (default 1); 0 = plain launches.
+extern int g_pdl;
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
+
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int grid_for(int64_t work, int threads, int per_sm = 8) {
   int64_t g = ceil_div(work, threads);

@@ -230,3 +230,24 @@ def test_stem_rejects_other_shapes(g):
     assert not g.stem_supported(x, y)                     # iw % 4
     x2, y2 = g.alloc((1, 16, 16, 4)), g.alloc((1, 8, 8, 32))
     assert not g.stem_supported(x2, y2)                   # 4 input channels
+
+
+def test_programmatic_launch_gives_identical_outputs(gpu):
+    """Option pdl: the fused and GEMM kernels launched with programmatic
+    stream serialisation (set-up overlapping the previous kernel's tail)
+    give the same bits as plain launches, in eager runs and graph replays."""
+    m = nets.mobilenet_v2(seed=0)
+    x = nets.make_input(m, 16, seed=5)
+    outs = []
+    try:
+        for pdl in (0, 1):
+            _lib.set_option("pdl", pdl)
+            ex = CnnExecutor(m, batch=16, device=gpu)
+            try:
+                outs += [ex.forward(x), ex.forward(x)]
+            finally:
+                ex.close()
+    finally:
+        _lib.set_option("pdl", 1)
+    for o in outs[1:]:
+        np.testing.assert_array_equal(o, outs[0])
