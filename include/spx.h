@@ -118,6 +118,10 @@ int spx_device_status(void);
  * kernel uses (2..4, default 4; fewer where shared memory is short).  More
  * stages let the depthwise builders run ahead of the tensor core.  Results
  * are identical for every value.
+ * "dwp_accs": 4 (default) = the fused depthwise -> projection kernel and the
+ * tensor-core stem keep four TMEM accumulators where they fit (projection
+ * width <= 64), so the tensor core can run two tiles ahead of each epilogue
+ * group; 2 = two.  Results are identical either way.
  * "pdl": 1 (default) = the tensor-core GEMM and fused depthwise kernels are
  * launched with programmatic stream serialisation: a launch may start its
  * set-up (barriers, tensor memory, staged bias) on SMs the previous kernel

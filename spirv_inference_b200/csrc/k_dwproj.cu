@@ -11,10 +11,10 @@
 // image (128 GEMM rows) and, for each, every 32-channel block of the
 // depthwise width (the GEMM's K):
 //   warp 8      TMA producers: per K block the pre-split projection weights
-//               (hi and lo, NP x 32, 128-byte swizzle) into one of two
-//               stages, and per CB-channel sub-block the input halo box
-//               ((TH-1)*S+3) x ((TW-1)*S+3) x CB into a ring (the tensor map's
-//               zero fill is the depthwise padding);
+//               (hi and lo, NP x 32, 128-byte swizzle) into the A/B stages
+//               (lane 1), and per CB-channel sub-block the input halo box
+//               ((TH-1)*S+3) x ((TW-1)*S+3) x CB into a ring (lane 0; the
+//               tensor map's zero fill is the depthwise padding);
 //   warps 0-7   builders: the depthwise conv of the sub-block on CUDA cores
 //               (exact fp32 FMAs, bias and activation fused; a thread owns 2
 //               channels of R rows x 2 columns and reads each input row of its
@@ -29,7 +29,7 @@
 //               of two TMEM accumulators (NP columns each), a commit per K
 //               block frees the stage, a commit per tile hands the
 //               accumulator to the epilogue;
-//   warps 10-13 epilogue: TMEM lane quarter -> registers (a lane = an output
+//   warps 10-17 epilogue (two groups of four, alternate tiles): TMEM lane quarter -> registers (a lane = an output
 //               pixel, 32 channels) -> projection bias, residual, activation
 //               -> one contiguous 128-byte channel run of the NHWC output.
 // HBM traffic per tile: the halo (interior read once; the overlap between
@@ -101,6 +101,7 @@ struct DwpArgs {
   uint32_t idesc, tmem_cols;
   uint32_t idesc2;         // N = 2 NP (hi and lo weight tiles as one operand)
   int cat;                 // 1: raw*[hi;lo] + lo*hi (two MMAs per k-step), acc stride 2 NP
+  int nacc;                // TMEM accumulators (2 or 4; epilogue group g drains g, g + 2)
   const float* wd;         // depthwise weights [3][3][ce]
   const float* bd;         // depthwise bias [ce] or null
   int act_d;
@@ -167,8 +168,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bfull = afull + kMaxStages;
   uint64_t* empty = bfull + kMaxStages;
   uint64_t* tfull = empty + kMaxStages;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
+  uint64_t* tempty = tfull + 4;
+  uint64_t* drain = tempty + 4;
   uint64_t* rfull = drain + 1;  // [4 * kEpiGroups]: a warp's residual box landed
   uint32_t* tmem_slot = (uint32_t*)(rfull + 4 * kEpiGroups);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
@@ -189,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mb_init(&bfull[j], 1);
       mb_init(&empty[j], 1);
     }
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < 4; ++j) {
       mb_init(&tfull[j], 1);
       mb_init(&tempty[j], 4 * 32);
     }
@@ -348,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         mma_commit(&tfull[acc]);
-        if (++acc == 2) {
+        if (++acc == p.nacc) {
           acc = 0;
           aph ^= 1;
         }
@@ -575,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
     }
   } else {
-    // ---------------- epilogue (warps 10-13) ----------------
+    // ---------------- epilogue (warps 10-17) ----------------
     // A lane owns one GEMM row (one output pixel): tcgen05.ld gives it 32
     // consecutive output channels, which it writes (with bias, residual and
     // activation) as one contiguous 128-byte run of the NHWC output.
@@ -586,7 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // never wait on one another.
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int grp = (warp - kEpiWarp0) / 4;
-    const int acc = grp;
+    int acc = grp;  // accumulators grp, grp + 2, ... (tiles of this group's parity)
     uint8_t* stg = estage + (size_t)(warp - kEpiWarp0) * kEWarp;
     uint64_t* rbar = &rfull[warp - kEpiWarp0];
     const int row0 = q * 32;                     // first GEMM row of this warp
@@ -669,7 +670,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_before();
       mb_arrive(&tempty[acc]);
       if (warp == kEpiWarp0 + 2 && lane == 0) DWP_TRACE(7, (t - (int)blockIdx.x) / (int)gridDim.x);
-      aph ^= 1;
+      acc += kEpiGroups;
+      if (acc >= p.nacc) {
+        acc -= p.nacc;
+        aph ^= 1;
+      }
     }
     if (lane == 0) bulk_wait_all();  // this warp's stores have completed
   }
@@ -768,8 +773,11 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
   p.b_bytes = (uint32_t)p.np * 128;
   p.stage_bytes = 2 * kAHalf + 2 * p.b_bytes;
   p.cat = p.np <= 128 ? 1 : 0;
+  // Four accumulators where tensor memory holds them: the MMA can then run
+  // up to two tiles ahead of an epilogue group (short K loops).
+  p.nacc = (g_dwp_accs == 4 && 4 * p.np * (1 + p.cat) <= 512) ? 4 : 2;
   uint32_t cols = 32;
-  while (cols < (uint32_t)(2 * p.np * (1 + p.cat))) cols <<= 1;
+  while (cols < (uint32_t)(p.nacc * p.np * (1 + p.cat))) cols <<= 1;
   p.tmem_cols = cols;
   p.idesc = idesc_tf32(128, p.np);
   p.idesc2 = idesc_tf32(128, 2 * p.np);
@@ -904,8 +912,11 @@ int launch_stem(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
   p.b_bytes = (uint32_t)p.np * 128;
   p.stage_bytes = 2 * kAHalf + 2 * p.b_bytes;
   p.cat = p.np <= 128 ? 1 : 0;
+  // Four accumulators where tensor memory holds them: the MMA can then run
+  // up to two tiles ahead of an epilogue group (short K loops).
+  p.nacc = (g_dwp_accs == 4 && 4 * p.np * (1 + p.cat) <= 512) ? 4 : 2;
   uint32_t cols = 32;
-  while (cols < (uint32_t)(2 * p.np * (1 + p.cat))) cols <<= 1;
+  while (cols < (uint32_t)(p.nacc * p.np * (1 + p.cat))) cols <<= 1;
   p.tmem_cols = cols;
   p.idesc = idesc_tf32(128, p.np);
   p.idesc2 = idesc_tf32(128, 2 * p.np);

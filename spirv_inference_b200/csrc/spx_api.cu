@@ -47,6 +47,7 @@ int g_pw_path = 0;
 int g_pw_gemm = 0;
 int g_dwp_groups = 47;
 int g_dwp_stages = 4;
+int g_dwp_accs = 4;
 int g_pdl = 1;
 
 // ---- algorithm selection for dense contractions ---------------------------
@@ -523,6 +524,11 @@ int spx_set_option(const char* name, int64_t value) {
     g_dwp_stages = (int)value;
     return SPX_OK;
   }
+  if (n == "dwp_accs") {
+    if (value != 2 && value != 4) return fail(SPX_ERR_INVALID_ARGUMENT, "dwp_accs must be 2 or 4");
+    g_dwp_accs = (int)value;
+    return SPX_OK;
+  }
   if (n == "dwp_groups") {
     if (value < 0 || value > 63) return fail(SPX_ERR_INVALID_ARGUMENT, "dwp_groups must be 0..63");
     g_dwp_groups = (int)value;
@@ -555,6 +561,7 @@ int64_t spx_get_option(const char* name) {
   if (n == "pw_gemm") return g_pw_gemm;
   if (n == "dwp_groups") return g_dwp_groups;
   if (n == "dwp_stages") return g_dwp_stages;
+  if (n == "dwp_accs") return g_dwp_accs;
   if (n == "pdl") return g_pdl;
   return -1;
 }

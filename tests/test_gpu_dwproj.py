@@ -90,9 +90,9 @@ def test_dw_project_matches_float64(g, n, ih, c, s, cout, residual):
                                                    CASES[11], CASES[13]])
 def test_builder_groups_and_stages_give_identical_results(g, n, ih, c, s, cout, residual):
     """One builder group per K block or two taking alternate K blocks, two to
-    four A/B stages: every depthwise value is accumulated by one thread in
-    the same order and every GEMM in the same k order either way, so the
-    outputs are bit-identical."""
+    four A/B stages, two or four TMEM accumulators: every depthwise value is accumulated by one
+    thread in the same order and every GEMM in the same k order either way,
+    so the outputs are bit-identical."""
     oh = -(-ih // s)
     pt = max((oh - 1) * s + 3 - ih, 0) // 2
     x = g.tensor(_r(n, ih, ih, c, scale=2.0))
@@ -101,18 +101,19 @@ def test_builder_groups_and_stages_give_identical_results(g, n, ih, c, s, cout, 
     bp = g.tensor(_r(cout, scale=0.1))
     res = g.tensor(_r(n, oh, oh, cout)) if residual else None
     outs = []
-    defaults = _lib.get_option("dwp_groups"), _lib.get_option("dwp_stages")
+    names = ("dwp_groups", "dwp_stages", "dwp_accs")
+    defaults = [_lib.get_option(k) for k in names]
     try:
-        for mask, stages in ((0, 2), (63, 2), (0, 4), (63, 4), (63, 3)):
-            _lib.set_option("dwp_groups", mask)
-            _lib.set_option("dwp_stages", stages)
+        for setting in ((0, 2, 2), (63, 2, 4), (0, 4, 2), (63, 4, 4), (63, 3, 4), (47, 4, 2)):
+            for k, v in zip(names, setting):
+                _lib.set_option(k, v)
             dy = g.alloc((n, oh, oh, cout))
             g.dw_project_nhwc(x, wd, bd, split, bp, dy, stride=s, pad=(pt, pt),
                               act_dw=_lib.ACT_RELU6, residual=res)
             outs.append(dy.download())
     finally:
-        _lib.set_option("dwp_groups", defaults[0])
-        _lib.set_option("dwp_stages", defaults[1])
+        for k, v in zip(names, defaults):
+            _lib.set_option(k, v)
     for o in outs[1:]:
         np.testing.assert_array_equal(o, outs[0])
 
@@ -223,6 +224,24 @@ def test_stem_7x7_matches_float64(g, n, ih, iw, oc, pad):
     ref = np.maximum(R.conv_nhwc(x, w.transpose(1, 2, 3, 0), (2, 2), pad, (oh, ow)) + b, 0)
     got = dy.download()
     assert np.abs(got - ref).max() / np.abs(ref).max() <= 2.5e-8 * 147 + 1e-6
+
+
+def test_stem_accumulator_count_gives_identical_results(g):
+    """Two or four TMEM accumulators in the stem change only which tensor
+    memory columns a tile uses, not the arithmetic: identical bits."""
+    x = g.tensor(_r(2, 64, 64, 3, scale=2.0))
+    w = g.stem_weights(_r(32, 3, 3, 3, scale=0.5))
+    b = g.tensor(_r(32, scale=0.1))
+    outs = []
+    try:
+        for accs in (2, 4):
+            _lib.set_option("dwp_accs", accs)
+            dy = g.alloc((2, 32, 32, 32))
+            g.stem_conv_nhwc(x, w, b, dy, pad=(0, 0), activation=_lib.ACT_RELU6)
+            outs.append(dy.download())
+    finally:
+        _lib.set_option("dwp_accs", 4)
+    np.testing.assert_array_equal(outs[1], outs[0])
 
 
 def test_stem_rejects_other_shapes(g):
