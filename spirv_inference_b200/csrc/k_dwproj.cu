@@ -78,8 +78,11 @@ constexpr int kBuildWarps = 8;
 constexpr int kProdWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kEpiWarp0 = 10;
-constexpr int kEpiGroups = 2;  // epilogue groups of 4 warps, draining alternate tiles
-constexpr int kThreads = (kEpiWarp0 + 4 * kEpiGroups) * 32;
+// Epilogue groups of 4 warps draining alternate tiles: EG = 2 (576 threads,
+// 96 registers a thread) for one-K-block tiles, whose epilogue sets the pace;
+// EG = 1 (448 threads, 128 registers) where the builders' depthwise does.
+__host__ __device__ constexpr int threads_for(int eg) { return (kEpiWarp0 + 4 * eg) * 32; }
+constexpr int kMaxEpiGroups = 2;
 constexpr uint32_t kEWarp = 32 * 128;                     // one warp's 32 rows x 32 fp32
 constexpr uint32_t kEStage = 4 * kEWarp;                   // a group's staging (16 KB)
 constexpr uint32_t kAHalf = 128 * 32 * 4;        // one 128 x 32 fp32 A tile: 16 KB
@@ -116,8 +119,8 @@ struct DwpArgs {
 // one 32-wide K block): the halo slot is a 3-D box of whole input rows
 // (W * 3 floats), the builders gather each pixel's 27 taps into its A row.
 template <int KS, int S, int TH, int TW, int CB, int R, bool STEM = false, int TN = 1, int NG = 1,
-          int CW = 2, int AG = 0>
-__global__ void __launch_bounds__(kThreads, 1)
+          int CW = 2, int AG = 0, int EG = 2>
+__global__ void __launch_bounds__(threads_for(EG), 1)
     dwproj_kernel(const __grid_constant__ CUtensorMap tmX,
                   const __grid_constant__ CUtensorMap tmBhi,
                   const __grid_constant__ CUtensorMap tmBlo,
@@ -162,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Epilogue staging: one 128-row x 32-channel tile per group, 128-byte
   // swizzled (the TMA store / residual load box layout).
   uint8_t* estage = stages + (size_t)p.nst * p.stage_bytes;
-  uint64_t* hfull = (uint64_t*)(estage + kEpiGroups * (size_t)kEStage);
+  uint64_t* hfull = (uint64_t*)(estage + EG * (size_t)kEStage);
   uint64_t* hempty = hfull + kMaxHalo;
   uint64_t* afull = hempty + kMaxHalo;
   uint64_t* bfull = afull + kMaxStages;
@@ -170,13 +173,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull = empty + kMaxStages;
   uint64_t* tempty = tfull + 4;
   uint64_t* drain = tempty + 4;
-  uint64_t* rfull = drain + 1;  // [4 * kEpiGroups]: a warp's residual box landed
-  uint32_t* tmem_slot = (uint32_t*)(rfull + 4 * kEpiGroups);
+  uint64_t* rfull = drain + 1;  // [4 * EG]: a warp's residual box landed
+  uint32_t* tmem_slot = (uint32_t*)(rfull + 4 * EG);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   // Projection bias of every n tile, zero past cout (or without a bias): the
   // epilogue reads it as shared-memory broadcasts instead of global loads.
   float* bias_s = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(hfull) + kBarBytes);
-  for (int i = threadIdx.x; i < p.n_ntiles * p.np && i < kMaxBias; i += kThreads)
+  for (int i = threadIdx.x; i < p.n_ntiles * p.np && i < kMaxBias; i += threads_for(EG))
     bias_s[i] = (p.bp && i < p.cout) ? __ldg(p.bp + i) : 0.f;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -195,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mb_init(&tempty[j], 4 * 32);
     }
     mb_init(drain, 1);
-    for (int w2 = 0; w2 < 4 * kEpiGroups; ++w2) mb_init(&rfull[w2], 1);
+    for (int w2 = 0; w2 < 4 * EG; ++w2) mb_init(&rfull[w2], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -596,7 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool w_live = row0 < kTilePx;          // rows past a 64-row tile are padding
     uint32_t aph = 0, rph = 0;
     bool ok_all = true;
-    for (int t = blockIdx.x + grp * gridDim.x; t < p.total; t += kEpiGroups * gridDim.x) {
+    for (int t = blockIdx.x + grp * gridDim.x; t < p.total; t += EG * gridDim.x) {
       int nt, img, ty, tx;
       decode(t, nt, img, ty, tx);
       const bool ok = __all_sync(0xffffffffu, mb_wait(&tfull[acc], aph, abort_flag,
@@ -670,7 +673,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_before();
       mb_arrive(&tempty[acc]);
       if (warp == kEpiWarp0 + 2 && lane == 0) DWP_TRACE(7, (t - (int)blockIdx.x) / (int)gridDim.x);
-      acc += kEpiGroups;
+      acc += EG;
       if (acc >= p.nacc) {
         acc -= p.nacc;
         aph ^= 1;
@@ -742,7 +745,8 @@ struct DwpCfg {
   int th, tw, cb;
 };
 
-template <int KS, int S, int TH, int TW, int CB, int R, int TN = 1, int NG = 1, int CW = 2>
+template <int KS, int S, int TH, int TW, int CB, int R, int TN = 1, int NG = 1, int CW = 2,
+          int EG = 2>
 int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, const float* bd,
                const float* w_hi, const float* w_lo, const float* bp, const float* res, float* y,
                const spx_dwproj_params* q, bool dry_run, uint32_t* smem_out) {
@@ -792,7 +796,7 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
   // Shared memory: as many A/B stages as fit (up to the "dwp_stages"
   // option) with at least two halo slots, then a third halo slot if it fits.
   auto need = [&](int nst, int hst) {
-    return 1024 + (uint32_t)nst * p.stage_bytes + kEpiGroups * kEStage + kBarBytes + kBiasBytes +
+    return 1024 + (uint32_t)nst * p.stage_bytes + EG * kEStage + kBarBytes + kBiasBytes +
            (uint32_t)hst * p.halo_buf;
   };
   p.nst = 0;
@@ -858,20 +862,20 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
       return fail(SPX_ERR_CUDA, "dw_project: depthwise weight map encode failed (%d)", (int)r);
   }
   const bool heavy = act_group(p.act_d) || act_group(p.act_p);
-  auto kern = heavy ? dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG, CW, 1>
-                    : dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG, CW, 0>;
+  auto kern = heavy ? dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG, CW, 1, EG>
+                    : dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG, CW, 0, EG>;
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [&] {
-    attr = cudaFuncSetAttribute(dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG, CW, 0>,
+    attr = cudaFuncSetAttribute(dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG, CW, 0, EG>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
     if (attr == cudaSuccess)
-      attr = cudaFuncSetAttribute(dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG, CW, 1>,
+      attr = cudaFuncSetAttribute(dwproj_kernel<KS, S, TH, TW, CB, R, false, TN, NG, CW, 1, EG>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
   });
   if (attr != cudaSuccess) return check_cuda(attr, "dw_project: smem attribute");
   const int grid = (int)(p.total < num_sms() ? p.total : num_sms());
-  const cudaError_t le = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, mx, mh, ml, mw, mb,
+  const cudaError_t le = launch_pdl(kern, dim3(grid), dim3(threads_for(EG)), smem, s, mx, mh, ml, mw, mb,
                                     my, mr, p);
   if (le != cudaSuccess) return check_cuda(le, "dw_project launch");
   return after_launch(cnt, "dw_project");
@@ -927,7 +931,7 @@ int launch_stem(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
   // then up to four halo slots.
   const uint32_t cap = 227 * 1024;
   auto need = [&](int nst, int hst) {
-    return 1024 + (uint32_t)nst * p.stage_bytes + kEpiGroups * kEStage + kBarBytes + kBiasBytes +
+    return 1024 + (uint32_t)nst * p.stage_bytes + kMaxEpiGroups * kEStage + kBarBytes + kBiasBytes +
            (uint32_t)hst * p.halo_buf;
   };
   p.nst = 2;
@@ -973,7 +977,7 @@ int launch_stem(cudaStream_t s, int64_t* cnt, const float* x, const float* w_hi,
   });
   if (attr != cudaSuccess) return check_cuda(attr, "stem: smem attribute");
   const int grid = (int)(p.total < num_sms() ? p.total : num_sms());
-  const cudaError_t le = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, mx, mh, ml, mx, mx,
+  const cudaError_t le = launch_pdl(kern, dim3(grid), dim3(threads_for(kMaxEpiGroups)), smem, s, mx, mh, ml, mx, mx,
                                     my, my, p);
   if (le != cudaSuccess) return check_cuda(le, "stem launch");
   return after_launch(cnt, "stem_tc");
@@ -1051,12 +1055,22 @@ int launch_dw_project(cudaStream_t s, int64_t* cnt, const float* x, const float*
   // Builder groups per tile class (bit set: two groups, each with twice the
   // rows per thread), from the "dwp_groups" option.
   const int g = g_dwp_groups;
-#define SPX_DWP_CFG(bit, S_, TH_, TW_, CB_, R_, TN_, CW_)                                      \
-  return (g >> bit) & 1                                                                        \
-             ? launch_cfg<3, S_, TH_, TW_, CB_, 2 * R_, TN_, 2, CW_>(                          \
-                   s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run, nullptr)             \
-             : launch_cfg<3, S_, TH_, TW_, CB_, R_, TN_, 1, CW_>(s, cnt, x, wd, bd, w_hi, w_lo, \
-                                                                 bp, res, y, q, dry_run, nullptr)
+  // Tile classes with one epilogue group (and 128 registers a thread), from
+  // the "dwp_epi1" option (same bits).
+  const int e1 = g_dwp_epi1;
+#define SPX_DWP_CFG(bit, S_, TH_, TW_, CB_, R_, TN_, CW_)                                       \
+  {                                                                                             \
+  if ((e1 >> bit) & 1)                                                                          \
+    return (g >> bit) & 1                                                                       \
+               ? launch_cfg<3, S_, TH_, TW_, CB_, 2 * R_, TN_, 2, CW_, 1>(                      \
+                     s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run, nullptr)            \
+               : launch_cfg<3, S_, TH_, TW_, CB_, R_, TN_, 1, CW_, 1>(                          \
+                     s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run, nullptr);           \
+  return (g >> bit) & 1 ? launch_cfg<3, S_, TH_, TW_, CB_, 2 * R_, TN_, 2, CW_, 2>(             \
+                              s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run, nullptr)   \
+                        : launch_cfg<3, S_, TH_, TW_, CB_, R_, TN_, 1, CW_, 2>(                 \
+                              s, cnt, x, wd, bd, w_hi, w_lo, bp, res, y, q, dry_run, nullptr);  \
+  }
   if (q->stride == 1) {
     if (q->ow <= 8) SPX_DWP_CFG(0, 1, 8, 8, 16, 4, 2, 1);
     if (q->c <= 32) SPX_DWP_CFG(4, 1, 8, 16, 32, 4, 1, 2);

@@ -48,6 +48,7 @@ int g_pw_gemm = 0;
 int g_dwp_groups = 47;
 int g_dwp_stages = 4;
 int g_dwp_accs = 4;
+int g_dwp_epi1 = 54;
 int g_pdl = 1;
 
 // ---- algorithm selection for dense contractions ---------------------------
@@ -524,6 +525,11 @@ int spx_set_option(const char* name, int64_t value) {
     g_dwp_stages = (int)value;
     return SPX_OK;
   }
+  if (n == "dwp_epi1") {
+    if (value < 0 || value > 63) return fail(SPX_ERR_INVALID_ARGUMENT, "dwp_epi1 must be 0..63");
+    g_dwp_epi1 = (int)value;
+    return SPX_OK;
+  }
   if (n == "dwp_accs") {
     if (value != 2 && value != 4) return fail(SPX_ERR_INVALID_ARGUMENT, "dwp_accs must be 2 or 4");
     g_dwp_accs = (int)value;
@@ -562,6 +568,7 @@ int64_t spx_get_option(const char* name) {
   if (n == "dwp_groups") return g_dwp_groups;
   if (n == "dwp_stages") return g_dwp_stages;
   if (n == "dwp_accs") return g_dwp_accs;
+  if (n == "dwp_epi1") return g_dwp_epi1;
   if (n == "pdl") return g_pdl;
   return -1;
 }

@@ -320,6 +320,7 @@ extern int g_gemm_path;
 extern int64_t g_ar_wait_limit_us;
 extern int g_tc_epi12;
 extern int g_dwp_groups;
+extern int g_dwp_epi1;    // dw_project tile classes with one epilogue group (bit mask)
 extern int g_dwp_accs;    // dw_project / stem TMEM accumulators (2 or 4)
 extern int g_dwp_stages;  // dw_project A/B stage count cap (2..4)  // dw_project builder groups per tile class (bit mask)
 extern int g_tc_conv2;

@@ -90,7 +90,8 @@ def test_dw_project_matches_float64(g, n, ih, c, s, cout, residual):
                                                    CASES[11], CASES[13]])
 def test_builder_groups_and_stages_give_identical_results(g, n, ih, c, s, cout, residual):
     """One builder group per K block or two taking alternate K blocks, two to
-    four A/B stages, two or four TMEM accumulators: every depthwise value is accumulated by one
+    four A/B stages, two or four TMEM accumulators, one or two epilogue
+    groups: every depthwise value is accumulated by one
     thread in the same order and every GEMM in the same k order either way,
     so the outputs are bit-identical."""
     oh = -(-ih // s)
@@ -101,10 +102,11 @@ def test_builder_groups_and_stages_give_identical_results(g, n, ih, c, s, cout, 
     bp = g.tensor(_r(cout, scale=0.1))
     res = g.tensor(_r(n, oh, oh, cout)) if residual else None
     outs = []
-    names = ("dwp_groups", "dwp_stages", "dwp_accs")
+    names = ("dwp_groups", "dwp_stages", "dwp_accs", "dwp_epi1")
     defaults = [_lib.get_option(k) for k in names]
     try:
-        for setting in ((0, 2, 2), (63, 2, 4), (0, 4, 2), (63, 4, 4), (63, 3, 4), (47, 4, 2)):
+        for setting in ((0, 2, 2, 0), (63, 2, 4, 63), (0, 4, 2, 63), (63, 4, 4, 0), (63, 3, 4, 47),
+                        (47, 4, 2, 0)):
             for k, v in zip(names, setting):
                 _lib.set_option(k, v)
             dy = g.alloc((n, oh, oh, cout))
