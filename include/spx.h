@@ -201,6 +201,9 @@ int spx_run_kernel(const char* kernel, const float* input0, size_t input0_len,
  * convolutions whose input + weights + output exceed 4 Mi floats are rejected
  * with SPX_ERR_INVALID_ARGUMENT.  The first call on each device looks up the
  * array's device address; make that first call before any stream capture.
+ * That address (like the regular dispatch's per-device buffers) is cached
+ * for the life of the process: do not reset the device (cudaDeviceReset)
+ * while libspx is loaded.
  * All calls share the array: calls that can overlap on the GPU (other
  * streams, other host threads) race and must be serialised by the caller.
  * No cudaMalloc, cudaFree or allocating library routine is called.
