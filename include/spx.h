@@ -137,6 +137,11 @@ int spx_device_status(void);
  * activation; 0 = plain launches.  Results are identical either way.
  * "ar_wait_limit_us": bound of the peer all-reduce's wait for the other ranks
  * (default 2,000,000; 1,000 .. 60,000,000).
+ * "tc_acc4": 1 (default) = tensor-core GEMM tiles with one k-block (short
+ * reductions such as the 1x1 expand convolutions) keep three or four TMEM
+ * accumulators (as many as fit, tiles up to 170 columns wide) and issue the
+ * three products separately, so the tensor core can run ahead of the
+ * epilogue; 0 = two accumulators.
  * "tc_cat": 1 (default) = tensor-core GEMM tiles up to 128 columns wide issue
  * raw A x [B hi; B lo] as one product of twice the width plus lo A x hi B
  * (two wide MMAs instead of three narrow ones per k-step; the epilogue adds

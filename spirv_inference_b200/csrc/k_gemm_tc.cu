@@ -50,6 +50,7 @@ int g_tc_epi12 = 1;
 int g_tc_conv2 = 1;
 int g_tc_lo_tmem = 0;
 int g_tc_cat = 1;
+int g_tc_acc4 = 1;
 
 #ifdef SPX_TC_TRACE
 // Development-only pipeline trace of CTA 0 (not compiled into the library).
@@ -1668,6 +1669,13 @@ int plan_gemm_tc(TcArgs& p, int M, int N, int K, bool presplit, bool conv, int m
   p.lo_tmem = g_tc_lo_tmem && p.presplit && p.k_blocks >= 2 && p.epi_warps <= kEpiWarps &&
               p.nacc * p.BN + 2 * kBK <= 512;
   p.cat = g_tc_cat && p.BN <= 128 && !p.lo_tmem;
+  // One k-block per tile (the expand layers): the epilogue sets the pace, so
+  // three or four accumulators (three separate products, no concatenated
+  // N = 2 BN one) let the tensor core run ahead of a slow chunk.
+  if (g_tc_acc4 && p.groups == 1 && p.tma_store && p.k_blocks == 1 && 3 * p.BN <= 512) {
+    p.nacc = 4 * p.BN <= 512 ? 4 : 3;
+    p.cat = 0;
+  }
   p.lo_col = p.nacc * p.BN;
   const int budget = 227 * 1024 - 1024 - p.epi_warps * (int)kEpiSlot - 512 -
                      (p.b_resident ? 2 * (int)p.b_bytes : 0);

@@ -525,6 +525,11 @@ int spx_set_option(const char* name, int64_t value) {
     g_dwp_stages = (int)value;
     return SPX_OK;
   }
+  if (n == "tc_acc4") {
+    if (value < 0 || value > 1) return fail(SPX_ERR_INVALID_ARGUMENT, "tc_acc4 must be 0..1");
+    g_tc_acc4 = (int)value;
+    return SPX_OK;
+  }
   if (n == "dwp_epi1") {
     if (value < 0 || value > 63) return fail(SPX_ERR_INVALID_ARGUMENT, "dwp_epi1 must be 0..63");
     g_dwp_epi1 = (int)value;
@@ -563,6 +568,7 @@ int64_t spx_get_option(const char* name) {
   if (n == "tc_conv_groups") return g_tc_conv2 ? 2 : 1;
   if (n == "tc_lo_tmem") return g_tc_lo_tmem;
   if (n == "tc_cat") return g_tc_cat;
+  if (n == "tc_acc4") return g_tc_acc4;
   if (n == "ar_wait_limit_us") return g_ar_wait_limit_us;
   if (n == "pw_gemm") return g_pw_gemm;
   if (n == "dwp_groups") return g_dwp_groups;

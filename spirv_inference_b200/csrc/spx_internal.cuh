@@ -326,6 +326,7 @@ extern int g_dwp_stages;  // dw_project A/B stage count cap (2..4)  // dw_projec
 extern int g_tc_conv2;
 extern int g_tc_lo_tmem;
 extern int g_tc_cat;  // tensor-core GEMM: concatenated hi/lo weight product for N tiles <= 128
+extern int g_tc_acc4; // tensor-core GEMM: four accumulators for one-k-block tiles
 // Depthwise path: 0 automatic (TMA tiles where the shape allows), 1 register
 // sliding-window kernel only.
 extern int g_dw_path;

@@ -243,3 +243,34 @@ def test_tc_concatenated_product_matches_three_products(g, M, N, K, conv):
     for o in outs:
         assert np.abs(o - ref).max() / scale <= 2.5e-8 * K + 1e-6
     assert np.abs(outs[0] - outs[1]).max() / scale <= 2 * (2.5e-8 * K + 1e-6)
+
+
+@pytest.mark.parametrize("M,N,K", [(3211264, 96, 16), (802816, 144, 24), (50000, 160, 8),
+                                   (300001, 128, 20), (200704, 64, 24)])
+def test_tc_more_accumulators_give_identical_results(g, M, N, K):
+    """Option tc_acc4: one-k-block tiles on three or four accumulators issue
+    the three separate products, so they must give the bits of the
+    three-product form on two accumulators (tc_cat = 0, tc_acc4 = 0), and
+    stay within the 3xTF32 bound of float64."""
+    a = _r(M, K)
+    w = _r(N, K, scale=1.0 / np.sqrt(K))
+    bias = _r(N)
+    da, dw, db = g.tensor(a), g.tensor(w), g.tensor(bias)
+    split = g.weights_split(dw)
+    outs = []
+    try:
+        for cat, acc4 in ((0, 0), (1, 1)):
+            _lib.set_option("tc_cat", cat)
+            _lib.set_option("tc_acc4", acc4)
+            assert _lib.gemm_tc_plan(M, N, K)["nacc"] == (2 if not acc4 else
+                                                          (4 if N <= 128 else 3))
+            dc = g.alloc((M, N))
+            g.gemm(da, dw, dc, m=M, n=N, k=K, a_strides=(0, K, 1), b_strides=(0, 1, K),
+                   c_strides=(0, N), bias=db, b_split=split)
+            outs.append(dc.download())
+    finally:
+        _lib.set_option("tc_cat", 1)
+        _lib.set_option("tc_acc4", 1)
+    np.testing.assert_array_equal(outs[0], outs[1])
+    ref = a[:4096].astype(np.float64) @ w.T.astype(np.float64) + bias
+    assert np.abs(outs[1][:4096] - ref).max() / np.abs(ref).max() <= 2.5e-8 * K + 1e-6
