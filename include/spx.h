@@ -126,10 +126,10 @@ int spx_device_status(void);
  * runs the class with one epilogue group of four warps (448 threads, up to
  * 128 registers a thread: the depthwise builders keep everything in
  * registers), a clear bit with two groups draining alternate tiles (576
- * threads, 96 registers).  Default 54 (bits 1, 2, 4, 5; measured at batch
- * 256 on the MobileNetV2 layers: 56x56x144 -> 24 262 -> 230 us, 112x112x96
- * stride 2 273 -> 320 us with one group, so bit 3 stays clear).  Results are
- * identical either way.
+ * threads, 96 registers).  Default 62 (bits 1-5; measured at batch 256 on
+ * the MobileNetV2 layers: 56x56x144 -> 24 262 -> 230 us, 112x112x96 stride 2
+ * 273 -> 268 us with one group; the 7x7-map class, bit 0, is level or slower
+ * with one).  Results are identical either way.
  * "pdl": 1 (default) = the tensor-core GEMM and fused depthwise kernels are
  * launched with programmatic stream serialisation: a launch may start its
  * set-up (barriers, tensor memory, staged bias) on SMs the previous kernel

@@ -799,14 +799,27 @@ int launch_cfg(cudaStream_t s, int64_t* cnt, const float* x, const float* wd, co
     return 1024 + (uint32_t)nst * p.stage_bytes + EG * kEStage + kBarBytes + kBiasBytes +
            (uint32_t)hst * p.halo_buf;
   };
+  // Half-width halo blocks (CB = 16: two fills per K block) need the third
+  // halo slot more than a third A/B stage; full-width ones the other way
+  // round.
   p.nst = 0;
-  for (int nst = g_dwp_stages; nst >= 2 && !p.nst; --nst)
-    for (int hst = 3; hst >= 2; --hst)
-      if (need(nst, hst) <= cap) {
-        p.nst = nst;
-        p.hst = hst;
-        break;
-      }
+  if (CB < 32) {
+    for (int hst = 3; hst >= 2 && !p.nst; --hst)
+      for (int nst = g_dwp_stages; nst >= 2; --nst)
+        if (need(nst, hst) <= cap) {
+          p.nst = nst;
+          p.hst = hst;
+          break;
+        }
+  } else {
+    for (int nst = g_dwp_stages; nst >= 2 && !p.nst; --nst)
+      for (int hst = 3; hst >= 2; --hst)
+        if (need(nst, hst) <= cap) {
+          p.nst = nst;
+          p.hst = hst;
+          break;
+        }
+  }
   if (!p.nst) return fail(SPX_ERR_UNSUPPORTED, "dw_project: tile buffers exceed shared memory");
   const uint32_t smem = need(p.nst, p.hst);
   if (smem_out) *smem_out = smem;

@@ -48,7 +48,7 @@ int g_pw_gemm = 0;
 int g_dwp_groups = 47;
 int g_dwp_stages = 4;
 int g_dwp_accs = 4;
-int g_dwp_epi1 = 54;
+int g_dwp_epi1 = 62;
 int g_pdl = 1;
 
 // ---- algorithm selection for dense contractions ---------------------------

@@ -142,7 +142,7 @@ def test_lowering_dispatch_sequence_with_oracle(oracle_built):
 def test_process_options(spx_built):
     """Path options are host-side state: defaults, round trip, range errors."""
     defaults = {"gemm_path": 0, "dw_path": 0, "pw_path": 0, "tc_wide_epilogue": 1,
-                "tc_conv_groups": 2, "tc_lo_tmem": 0, "pw_gemm": 0, "dwp_groups": 47, "dwp_stages": 4, "dwp_accs": 4, "dwp_epi1": 54, "tc_cat": 1, "tc_acc4": 1, "pdl": 1}
+                "tc_conv_groups": 2, "tc_lo_tmem": 0, "pw_gemm": 0, "dwp_groups": 47, "dwp_stages": 4, "dwp_accs": 4, "dwp_epi1": 62, "tc_cat": 1, "tc_acc4": 1, "pdl": 1}
     for name, v in defaults.items():
         assert _lib.get_option(name) == v, name
     assert _lib.get_option("no_such_option") == -1
