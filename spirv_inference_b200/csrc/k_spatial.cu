@@ -142,6 +142,9 @@ __global__ void gap_nhwc_kernel(const float* __restrict__ x, float* __restrict__
     float acc[VEC];
 #pragma unroll
     for (int v = 0; v < VEC; ++v) acc[v] = 0.0f;
+    // Unrolled so several independent loads are in flight per thread; the
+    // additions stay in pixel order.
+#pragma unroll 8
     for (int i = 0; i < hw; ++i) {
       if (VEC == 4) {
         float4 q = __ldg(reinterpret_cast<const float4*>(xp + (int64_t)i * c));
