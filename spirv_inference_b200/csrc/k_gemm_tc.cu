@@ -1063,6 +1063,9 @@ __global__ void __launch_bounds__(kSkThreads)
 #pragma unroll
         for (int q = 0; q < 8; ++q)
           base[q] = q < p.splits ? peer_addr(red + row, (uint32_t)q) : 0u;
+        // Unrolled: several rows' peer loads are in flight at once (each
+        // row still sums its partials in the fixed order below).
+#pragma unroll 4
         for (int m = split; m < p.M; m += p.splits) {
           float part[8];
 #pragma unroll
