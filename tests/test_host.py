@@ -202,3 +202,33 @@ def test_dw_project_eligibility_on_host(spx_built):
         assert l.spx_dw_project_supported(ctypes.byref(q)) == 0, field
     assert l.spx_op_dw_project_nhwc(None, *([None] * 8), ctypes.byref(ok)) == \
         _lib.SPX_ERR_INVALID_ARGUMENT
+
+
+# (map, channels, stride, outputs) of every fused block of MobileNetV2 and the
+# 3x3 ones of EfficientNet-Lite0
+_DWP_LAYERS = [(112, 32, 1, 16), (112, 96, 2, 24), (56, 144, 1, 24), (56, 144, 2, 32),
+               (28, 192, 1, 32), (28, 192, 2, 64), (14, 384, 1, 64), (14, 384, 1, 96),
+               (14, 576, 1, 96), (14, 576, 2, 160), (7, 960, 1, 160), (7, 960, 1, 320),
+               (28, 240, 2, 80), (14, 480, 1, 80)]
+
+
+def test_dw_project_shared_memory_fits_every_option(spx_built):
+    """Every tile class fits shared memory (at least two A/B stages and two
+    halo slots) for every value of the kernel's options, so no option setting
+    turns a supported layer into an unsupported one."""
+    l = _lib.lib()
+    names = ("dwp_groups", "dwp_stages", "dwp_accs", "dwp_epi1")
+    defaults = [_lib.get_option(k) for k in names]
+    try:
+        for setting in [(g, st, a, e) for g in (0, 63) for st in (2, 3, 4) for a in (2, 4)
+                        for e in (0, 63)]:
+            for k, v in zip(names, setting):
+                _lib.set_option(k, v)
+            for h, c, s, cout in _DWP_LAYERS:
+                oh = -(-h // s)
+                pt = max((oh - 1) * s + 3 - h, 0) // 2
+                q = _lib.DwProjParams(256, h, h, c, oh, oh, 3, s, pt, pt, 3, cout, 0)
+                assert l.spx_dw_project_supported(ctypes.byref(q)) == 1, (setting, h, c, s, cout)
+    finally:
+        for k, v in zip(names, defaults):
+            _lib.set_option(k, v)
