@@ -706,6 +706,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         // lane's proxy fence has to wait behind its own in-flight store.
         const bool trc = warp == 0 && lane == 0 && c0 == 0;
         if (trc) TC_TRACE(8, (t - blockIdx.x) / gridDim.x);
+        // The accumulator chunk comes out of TMEM first (it does not touch
+        // the staging tile), so its latency overlaps the wait for the
+        // previous store's read of the staging tile.
+        float v[32];
+        tmem_ld32(tbase + (uint32_t)c0, v);
+        if (p.cat) add_tmem32(tbase + (uint32_t)(p.BN + c0), v);
+        if (trc) TC_TRACE(9, (t - blockIdx.x) / gridDim.x);
         if (lane == issuer) bulk_wait_read0();
         const int next = (issuer + 1) & 31;
         if (lane == next) {
@@ -715,10 +722,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         __syncwarp();
-        if (trc) TC_TRACE(9, (t - blockIdx.x) / gridDim.x);
-        float v[32];
-        tmem_ld32(tbase + (uint32_t)c0, v);
-        if (p.cat) add_tmem32(tbase + (uint32_t)(p.BN + c0), v);
         if (trc) TC_TRACE(10, (t - blockIdx.x) / gridDim.x);
         if (p.res) {
           ok = bar_wait(&rfull[warp], rph, abort_flag) && ok;
